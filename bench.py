@@ -1,0 +1,675 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 batch-1 decode GEMV family (the driver's contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}] [--sweep]
+
+Workload (the one the headline metric is quoted on): the Llama-3.1-8B FP8 W8A16 decode-layer GEMV
+sequence at batch 1 -- qkv 6144x4096 -> o 4096x4096 -> gate_up 28672x4096 -> down 4096x14336, each GEMV reading the
+previous one's output as x (o reads qkv[:4096], down reads gate_up[:14336]). One step = one decode layer (4 launches).
+Weights ~ N(0, 0.02) quantised to e4m3 with a per-row fp32 scale, x ~ N(0, 1) bf16, synthetic (no checkpoints).
+The steps rotate over L distinct layers (L * 208 MiB > 4 x L2), so weights always stream from HBM.
+
+value   = algorithmic bytes (e4m3 weights + fp32 row scales) of all steps / device time of the K steps, GB/s,
+          max over ranks; at N > 1 every rank runs its own layers (weak scaling, no data-path collective).
+e2e     = the same metric through the public Python API (ctypes -> C ABI, eager launches), with each step's x copied
+          host->device from pinned memory and the layer output copied device->host inside the timed region.
+roofline: the dominant (and only) kernel of the step is the FP8 GEMV kernel; achieved = algorithmic bytes / time.
+cpu_baseline: the reference's CPU path (dequantise + chunked fp32 matmul, oracle/cpu_reference.py) on the host cores.
+--impl reference: that CPU path alone, as the reference arm (rank 0 only).
+--sweep: per-shape / per-format / per-model table as JSON lines, plus decode us/token.
+"""
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "paia-project_b200"))
+
+METRIC = "GEMV achieved HBM GB/s, Llama-3.1-8B FP8 W8A16 decode-layer sweep (qkv, o, gate_up, down), batch 1"
+FALLBACK_HBM_GBS = 6650.0
+REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+# ----------------------------------------------------------------------------------------------- helpers
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def kernel_traffic():
+    """dram bytes per launch of the FP8 GEMV kernel from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler(threading.Thread):
+    """NVML sampling of SM clock and clock-event reasons (what `nvidia-smi --query-gpu=clocks.sm,...` reports)."""
+
+    def __init__(self, dev_index, period=0.01):
+        super().__init__(daemon=True)
+        self.period, self.samples, self.ok = period, [], False
+        self._halt = threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml as N
+            import torch
+            N.nvmlInit()
+            u = str(torch.cuda.get_device_properties(dev_index).uuid)
+            u = u if u.startswith("GPU-") else f"GPU-{u}"
+            self.h = N.nvmlDeviceGetHandleByUUID(u)
+            self.N = N
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self._reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.ok = True
+        except Exception as e:  # NVML missing: report no clocks rather than invent them
+            self.err = repr(e)
+
+    def run(self):
+        while self.ok and not self._halt.is_set():
+            try:
+                self.samples.append((time.perf_counter(), self.N.nvmlDeviceGetClockInfo(self.h, self.N.NVML_CLOCK_SM),
+                                     int(self._reasons(self.h)),
+                                     self.N.nvmlDeviceGetPowerUsage(self.h) / 1000.0))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def stop(self):
+        self._halt.set()
+        if self.is_alive():
+            self.join(timeout=2)
+
+    def summary(self, t0, t1):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "NVML unavailable"}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        note = "sampled during the timed region"
+        if len(inside) < 3:      # a short timed region: use the samples of the sustained run around it
+            inside = [s for s in self.samples if t0 - 1.0 <= s[0] <= t1 + 0.2]
+            note = "timed region shorter than the sampling period; samples from the 1 s of load around it"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0, "note": "no samples"}
+        mask = 0
+        for s in inside:
+            mask |= s[2]
+        reasons = [n for b, n in REASON_BITS.items() if mask & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "power_w_max": max(s[3] for s in inside), "samples": len(inside), "note": note}
+
+
+# ----------------------------------------------------------------------------------------------- operands
+
+class Gemv:
+    """One GEMV of a layer: quantised weights on the device, its variant, and a ctypes launch with fixed pointers."""
+
+    def __init__(self, lib, kind, N, K, g, name, bias=False, variant=None, random_codes=False):
+        import torch
+        from paia_gemv import quant, synthetic
+        self.kind, self.N, self.K, self.name = kind, N, K, name
+        self.s = self.z = None
+        self.bias = synthetic.bias_bf16(N, g, device="cuda") if bias else None
+        if random_codes:      # timing-only copies: valid codes of the format, no data-dependent control flow
+            if kind == "bf16":
+                self.W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+            elif kind == "fp8":
+                b = torch.randint(0, 256, (N, K), device="cuda", dtype=torch.uint8, generator=g)
+                b[(b & 0x7F) == 0x7F] = 0x7E
+                self.W = b
+                self.s = torch.rand(N, device="cuda", generator=g) * 1e-4 + 1e-5
+            else:
+                self.W = torch.randint(0, 256, (N, K // 2), device="cuda", dtype=torch.uint8, generator=g)
+                dt = torch.float16 if kind == "int4" else torch.bfloat16
+                self.s = (torch.rand(N, K // 128, device="cuda", generator=g) * 1e-3 + 1e-4).to(dt)
+                if kind == "int4_asym":
+                    self.z = (torch.randn(N, K // 128, device="cuda", generator=g) * 1e-3).to(torch.bfloat16)
+        else:
+            W = synthetic.weights_f32(N, K, g, device="cuda")
+            if kind == "bf16":
+                self.W = W.to(torch.bfloat16)
+            elif kind == "fp8":
+                self.W, self.s = quant.quantize_fp8_rowwise(W)
+            elif kind == "int4":
+                self.W, self.s = quant.quantize_int4_g128(W)
+            else:
+                self.W, self.s, self.z = quant.quantize_int4_asym(W)
+            del W
+        self.variant = variant
+        self.lib = lib
+
+    def weight_bytes(self):
+        """Algorithmic bytes: weights + scales/zeros (the roofline numerator of the metric)."""
+        n = self.W.numel() * self.W.element_size()
+        for t in (self.s, self.z):
+            if t is not None:
+                n += t.numel() * t.element_size()
+        return n
+
+    def io_bytes(self):
+        return 2 * self.K + 2 * self.N + (2 * self.N if self.bias is not None else 0)
+
+    def launcher(self, x, y):
+        """A zero-argument function launching this GEMV on torch's current stream (raw ctypes call)."""
+        import ctypes
+        import torch
+        L = self.lib._lib
+        P = ctypes.c_void_p
+        W, s, z = P(self.W.data_ptr()), P(self.s.data_ptr() if self.s is not None else 0), \
+            P(self.z.data_ptr() if self.z is not None else 0)
+        xp, yp = P(x.data_ptr()), P(y.data_ptr())
+        b = P(self.bias.data_ptr()) if self.bias is not None else None
+        N, K, v = self.N, self.K, self.variant
+        dev = torch.cuda.current_device()
+        cur = torch._C._cuda_getCurrentRawStream
+        if self.kind == "bf16":
+            fn = L.paia_gemv_bf16_bias
+            return lambda: fn(W, xp, b, yp, N, K, v, P(cur(dev)))
+        if self.kind == "fp8":
+            fn = L.paia_gemv_fp8_bias
+            return lambda: fn(W, s, xp, b, yp, N, K, v, P(cur(dev)))
+        if self.kind == "int4":
+            fn = L.paia_gemv_int4_bias
+            return lambda: fn(W, s, xp, b, yp, N, K, v, P(cur(dev)))
+        fn = L.paia_gemv_int4_asym_bias
+        return lambda: fn(W, s, z, xp, b, yp, N, K, v, P(cur(dev)))
+
+    def api_call(self, x, y):
+        """The public op API a user calls (paia_gemv.loader.GemvLib methods)."""
+        W, xp, yp = self.W.data_ptr(), x.data_ptr(), y.data_ptr()
+        if self.kind == "bf16":
+            if self.bias is not None:
+                return self.lib.bf16_bias(W, xp, self.bias.data_ptr(), yp, self.N, self.K, self.variant)
+            return self.lib.bf16(W, xp, yp, self.N, self.K, self.variant)
+        if self.kind == "fp8":
+            if self.bias is not None:
+                return self.lib.fp8_bias(W, self.s.data_ptr(), xp, self.bias.data_ptr(), yp, self.N, self.K, self.variant)
+            return self.lib.fp8(W, self.s.data_ptr(), xp, yp, self.N, self.K, self.variant)
+        if self.kind == "int4":
+            if self.bias is not None:
+                return self.lib.int4_bias(W, self.s.data_ptr(), xp, self.bias.data_ptr(), yp, self.N, self.K,
+                                          self.variant)
+            return self.lib.int4(W, self.s.data_ptr(), xp, yp, self.N, self.K, self.variant)
+        if self.bias is not None:
+            return self.lib.int4_asym_bias(W, self.s.data_ptr(), self.z.data_ptr(), xp, self.bias.data_ptr(), yp,
+                                           self.N, self.K, self.variant)
+        return self.lib.int4_asym(W, self.s.data_ptr(), self.z.data_ptr(), xp, yp, self.N, self.K, self.variant)
+
+
+def variant_for(lib, kind, N, K, tuned):
+    """Tuned tuple for this shape from paia-project_b200/tuned/b200.json, else the reference adapters' default."""
+    defaults = {"bf16": (2, 4, 4, 0, 1), "fp8": (2, 2, 4, 0, 1), "int4": (4, 2, 4, 0, 1), "int4_asym": (4, 2, 4, 0, 1)}
+    key = {"bf16": "shapes", "fp8": "fp8_shapes", "int4": "int4_shapes", "int4_asym": "int4_asym_shapes"}[kind]
+    want = defaults[kind]
+    e = (tuned or {}).get(key, {}).get(f"{N}x{K}")
+    if e:
+        want = tuple(e["variant"][k] for k in "RUWSH")
+    table = {"bf16": lib.variants, "fp8": lib.variants_fp8, "int4": lib.variants_int4,
+             "int4_asym": lib.variants_int4_asym}[kind]
+    for v in table:
+        if (v["R"], v["U"], v["W"], v["S"], v["H"]) == want:
+            return v["id"], want
+    raise KeyError(want)
+
+
+def load_tuned():
+    p = ROOT / "paia-project_b200" / "tuned" / "b200.json"
+    return json.loads(p.read_text()) if p.exists() else None
+
+
+class Layer:
+    """The per-layer GEMV sequence of one decode step, chained: each GEMV reads the previous one's output."""
+
+    def __init__(self, lib, kind, model, g, tuned, random_codes=False):
+        import torch
+        from paia_gemv import synthetic
+        self.gemvs = []
+        for name in synthetic.LAYER_SEQUENCE:
+            N, K = synthetic.SHAPES[model][name]
+            vid, _ = variant_for(lib, kind, N, K, tuned)
+            bias = (model == "qwen25_7b" and name == "qkv_fused")
+            self.gemvs.append(Gemv(lib, kind, N, K, g, name, bias=bias, variant=vid, random_codes=random_codes))
+        self.x = synthetic.activation_bf16(self.gemvs[0].K, g, device="cuda")
+        self.ys = [torch.empty(gm.N, dtype=torch.bfloat16, device="cuda") for gm in self.gemvs]
+        self.xs = [self.x] + [self.ys[i][:self.gemvs[i + 1].K] for i in range(len(self.gemvs) - 1)]
+        self.calls = [gm.launcher(x, y) for gm, x, y in zip(self.gemvs, self.xs, self.ys)]
+
+    def step(self):
+        for c in self.calls:
+            rc = c()
+            if rc:
+                raise RuntimeError(f"launch failed with code {rc}")
+
+    def step_api(self):
+        for gm, x, y in zip(self.gemvs, self.xs, self.ys):
+            gm.api_call(x, y)
+
+    def weight_bytes(self):
+        return sum(gm.weight_bytes() for gm in self.gemvs)
+
+
+def capture(fn, warm=1):
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def check_layer(layer):
+    """Sanity check on the device against torch's own fp32 dequantise-then-matmul (not the oracle)."""
+    import torch
+    from paia_gemv import quant
+    layer.step()
+    torch.cuda.synchronize()
+    errs = []
+    for gm, x, y in zip(layer.gemvs, layer.xs, layer.ys):
+        if gm.kind == "bf16":
+            deq = gm.W.float()
+        elif gm.kind == "fp8":
+            deq = quant.dequant_fp8(gm.W, gm.s)
+        elif gm.kind == "int4":
+            deq = quant.dequant_int4(gm.W, gm.s)
+        else:
+            deq = quant.dequant_int4_asym(gm.W, gm.s, gm.z)
+        ref = deq @ x.float()
+        if gm.bias is not None:
+            ref = ref + gm.bias.float()
+        ref = ref.to(torch.bfloat16).float()
+        errs.append(((y.float() - ref).norm() / ref.norm()).item())
+        del deq
+    return max(errs)
+
+
+# ----------------------------------------------------------------------------------------------- CPU baseline
+
+def cpu_layer_operands(kind="fp8", model="llama31_8b", seed=0):
+    """Seeded CPU operands of one decode layer: (name, N, K, W, s, z, x) per GEMV."""
+    import torch
+    from paia_gemv import quant, synthetic
+    g = synthetic.generator(seed)
+    ops = []
+    for name in synthetic.LAYER_SEQUENCE:
+        N, K = synthetic.SHAPES[model][name]
+        W = synthetic.weights_f32(N, K, g)
+        x = synthetic.activation_bf16(K, g)
+        if kind == "fp8":
+            q, s = quant.quantize_fp8_rowwise(W)
+            ops.append((name, N, K, q, s, None, x))
+        elif kind == "bf16":
+            ops.append((name, N, K, W.to(torch.bfloat16), None, None, x))
+        elif kind == "int4":
+            p, s = quant.quantize_int4_g128(W)
+            ops.append((name, N, K, p, s, None, x))
+        else:
+            p, s, z = quant.quantize_int4_asym(W)
+            ops.append((name, N, K, p, s, z, x))
+        del W
+    return ops
+
+
+def cpu_run_layer(ops, frac, kind="fp8"):
+    """The reference's CPU path over the first frac of every GEMV's rows; returns (bytes, dequant s, matmul s)."""
+    import cpu_reference as C
+    nbytes, td, tm = 0, 0.0, 0.0
+    for (name, N, K, W, s, z, x) in ops:
+        rows = max(1, int(round(N * frac)))
+        Wr = W[:rows]
+        sr = None if s is None else s[:rows]
+        zr = None if z is None else z[:rows]
+        _, a, b = C.gemv(kind, x, Wr, sr, zr)
+        td += a
+        tm += b
+        nbytes += Wr.numel() * Wr.element_size() + sum(t.numel() * t.element_size() for t in (sr, zr) if t is not None)
+    return nbytes, td, tm
+
+
+def cpu_baseline(target_s=15.0, kind="fp8"):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_reference as C
+    threads = C.set_threads()
+    ops = cpu_layer_operands(kind)
+    t0 = time.perf_counter()
+    cpu_run_layer(ops, 1.0, kind)               # warm-up and calibration
+    t_layer = time.perf_counter() - t0
+    frac = 1.0 if t_layer * 3 <= target_s else max(0.02, target_s / 3 / t_layer)
+    reps = max(3, min(20, int(target_s / max(t_layer * frac, 1e-3))))
+    times, tds, tms, nb = [], [], [], 0
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        nb, td, tm = cpu_run_layer(ops, frac, kind)
+        times.append(time.perf_counter() - t0)
+        tds.append(td)
+        tms.append(tm)
+    med = statistics.median(times)
+    return {"value": nb / med / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": (f"{'all' if frac == 1.0 else f'{frac:.3f} of the'} rows of one Llama-3.1-8B {kind} decode layer "
+                       f"(qkv, o, gate_up, down; {nb / 2**20:.1f} MiB): dequantise + fp32 matmul in 8192-row chunks "
+                       f"(the reference harness's CPU reference path), median of {reps} reps after 1 warm-up; "
+                       f"dequant {statistics.median(tds) * 1e3:.1f} ms + matmul {statistics.median(tms) * 1e3:.1f} ms "
+                       f"per rep; CPU {C.cpu_model()}, torch threads {threads}, os.cpu_count {os.cpu_count()}"),
+            "ms_per_layer": med * 1e3 / frac}
+
+
+# ----------------------------------------------------------------------------------------------- arms
+
+def run_reference_arm(args, rank, world):
+    """--impl reference: the reference's CPU implementation on this host's cores; rank 0 only."""
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_reference as C
+    threads = C.set_threads()
+    ops = cpu_layer_operands("fp8")
+    t0 = time.perf_counter()
+    cpu_run_layer(ops, 1.0)
+    t_layer = time.perf_counter() - t0
+    budget = 150.0
+    frac = min(1.0, budget / max(1, args.steps + args.warmup) / t_layer)
+    frac = max(frac, 1e-3)
+    for _ in range(args.warmup):
+        cpu_run_layer(ops, frac)
+    nbytes = 0
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        nb, _, _ = cpu_run_layer(ops, frac)
+        nbytes += nb
+    dt = time.perf_counter() - t0
+    value = nbytes / dt / 1e9
+    sample = (f"each step: {frac:.4f} of the rows of every GEMV of one Llama-3.1-8B FP8 decode layer "
+              f"({nbytes / args.steps / 2**20:.2f} MiB), dequantise + fp32 matmul in 8192-row chunks (the reference "
+              f"harness's CPU reference path, restated in oracle/cpu_reference.py); CPU {C.cpu_model()}, "
+              f"{threads} torch threads")
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to e4m3, N(0,1) bf16 x)",
+            "config": {"workload": "llama31_8b fp8 w8a16 decode-layer GEMV sweep, batch 1", "device": "cpu"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_main(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from paia_gemv import load_lib, synthetic, timing
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    lib = load_lib()
+    tuned = load_tuned()
+    kind, model = "fp8", "llama31_8b"
+    g = torch.Generator(device="cuda").manual_seed(1000 * rank + 1)
+    l2 = timing.l2_bytes()
+    probe = Layer(lib, kind, model, g, tuned)
+    lbytes = probe.weight_bytes()
+    L = max(4, math.ceil(4 * l2 / lbytes))
+    layers = [probe] + [Layer(lib, kind, model, g, tuned) for _ in range(L - 1)]
+    check_err = check_layer(layers[0])
+    if not check_err <= 1e-3:
+        raise RuntimeError(f"device sanity check failed: rel L2 {check_err:.3e} against torch fp32")
+
+    def run_steps(n):
+        for i in range(n):
+            layers[i % L].step()
+
+    # graphs: one full rotation (L steps) and a tail, so exactly K (or W) steps run
+    g_round = capture(lambda: run_steps(L))
+    tails = {}
+
+    def replay(n):
+        for _ in range(n // L):
+            g_round.replay()
+        r = n % L
+        if r:
+            if r not in tails:
+                tails[r] = capture(lambda: run_steps(r))
+            tails[r].replay()
+
+    if args.steps % L:
+        tails[args.steps % L] = capture(lambda: run_steps(args.steps % L))
+    if args.warmup % L and args.warmup % L not in tails:
+        tails[args.warmup % L] = capture(lambda: run_steps(args.warmup % L))
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    replay(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_host0 = time.perf_counter()
+    e0.record()
+    replay(args.steps)
+    e1.record()
+    torch.cuda.synchronize()
+    t_host1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    sampler.stop()
+    clocks = sampler.summary(t_host0, t_host1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = t.item()
+    total_bytes = lbytes * args.steps * world
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+    launches = 4 * args.steps * world
+
+    # per-shape GEMV microseconds (graph mode, each shape alone, L2-rotated random-code copies)
+    per_shape = {}
+    for gi, name in enumerate(synthetic.LAYER_SEQUENCE):
+        N, K = synthetic.SHAPES[model][name]
+        ref = layers[0].gemvs[gi]
+        n = timing.plan_rotation(ref.weight_bytes(), l2)
+        copies = [ref] + [Gemv(lib, kind, N, K, g, name, variant=ref.variant, random_codes=True) for _ in range(n - 1)]
+        xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in copies]
+        ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in copies]
+        calls = [c.launcher(x, y) for c, x, y in zip(copies, xs, ys)]
+        us = timing.median(timing.time_graph(calls, samples=15))
+        wb = ref.weight_bytes()
+        per_shape[name] = {"N": N, "K": K, "us": round(us, 3), "GBps": round(wb / us / 1e3, 1),
+                           "variant": layers[0].gemvs[gi].variant}
+        del copies, xs, ys, calls
+    torch.cuda.empty_cache()
+
+    # e2e through the public API with host buffers (eager launches, async copies, one sync at the end)
+    x_host = torch.empty(layers[0].x.numel(), dtype=torch.bfloat16).pin_memory()
+    x_host.copy_(layers[0].x.cpu())
+    y_host = torch.empty(layers[0].ys[-1].numel(), dtype=torch.bfloat16).pin_memory()
+    for i in range(min(args.warmup, 2 * L)):
+        lay = layers[i % L]
+        lay.x.copy_(x_host, non_blocking=True)
+        lay.step_api()
+        y_host.copy_(lay.ys[-1], non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for i in range(args.steps):
+        lay = layers[i % L]
+        lay.x.copy_(x_host, non_blocking=True)
+        lay.step_api()
+        y_host.copy_(lay.ys[-1], non_blocking=True)
+    a1.record()
+    torch.cuda.synchronize()
+    e2e_ms = a0.elapsed_time(a1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+
+    peak, peak_src = measured_peaks()
+    achieved = lbytes * args.steps / (ms * 1e-3) / 1e9
+    traffic = kernel_traffic()
+    result = None
+    if rank == 0:
+        cb = None
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_baseline()
+            cb = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items() if k != "ms_per_layer"}
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp8 e4m3 weights x bf16 x, fp32 accumulate)",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to e4m3 + fp32 row scale, N(0,1) bf16 x)",
+            "config": {"workload": "llama31_8b fp8 w8a16 decode-layer GEMV sweep: qkv 6144x4096 -> o 4096x4096 -> "
+                                   "gate_up 28672x4096 -> down 4096x14336, batch 1, chained",
+                       "layers_rotated": L, "bytes_per_step": lbytes,
+                       "l2": f"inputs larger than L2: rotation over {L} layers = {L * lbytes / 2**20:.0f} MiB "
+                             f"> 4 x L2 ({l2 / 2**20:.0f} MiB)",
+                       "launch": "CUDA graph of back-to-back launches with programmatic dependent launch",
+                       "per_gpu_layers": "each rank streams its own layers" if world > 1 else None},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "traffic": (traffic or {}).get("fp8_layer_bytes_per_step"),
+                         "kernel": "pb2::gemv_kernel<FP8> (all 4 launches of the step)"},
+            "per_shape_us": per_shape,
+            "us_per_layer": round(ms_max * 1e3 / args.steps, 3),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": layers[0].x.numel() * 2,
+                    "d2h_bytes_per_step": layers[0].ys[-1].numel() * 2,
+                    "how": "public API (paia_gemv.loader ctypes -> C ABI), eager launches; per step pinned H2D of x, "
+                           "4 GEMVs, D2H of the layer output; CUDA events around all K steps"},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "check_rel_l2_vs_torch": round(check_err, 6),
+        }
+        if cb is not None:
+            result["cpu_baseline"] = cb
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def run_sweep(args):
+    """All BASELINE configs 1-4 per shape and format (graph mode, L2 rotation), one JSON line each, plus the decode
+    us/token of both models in every format (layers back to back with PDL, distinct weights per layer)."""
+    import torch
+    from paia_gemv import load_lib, synthetic, timing
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    tuned = load_tuned()
+    peak, src = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    l2 = timing.l2_bytes()
+    kinds = args.kinds.split(",")
+    for kind in kinds:
+        for model in ("llama31_8b", "qwen25_7b"):
+            for name in ("qkv_fused", "o_proj", "gate_up_fused", "down_proj", "lm_head", "q_proj", "k_proj",
+                         "gate_proj"):
+                N, K = synthetic.SHAPES[model][name]
+                vid, tup = variant_for(lib, kind, N, K, tuned)
+                bias = model == "qwen25_7b" and name == "qkv_fused"
+                first = Gemv(lib, kind, N, K, g, name, bias=bias, variant=vid)
+                n = timing.plan_rotation(first.weight_bytes(), l2)
+                copies = [first] + [Gemv(lib, kind, N, K, g, name, bias=bias, variant=vid, random_codes=True)
+                                    for _ in range(n - 1)]
+                xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in copies]
+                ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in copies]
+                calls = [c.launcher(x, y) for c, x, y in zip(copies, xs, ys)]
+                us = timing.median(timing.time_graph(calls, samples=15))
+                wb = first.weight_bytes()
+                print(json.dumps({"kind": kind, "model": model, "layer": name, "N": N, "K": K, "variant": tup,
+                                  "us": round(us, 3), "GBps": round(wb / us / 1e3, 1),
+                                  "frac_of_peak": round(wb / us / 1e3 / peak, 4), "peak": peak, "peak_source": src,
+                                  "copies": n}), flush=True)
+                del copies, xs, ys, calls, first
+                torch.cuda.empty_cache()
+        for model in ("llama31_8b", "qwen25_7b"):
+            nl = synthetic.N_LAYERS[model]
+            layers = [Layer(lib, kind, model, g, tuned, random_codes=True) for _ in range(nl)]
+            N, K = synthetic.SHAPES[model]["lm_head"]
+            vid, _ = variant_for(lib, kind, N, K, tuned)
+            head = Gemv(lib, kind, N, K, g, "lm_head", variant=vid, random_codes=True)
+            hy = torch.empty(N, device="cuda", dtype=torch.bfloat16)
+            hcall = head.launcher(layers[-1].ys[-1], hy)
+
+            def token():
+                for lay in layers:
+                    lay.step()
+                hcall()
+
+            gph = capture(token)
+            for _ in range(3):
+                gph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 10
+            e0.record()
+            for _ in range(reps):
+                gph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            tb = sum(l.weight_bytes() for l in layers) + head.weight_bytes()
+            print(json.dumps({"kind": kind, "model": model, "decode_us_per_token": round(us, 2),
+                              "layers": nl, "weight_GB": round(tb / 1e9, 3), "GBps": round(tb / us / 1e3, 1),
+                              "frac_of_peak": round(tb / us / 1e3 / peak, 4)}), flush=True)
+            del layers, head, gph
+            torch.cuda.empty_cache()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--kinds", default="bf16,fp8,int4,int4_asym")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+    if args.sweep:
+        return run_sweep(args)
+    return run_main(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

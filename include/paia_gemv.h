@@ -1,0 +1,104 @@
+/*
+ * paia_gemv.h: C ABI of libpaia_gemv.so, the B200 (sm_100a) batch-1 decode GEMV family.
+ *
+ * y[N] = dequant(W)[N,K] . x[K] (+ bias), bf16 activations and outputs, fp32 accumulation. Pointers are device
+ * pointers; `stream` is a cudaStream_t (NULL = legacy default stream). Every entry point launches asynchronously on
+ * `stream`, allocates nothing, never synchronises and is safe to capture in a CUDA graph.
+ * Return codes: 0 ok, -1 bad variant, -2 bad shape or alignment, >0 the cudaError_t of the launch.
+ *
+ * The entry points marked REF replace the reference's (Bejaine/PAIA-Project) symbols of the same name with identical
+ * signatures, argument checks and return codes, so its ctypes loader (src/paia_gemv/loader.py:28-99) and harness
+ * adapters (paia-bench/bench/ops/ours_bf16.py, ours_quant.py) load this library through $PAIA_GEMV_LIB unchanged.
+ *
+ * Formats (byte-identical to the reference's, src/paia_gemv/quant_host.h:1-13):
+ *   BF16        W bf16 [N][K] row-major (nn.Linear layout), K % 8 == 0, W/x/y 16-byte aligned.
+ *   FP8 W8A16   Wq e4m3fn bytes [N][K], scale fp32 [N] (row amax / 448), K % 16 == 0, Wq/x 16 B, scale 4 B, y 2 B.
+ *   INT4 W4A16  Wq uint8 [N][K/2] (byte j: weight 2j in the low nibble, 2j+1 in the high nibble, zero point 8),
+ *               scales fp16 [N][K/128], K % 128 == 0, Wq/x 16 B, scales/y 2 B.
+ *   INT4 asym   Wq as INT4 (a little-endian int32 [N][K/8] with nibble j at bits 4j holding k = 8i + j is the same
+ *               bytes), scales and zeros bf16 [N][K/128] each, w = (q - 8) * scale + zero
+ *               (paia-bench/bench/ops/lib_quant.py:159-167, :227-231).
+ * Additional limit of the B200 kernels: x is staged in shared memory, so K <= 98304 (else -2).
+ *
+ * Weights, scales, zeros and bias are read before the kernel waits on its predecessor when the variant launches with
+ * programmatic dependent launch (H = 1): they must not be written by the kernel immediately before on the same stream.
+ * x and y are only touched after that wait.
+ */
+#ifndef PAIA_GEMV_H
+#define PAIA_GEMV_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* REF src/paia_gemv/gemv_bf16.cu:37. Number of BF16 variants. */
+int paia_gemv_bf16_variant_count(void);
+/* REF src/paia_gemv/gemv_bf16.cu:40-44. (R, U, W, S, H) of variant v; -1 if out of range. */
+int paia_gemv_bf16_variant_info(int v, int* R, int* U, int* W, int* S, int* H);
+/* REF src/paia_gemv/gemv_bf16.cu:48-53. y[N] = W[N,K] x[K]. */
+int paia_gemv_bf16(const void* W, const void* x, void* y, int N, int K, int variant, void* stream);
+
+/* REF src/paia_gemv/gemv_quant.cu:61-62. */
+int paia_gemv_fp8_variant_count(void);
+int paia_gemv_fp8_variant_info(int v, int* R, int* U, int* W, int* H);
+/* REF src/paia_gemv/gemv_quant.cu:64-68. y = scale[n] * sum_k e4m3(Wq[n,k]) x[k]. */
+int paia_gemv_fp8(const void* Wq, const void* scale, const void* x, void* y, int N, int K, int variant, void* stream);
+
+/* REF src/paia_gemv/gemv_quant.cu:70-71. */
+int paia_gemv_int4_variant_count(void);
+int paia_gemv_int4_variant_info(int v, int* R, int* U, int* W, int* H);
+/* REF src/paia_gemv/gemv_quant.cu:73-77. Fused INT4 W4A16 g128 (symmetric, fp16 scale). */
+int paia_gemv_int4(const void* Wq, const void* scales, const void* x, void* y, int N, int K, int variant, void* stream);
+/* REF src/paia_gemv/gemv_quant.cu:80-85. Naive control kernel (same result, deliberately slow). */
+int paia_gemv_int4_naive(const void* Wq, const void* scales, const void* x, void* y, int N, int K, void* stream);
+/* REF src/paia_gemv/gemv_quant.cu:88-97. Unfused control: dequantise into scratch_bf16 (2*N*K bytes, 16-byte
+ * aligned, caller-owned), then the default BF16 GEMV variant. */
+int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, void* y, void* scratch_bf16, int N, int K,
+                           void* stream);
+
+/* ---- B200 additions (no reference kernel; the reference's survey of this path proposes them) ---- */
+
+/* Library identification string. */
+const char* paia_gemv_version(void);
+
+/* Asymmetric INT4 g128 (replaces the tinygemm call of paia-bench/bench/ops/lib_quant.py:221 for this format, with
+ * this repo's packing). It shares the INT4 variant tuples. */
+int paia_gemv_int4_asym_variant_count(void);
+int paia_gemv_int4_asym_variant_info(int v, int* R, int* U, int* W, int* H);
+int paia_gemv_int4_asym(const void* Wq, const void* scales, const void* zeros, const void* x, void* y, int N, int K,
+                        int variant, void* stream);
+
+/* Fused bias epilogue, y = W x + bias (bias bf16 [N], 2-byte aligned, may be NULL), added in fp32 before the single
+ * rounding to bf16. For the Qwen2.5 QKV projection, whose bias the reference harness ignores
+ * (paia-bench/configs/shapes.yaml:7). */
+int paia_gemv_bf16_bias(const void* W, const void* x, const void* bias, void* y, int N, int K, int variant,
+                        void* stream);
+int paia_gemv_fp8_bias(const void* Wq, const void* scale, const void* x, const void* bias, void* y, int N, int K,
+                       int variant, void* stream);
+int paia_gemv_int4_bias(const void* Wq, const void* scales, const void* x, const void* bias, void* y, int N, int K,
+                        int variant, void* stream);
+int paia_gemv_int4_asym_bias(const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                             void* y, int N, int K, int variant, void* stream);
+
+/* How the B200 build interprets variant v of `kind` (0 bf16, 1 fp8, 2 int4, 3 int4_asym): R rows per warp slot,
+ * U 16-byte steps per row in flight, W warps per CTA, S (bf16) mixed-precision FMA, H programmatic dependent launch,
+ * KS warps per row (0 = chosen at launch from K and N), vec_bytes per load, math = dequantisation path. Extends the
+ * tuple interface of src/paia_gemv/gemv_quant.cu:61-71. */
+typedef struct paia_gemv_variant_ex { int R, U, W, S, H, KS, pdl, vec_bytes, math; } paia_gemv_variant_ex;
+int paia_gemv_variant_info_ex(int kind, int v, paia_gemv_variant_ex* out);
+
+/* Tuning entry point (the B200 analogue of the variant sweep of src/tools/dev_sweep_bf16.py): launch any compiled
+ * kernel instance (R, U, W, math) of `kind` with explicit PDL (0/1), warps per row ks (0 = auto) and CTAs per SM
+ * (0 = auto). s/z/bias as in the per-format entry points (unused ones may be NULL). -1 if no such instance exists. */
+int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks, int ctas_per_sm, const void* Wq,
+                        const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
+                        void* stream);
+
+/* Device-side error word of the current device (0 = none), set by kernels whose bounded waits gave up; clear != 0
+ * resets it. Synchronous. */
+int paia_gemv_device_error(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PAIA_GEMV_H */

@@ -1,0 +1,305 @@
+// libpaia_gemv.so: the C ABI of the B200 decode GEMV family.
+//
+// The first group of symbols is the reference's ABI with identical names, signatures, argument checks and return
+// codes (Bejaine/PAIA-Project src/paia_gemv/gemv_bf16.cu:35-55 and gemv_quant.cu:58-99), so the reference's ctypes
+// loader (src/paia_gemv/loader.py) and its harness adapters load this library unchanged through $PAIA_GEMV_LIB.
+// Return codes: 0 ok, -1 bad variant, -2 bad shape or alignment, >0 cudaError_t of the launch.
+// The library allocates nothing, keeps no per-call state, never synchronises and launches on the caller's stream
+// (CUDA-graph capturable). Its only static state is a per-device cache of SM counts and occupancies.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <mutex>
+#include <unordered_map>
+#include "gemv_launch.cuh"
+#include "paia_gemv.h"
+
+namespace pb2 {
+int launch_int4_naive(const void* Wq, const void* sc, const void* x, void* y, int N, int K, cudaStream_t st);
+int launch_int4_dequant(const void* Wq, const void* sc, void* out, int N, int K, cudaStream_t st);
+const Variant* extra_int4(int* n);
+const Variant* extra_int4a(int* n);
+
+// ------------------------------------------------------------------ per-device caches
+namespace {
+constexpr int kMaxDev = 64;
+int g_sms[kMaxDev];
+size_t g_smem_optin[kMaxDev];
+std::mutex g_mu;
+struct OccKey {
+    const void* fn; int dev; int threads; size_t smem;
+    bool operator==(const OccKey& o) const { return fn == o.fn && dev == o.dev && threads == o.threads && smem == o.smem; }
+};
+struct OccHash {
+    size_t operator()(const OccKey& k) const {
+        return std::hash<const void*>()(k.fn) ^ (size_t)k.dev * 0x9E3779B97F4A7C15ull ^ (k.smem << 8) ^ (size_t)k.threads;
+    }
+};
+std::unordered_map<OccKey, int, OccHash> g_occ;
+
+int cur_dev() { int d = 0; cudaGetDevice(&d); return (d >= 0 && d < kMaxDev) ? d : 0; }
+}  // namespace
+
+int sm_count() {
+    const int d = cur_dev();
+    if (g_sms[d] == 0) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
+        g_sms[d] = v > 0 ? v : 1;
+    }
+    return g_sms[d];
+}
+
+size_t max_dyn_smem() {
+    const int d = cur_dev();
+    if (g_smem_optin[d] == 0) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, d);
+        g_smem_optin[d] = v > 0 ? (size_t)v : 48 * 1024;
+    }
+    return g_smem_optin[d];
+}
+
+int max_ctas_per_sm(KernelFn fn, int threads, size_t smem) {
+    const OccKey key{(const void*)fn, cur_dev(), threads, smem};
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dyn_smem());
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess) { (void)cudaGetLastError(); n = 0; }
+    g_occ.emplace(key, n);
+    return n;
+}
+
+const Variant* find_instance(int fmt, int R, int U, int W, int math) {
+    int n = 0;
+    const Variant* tabs[2] = {nullptr, nullptr};
+    int counts[2] = {0, 0};
+    switch (fmt) {
+        case kBF16: tabs[0] = table_bf16(&counts[0]); break;
+        case kFP8: tabs[0] = table_fp8(&counts[0]); break;
+        case kINT4: tabs[0] = table_int4(&counts[0]); tabs[1] = extra_int4(&counts[1]); break;
+        case kINT4A: tabs[0] = table_int4a(&counts[0]); tabs[1] = extra_int4a(&counts[1]); break;
+        default: return nullptr;
+    }
+    (void)n;
+    for (int t = 0; t < 2; ++t)
+        for (int i = 0; i < counts[t]; ++i) {
+            const Variant& v = tabs[t][i];
+            if (v.R == R && v.U == U && v.W == W && v.math == math) return &v;
+        }
+    return nullptr;
+}
+
+}  // namespace pb2
+
+using namespace pb2;
+
+namespace {
+inline bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(a - 1)) == 0; }
+
+const Variant* table_of(int fmt, int* n) {
+    switch (fmt) {
+        case kBF16: return table_bf16(n);
+        case kFP8: return table_fp8(n);
+        case kINT4: return table_int4(n);
+        case kINT4A: return table_int4a(n);
+        default: *n = 0; return nullptr;
+    }
+}
+
+// Shape and alignment contract of each format (the reference's checks, plus the bias and zero pointers).
+int check_args(int fmt, const void* W, const void* s, const void* z, const void* x, const void* bias, const void* y,
+               int N, int K) {
+    if (N <= 0 || K <= 0) return -2;
+    switch (fmt) {
+        case kBF16:   // gemv_bf16.cu:49-51: K % 8, W/x/y 16-byte aligned
+            if ((K & 7) || !aligned(W, 16) || !aligned(x, 16) || !aligned(y, 16)) return -2;
+            break;
+        case kFP8:    // gemv_quant.cu:66: K % 16, Wq/x 16 B, scale 4 B, y 2 B
+            if ((K & 15) || !aligned(W, 16) || !aligned(x, 16) || !aligned(s, 4) || !aligned(y, 2)) return -2;
+            break;
+        case kINT4:   // gemv_quant.cu:75: K % 128, Wq/x 16 B, scales 2 B, y 2 B
+            if ((K & 127) || !aligned(W, 16) || !aligned(x, 16) || !aligned(s, 2) || !aligned(y, 2)) return -2;
+            break;
+        case kINT4A:
+            if ((K & 127) || !aligned(W, 16) || !aligned(x, 16) || !aligned(s, 2) || !aligned(z, 2) || !aligned(y, 2))
+                return -2;
+            break;
+        default: return -2;
+    }
+    if (bias && !aligned(bias, 2)) return -2;
+    return 0;
+}
+
+int row_bytes(int fmt, int K) { return fmt == kBF16 ? K * 2 : fmt == kFP8 ? K : K / 2; }
+
+int run(int fmt, const void* W, const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
+        int variant, void* stream, const LaunchOpts* opts) {
+    int n = 0;
+    const Variant* tab = table_of(fmt, &n);
+    if (variant < 0 || variant >= n) return -1;
+    const int rc = check_args(fmt, W, s, z, x, bias, y, N, K);
+    if (rc) return rc;
+    Params p{};
+    p.W = static_cast<const uint8_t*>(W);
+    p.s = s;
+    p.z = z;
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.bias = static_cast<const __nv_bfloat16*>(bias);
+    p.y = static_cast<__nv_bfloat16*>(y);
+    p.N = N;
+    p.K = K;
+    p.nchunk = row_bytes(fmt, K) / 16;
+    p.groups = K / 128;
+    const LaunchOpts none{0, 0};
+    return launch_variant(tab[variant], p, opts ? *opts : none, static_cast<cudaStream_t>(stream));
+}
+
+int info4(int fmt, int v, int* R, int* U, int* W, int* H) {
+    int n = 0;
+    const Variant* t = table_of(fmt, &n);
+    if (v < 0 || v >= n) return -1;
+    *R = t[v].R; *U = t[v].U; *W = t[v].W; *H = t[v].H;
+    return 0;
+}
+
+int default_bf16_variant() {   // (R, U, W, S, H) = (2, 4, 4, 0, 1), looked up by tuple as gemv_quant.cu:47-56 does
+    int n = 0;
+    const Variant* t = table_bf16(&n);
+    for (int i = 0; i < n; ++i)
+        if (t[i].R == 2 && t[i].U == 4 && t[i].W == 4 && t[i].S == 0 && t[i].H == 1) return i;
+    return 0;
+}
+
+__device__ int g_device_error;   // written only by kernels whose bounded waits gave up (tensor-parallel path)
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------------ the reference's ABI
+
+int paia_gemv_bf16_variant_count(void) { int n = 0; table_bf16(&n); return n; }
+
+int paia_gemv_bf16_variant_info(int v, int* R, int* U, int* W, int* S, int* H) {
+    int n = 0;
+    const Variant* t = table_bf16(&n);
+    if (v < 0 || v >= n) return -1;
+    *R = t[v].R; *U = t[v].U; *W = t[v].W; *S = t[v].S; *H = t[v].H;
+    return 0;
+}
+
+int paia_gemv_bf16(const void* W, const void* x, void* y, int N, int K, int variant, void* stream) {
+    return run(kBF16, W, nullptr, nullptr, x, nullptr, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_fp8_variant_count(void) { int n = 0; table_fp8(&n); return n; }
+int paia_gemv_fp8_variant_info(int v, int* R, int* U, int* W, int* H) { return info4(kFP8, v, R, U, W, H); }
+
+int paia_gemv_fp8(const void* Wq, const void* scale, const void* x, void* y, int N, int K, int variant, void* stream) {
+    return run(kFP8, Wq, scale, nullptr, x, nullptr, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_int4_variant_count(void) { int n = 0; table_int4(&n); return n; }
+int paia_gemv_int4_variant_info(int v, int* R, int* U, int* W, int* H) { return info4(kINT4, v, R, U, W, H); }
+
+int paia_gemv_int4(const void* Wq, const void* scales, const void* x, void* y, int N, int K, int variant, void* stream) {
+    return run(kINT4, Wq, scales, nullptr, x, nullptr, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_int4_naive(const void* Wq, const void* scales, const void* x, void* y, int N, int K, void* stream) {
+    if (check_args(kINT4, Wq, scales, nullptr, x, nullptr, y, N, K)) return -2;
+    return launch_int4_naive(Wq, scales, x, y, N, K, static_cast<cudaStream_t>(stream));
+}
+
+int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, void* y, void* scratch_bf16, int N, int K,
+                           void* stream) {
+    // gemv_quant.cu:89: the reference checks Wq/x/scratch 16 B and scales 2 B; y is checked by the BF16 GEMV.
+    if (N <= 0 || K <= 0 || (K & 127) || !aligned(Wq, 16) || !aligned(x, 16) || !aligned(scales, 2) ||
+        !aligned(scratch_bf16, 16))
+        return -2;
+    const int rc = launch_int4_dequant(Wq, scales, scratch_bf16, N, K, static_cast<cudaStream_t>(stream));
+    if (rc) return rc;
+    return paia_gemv_bf16(scratch_bf16, x, y, N, K, default_bf16_variant(), stream);
+}
+
+// ------------------------------------------------------------------ B200 additions
+
+const char* paia_gemv_version(void) { return "paia-gemv-b200 1.0 (sm_100a)"; }
+
+int paia_gemv_int4_asym_variant_count(void) { int n = 0; table_int4a(&n); return n; }
+int paia_gemv_int4_asym_variant_info(int v, int* R, int* U, int* W, int* H) { return info4(kINT4A, v, R, U, W, H); }
+
+int paia_gemv_int4_asym(const void* Wq, const void* scales, const void* zeros, const void* x, void* y, int N, int K,
+                        int variant, void* stream) {
+    return run(kINT4A, Wq, scales, zeros, x, nullptr, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_bf16_bias(const void* W, const void* x, const void* bias, void* y, int N, int K, int variant,
+                        void* stream) {
+    return run(kBF16, W, nullptr, nullptr, x, bias, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_fp8_bias(const void* Wq, const void* scale, const void* x, const void* bias, void* y, int N, int K,
+                       int variant, void* stream) {
+    return run(kFP8, Wq, scale, nullptr, x, bias, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_int4_bias(const void* Wq, const void* scales, const void* x, const void* bias, void* y, int N, int K,
+                        int variant, void* stream) {
+    return run(kINT4, Wq, scales, nullptr, x, bias, y, N, K, variant, stream, nullptr);
+}
+
+int paia_gemv_int4_asym_bias(const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                             void* y, int N, int K, int variant, void* stream) {
+    return run(kINT4A, Wq, scales, zeros, x, bias, y, N, K, variant, stream, nullptr);
+}
+
+// Variant details as the B200 build interprets them. kind: 0 bf16, 1 fp8, 2 int4, 3 int4_asym.
+int paia_gemv_variant_info_ex(int kind, int v, paia_gemv_variant_ex* out) {
+    int n = 0;
+    const Variant* t = table_of(kind, &n);
+    if (!t || v < 0 || v >= n || !out) return -1;
+    *out = {t[v].R, t[v].U, t[v].W, t[v].S, t[v].H, 0, t[v].H, 16, t[v].math};
+    return 0;
+}
+
+// Tuning entry point: any compiled instance (R, U, W, math) of a format with explicit K-split (ks, 0 = auto),
+// CTAs per SM (0 = auto) and PDL (0/1). Pointers and bias as in the per-format entry points (s/z unused where the
+// format has none). Same return codes; -1 when no such instance is compiled.
+int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks, int ctas_per_sm, const void* Wq,
+                        const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
+                        void* stream) {
+    const Variant* inst = find_instance(kind, R, U, W, math);
+    if (!inst) return -1;
+    const int rc = check_args(kind, Wq, s, z, x, bias, y, N, K);
+    if (rc) return rc;
+    Variant v = *inst;
+    v.H = pdl ? 1 : 0;
+    Params p{};
+    p.W = static_cast<const uint8_t*>(Wq);
+    p.s = s;
+    p.z = z;
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.bias = static_cast<const __nv_bfloat16*>(bias);
+    p.y = static_cast<__nv_bfloat16*>(y);
+    p.N = N;
+    p.K = K;
+    p.nchunk = row_bytes(kind, K) / 16;
+    p.groups = K / 128;
+    const LaunchOpts o{ks, ctas_per_sm};
+    return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));
+}
+
+// Device-side error word of the current device (0 = none); clear != 0 resets it. Synchronous (a symbol copy).
+int paia_gemv_device_error(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
+    if (clear && v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    }
+    return v;
+}
+
+}  // extern "C"

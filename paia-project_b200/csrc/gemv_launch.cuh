@@ -1,0 +1,94 @@
+// Host-side launch machinery shared by the per-format translation units: variant tables, grid sizing, the K-split
+// choice and the (optionally programmatic) launch. No allocation, no synchronisation, graph-capturable.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "gemv_kernel.cuh"
+
+namespace pb2 {
+
+using KernelFn = void (*)(const Params);
+
+// One variant: the reference's (R, U, W, S, H) tuple and the kernel instance it maps to on B200.
+//   R  rows per warp row-slot            U  16-byte steps per row in flight (x2 with double buffering)
+//   W  warps per CTA                     S  BF16 only: 1 = mixed-precision bf16 FMA, 0 = fp32 conversion + FFMA
+//   H  1 = launch with programmatic dependent launch (PDL) and leave room on each SM for the next kernel
+struct Variant {
+    int R, U, W, S, H;
+    int math;                 // dequantisation/FMA path of the kernel instance (see gemv_kernel.cuh)
+    KernelFn fn;
+    size_t (*smem)(int K);    // dynamic shared memory bytes for a given K
+};
+
+// Launch-time knobs beyond the tuple (the _ex entry points); zero means "choose automatically".
+struct LaunchOpts {
+    int ks;                   // warps per row (power of two dividing W), 0 = auto
+    int ctas_per_sm;          // 0 = auto (resident CTAs, halved under PDL)
+};
+
+int sm_count();                                              // current device, cached
+int max_ctas_per_sm(KernelFn fn, int threads, size_t smem);  // occupancy, cached; 0 if it cannot launch
+size_t max_dyn_smem();                                       // opt-in shared memory per block, current device
+
+inline int ilog2(int v) { int l = 0; while ((1 << (l + 1)) <= v) ++l; return l; }
+
+// Warps per row: enough that every warp still has >= U steps of its row (K-split for long rows), and enough that the
+// CTA's row slots are not left idle when a CTA owns few rows, but never more warps than 512-byte steps in a row.
+inline int choose_ks(int nchunk, int rows_per_cta, int W, int R, int U) {
+    const int steps = (nchunk + 31) / 32;
+    int ks_k = 1;
+    while (ks_k * 2 <= W && steps >= ks_k * 2 * U) ks_k *= 2;
+    const int slots = (rows_per_cta + R - 1) / R;
+    int nr = 1;
+    while (nr * 2 <= W && nr * 2 <= slots) nr *= 2;
+    const int ks_r = W / nr;
+    int ks = ks_k > ks_r ? ks_k : ks_r;
+    int cap = 1;
+    while (cap * 2 <= W && cap * 2 <= steps) cap *= 2;
+    return ks < cap ? ks : cap;
+}
+
+inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaStream_t st) {
+    const size_t smem = v.smem(p.K);
+    if (smem > max_dyn_smem()) return -2;
+    const int threads = v.W * 32;
+    const int occ = max_ctas_per_sm(v.fn, threads, smem);
+    if (occ <= 0) return -2;
+    int per_sm = o.ctas_per_sm > 0 ? o.ctas_per_sm : (v.H ? (occ > 1 ? occ / 2 : 1) : occ);
+    if (per_sm > occ) per_sm = occ;
+    long long G = (long long)sm_count() * per_sm;
+    if (G > p.N) G = p.N;
+    const int rows_per_cta = (int)((p.N + G - 1) / G);
+    int ks = o.ks > 0 ? o.ks : choose_ks(p.nchunk, rows_per_cta, v.W, v.R, v.U);
+    if (ks > v.W || (v.W % ks) != 0 || (ks & (ks - 1)) != 0) return -2;
+    p.ks_log2 = ilog2(ks);
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)G);
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (v.H) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, v.fn, p);
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    return 0;
+}
+
+template <int F, int NW, int R>
+size_t smem_of(int K) { return smem_bytes<F, NW, R>(K); }
+
+// Table accessors, one translation unit per format (compiled in parallel).
+const Variant* table_bf16(int* n);
+const Variant* table_fp8(int* n);
+const Variant* table_int4(int* n);
+const Variant* table_int4a(int* n);
+// Extra kernel instances reachable only through paia_gemv_launch_ex (tuning): same tuple space, other math paths.
+const Variant* find_instance(int fmt, int R, int U, int W, int math);
+
+}  // namespace pb2

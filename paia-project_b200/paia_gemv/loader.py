@@ -1,0 +1,185 @@
+"""ctypes loader for libpaia_gemv.so, the B200 (sm_100a) build of the batch-1 decode GEMV family.
+
+Mirrors Bejaine/PAIA-Project src/paia_gemv/loader.py:1-109: the same library search order ($PAIA_GEMV_LIB, then
+build/<arch>/, then build/ under the package root), the same `GemvLib` methods with the same arguments (raw device
+pointers as ints, launch on torch's current raw CUDA stream so the ops are CUDA-graph capturable), the same variant
+tables (`variants`, `variants_fp8`, `variants_int4`: lists of {"id", "R", "U", "W", "S", "H"}) and the same error
+behaviour (a nonzero return code raises RuntimeError; -1 bad variant, -2 bad shape or alignment, >0 cudaError_t).
+
+Added for the B200 build: `int4_asym` (asymmetric INT4 g128, bf16 scale and zero), an optional fused bias on every
+format (`*_bias`), `variant_info_ex` (the B200 launch configuration a variant maps to), `device_error()`, and the
+tensor-parallel helpers used by paia_gemv.tp. There is no CPU fallback: without the library every op raises.
+"""
+import ctypes
+import os
+import platform
+from pathlib import Path
+
+_PKG_ROOT = Path(__file__).resolve().parent.parent    # paia-project_b200/, the analogue of the reference's src/
+
+
+def find_lib():
+    env = os.environ.get("PAIA_GEMV_LIB")
+    cands = [env] if env else []
+    cands += [str(_PKG_ROOT / "build" / platform.machine() / "libpaia_gemv.so"),
+              str(_PKG_ROOT / "build" / "libpaia_gemv.so")]
+    for c in cands:
+        if c and os.path.exists(c):
+            return c
+    raise FileNotFoundError("libpaia_gemv.so not found (run `python paia-project_b200/build.py`, or set "
+                            "PAIA_GEMV_LIB). Tried: " + ", ".join(c for c in cands if c))
+
+
+def current_raw_stream():
+    import torch
+    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device())
+
+
+_KINDS = {"bf16": 0, "fp8": 1, "int4": 2, "int4_asym": 3}
+_EX_FIELDS = ("R", "U", "W", "S", "H", "KS", "pdl", "vec_bytes", "math")
+
+
+class VariantEx(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_int) for f in _EX_FIELDS]
+
+
+class GemvLib:
+    def __init__(self, path=None):
+        self.path = path or find_lib()
+        lib = ctypes.CDLL(self.path)
+        P, I = ctypes.c_void_p, ctypes.c_int
+        # --- the reference's C ABI (gemv_bf16.cu:37-53, gemv_quant.cu:59-97), same argtypes as its loader.py:32-46
+        lib.paia_gemv_bf16.restype = I
+        lib.paia_gemv_bf16.argtypes = [P, P, P, I, I, I, P]
+        lib.paia_gemv_bf16_variant_count.restype = I
+        lib.paia_gemv_bf16_variant_info.restype = I
+        lib.paia_gemv_bf16_variant_info.argtypes = [I] + [ctypes.POINTER(I)] * 5
+        lib.paia_gemv_fp8.restype = I
+        lib.paia_gemv_fp8.argtypes = [P, P, P, P, I, I, I, P]
+        lib.paia_gemv_int4.restype = I
+        lib.paia_gemv_int4.argtypes = [P, P, P, P, I, I, I, P]
+        lib.paia_gemv_int4_naive.restype = I
+        lib.paia_gemv_int4_naive.argtypes = [P, P, P, P, I, I, P]
+        lib.paia_gemv_int4_unfused.restype = I
+        lib.paia_gemv_int4_unfused.argtypes = [P, P, P, P, P, I, I, P]
+        # --- B200 additions
+        lib.paia_gemv_int4_asym.restype = I
+        lib.paia_gemv_int4_asym.argtypes = [P, P, P, P, P, I, I, I, P]
+        lib.paia_gemv_bf16_bias.restype = I
+        lib.paia_gemv_bf16_bias.argtypes = [P, P, P, P, I, I, I, P]
+        lib.paia_gemv_fp8_bias.restype = I
+        lib.paia_gemv_fp8_bias.argtypes = [P, P, P, P, P, I, I, I, P]
+        lib.paia_gemv_int4_bias.restype = I
+        lib.paia_gemv_int4_bias.argtypes = [P, P, P, P, P, I, I, I, P]
+        lib.paia_gemv_int4_asym_bias.restype = I
+        lib.paia_gemv_int4_asym_bias.argtypes = [P, P, P, P, P, P, I, I, I, P]
+        lib.paia_gemv_int4_asym_variant_count.restype = I
+        lib.paia_gemv_variant_info_ex.restype = I
+        lib.paia_gemv_variant_info_ex.argtypes = [I, I, ctypes.POINTER(VariantEx)]
+        lib.paia_gemv_device_error.restype = I
+        lib.paia_gemv_device_error.argtypes = [I]
+        lib.paia_gemv_version.restype = ctypes.c_char_p
+        self.variants_fp8 = self._qvariants(lib, "fp8")
+        self.variants_int4 = self._qvariants(lib, "int4")
+        self._lib = lib
+        self._fn = lib.paia_gemv_bf16
+        self.n_variants = lib.paia_gemv_bf16_variant_count()
+        self.variants = []
+        for v in range(self.n_variants):
+            R, U, W, S, H = (ctypes.c_int() for _ in range(5))
+            assert lib.paia_gemv_bf16_variant_info(v, *map(ctypes.byref, (R, U, W, S, H))) == 0
+            self.variants.append({"id": v, "R": R.value, "U": U.value, "W": W.value, "S": S.value, "H": H.value})
+        # asymmetric INT4 shares the INT4 variant table (same tuples, same ids)
+        self.variants_int4_asym = self.variants_int4
+        self.version = lib.paia_gemv_version().decode()
+
+    @staticmethod
+    def _qvariants(lib, kind):
+        count = getattr(lib, f"paia_gemv_{kind}_variant_count")
+        count.restype = ctypes.c_int
+        info = getattr(lib, f"paia_gemv_{kind}_variant_info")
+        info.restype = ctypes.c_int
+        info.argtypes = [ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4
+        out = []
+        for v in range(count()):
+            R, U, W, H = (ctypes.c_int() for _ in range(4))
+            assert info(v, *map(ctypes.byref, (R, U, W, H))) == 0
+            out.append({"id": v, "R": R.value, "U": U.value, "W": W.value, "S": 0, "H": H.value})
+        return out
+
+    @staticmethod
+    def _check(rc, what):
+        if rc != 0:
+            raise RuntimeError(f"{what} failed with code {rc} (-1 bad variant, -2 bad shape/alignment, >0 cudaError_t)")
+
+    @staticmethod
+    def _st(stream):
+        return current_raw_stream() if stream is None else stream
+
+    # ------------------------------------------------------------------ the reference's op API
+    def fp8(self, Wq_ptr, scale_ptr, x_ptr, y_ptr, N, K, variant, stream=None):
+        """Wq [N,K] e4m3 bytes, scale [N] fp32, x [K] bf16, y [N] bf16; K % 16 == 0."""
+        self._check(self._lib.paia_gemv_fp8(Wq_ptr, scale_ptr, x_ptr, y_ptr, N, K, variant, self._st(stream)),
+                    "paia_gemv_fp8")
+
+    def int4(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, variant, stream=None):
+        """Wq [N,K/2] packed, scales [N,K/128] fp16; K % 128 == 0. Fused kernel."""
+        self._check(self._lib.paia_gemv_int4(Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, variant, self._st(stream)),
+                    "paia_gemv_int4")
+
+    def int4_naive(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, stream=None):
+        self._check(self._lib.paia_gemv_int4_naive(Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, self._st(stream)),
+                    "paia_gemv_int4_naive")
+
+    def int4_unfused(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, scratch_ptr, N, K, stream=None):
+        self._check(self._lib.paia_gemv_int4_unfused(Wq_ptr, scales_ptr, x_ptr, y_ptr, scratch_ptr, N, K,
+                                                     self._st(stream)), "paia_gemv_int4_unfused")
+
+    def bf16(self, W_ptr, x_ptr, y_ptr, N, K, variant, stream=None):
+        """y[N] = W[N,K] @ x[K]; pointers are ints. Raises on a nonzero return code."""
+        rc = self._fn(W_ptr, x_ptr, y_ptr, N, K, variant, self._st(stream))
+        if rc != 0:
+            raise RuntimeError(f"paia_gemv_bf16 failed with code {rc} (N={N}, K={K}, variant={variant}); "
+                               "-1 bad variant, -2 bad shape/alignment (K%8, 16B pointers), >0 cudaError_t")
+
+    # ------------------------------------------------------------------ B200 additions
+    def int4_asym(self, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, y_ptr, N, K, variant, stream=None):
+        """Asymmetric INT4 g128: Wq [N,K/2] packed, scales and zeros [N,K/128] bf16; w = (q - 8) * s + z."""
+        self._check(self._lib.paia_gemv_int4_asym(Wq_ptr, scales_ptr, zeros_ptr, x_ptr, y_ptr, N, K, variant,
+                                                  self._st(stream)), "paia_gemv_int4_asym")
+
+    def bf16_bias(self, W_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant, stream=None):
+        self._check(self._lib.paia_gemv_bf16_bias(W_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant, self._st(stream)),
+                    "paia_gemv_bf16_bias")
+
+    def fp8_bias(self, Wq_ptr, scale_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant, stream=None):
+        self._check(self._lib.paia_gemv_fp8_bias(Wq_ptr, scale_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant,
+                                                 self._st(stream)), "paia_gemv_fp8_bias")
+
+    def int4_bias(self, Wq_ptr, scales_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant, stream=None):
+        self._check(self._lib.paia_gemv_int4_bias(Wq_ptr, scales_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant,
+                                                  self._st(stream)), "paia_gemv_int4_bias")
+
+    def int4_asym_bias(self, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K, variant, stream=None):
+        self._check(self._lib.paia_gemv_int4_asym_bias(Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K,
+                                                       variant, self._st(stream)), "paia_gemv_int4_asym_bias")
+
+    def variant_info_ex(self, kind, v):
+        """The B200 launch configuration behind variant v of `kind` ("bf16", "fp8", "int4", "int4_asym")."""
+        out = VariantEx()
+        self._check(self._lib.paia_gemv_variant_info_ex(_KINDS[kind], v, ctypes.byref(out)), "paia_gemv_variant_info_ex")
+        return {f: getattr(out, f) for f in _EX_FIELDS}
+
+    def device_error(self, clear=True):
+        """The device-side error word (0 = none) written by kernels whose bounded waits gave up."""
+        return self._lib.paia_gemv_device_error(1 if clear else 0)
+
+
+_lib = None
+
+
+def load_lib():
+    global _lib
+    if _lib is None:
+        _lib = GemvLib()
+    return _lib
