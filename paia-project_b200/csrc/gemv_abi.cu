@@ -73,6 +73,12 @@ int max_ctas_per_sm(KernelFn fn, int threads, size_t smem) {
 
 const Variant* find_instance(int fmt, int R, int U, int W, int math) {
     int n = 0;
+    if (math == 2) {
+        const Variant* t = mma_instances(fmt, &n);
+        for (int i = 0; i < n; ++i)
+            if (t[i].U == U && t[i].W == W) return &t[i];
+        return nullptr;
+    }
     const Variant* tabs[2] = {nullptr, nullptr};
     int counts[2] = {0, 0};
     switch (fmt) {

@@ -54,7 +54,9 @@ inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaS
     const int threads = v.W * 32;
     const int occ = max_ctas_per_sm(v.fn, threads, smem);
     if (occ <= 0) return -2;
-    int per_sm = o.ctas_per_sm > 0 ? o.ctas_per_sm : (v.H ? (occ > 1 ? occ / 2 : 1) : occ);
+    // Full occupancy by default: under PDL the next kernel's CTAs take the SM slots that this grid's CTAs free at
+    // its tail (measured better than leaving half of each SM to the next kernel from the start).
+    int per_sm = o.ctas_per_sm > 0 ? o.ctas_per_sm : occ;
     if (per_sm > occ) per_sm = occ;
     long long G = (long long)sm_count() * per_sm;
     if (G > p.N) G = p.N;
@@ -90,5 +92,6 @@ const Variant* table_int4(int* n);
 const Variant* table_int4a(int* n);
 // Extra kernel instances reachable only through paia_gemv_launch_ex (tuning): same tuple space, other math paths.
 const Variant* find_instance(int fmt, int R, int U, int W, int math);
+const Variant* mma_instances(int fmt, int* n);
 
 }  // namespace pb2

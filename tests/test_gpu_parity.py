@@ -92,7 +92,8 @@ def test_big_shapes_sampled_rows_and_exact_properties(L, kind):
         if kind == "bf16":
             perm = torch.randperm(N, device="cuda", generator=g)
             yp = torch.empty_like(ops.y)
-            L.bf16(ops.W[perm].contiguous().data_ptr(), ops.x.data_ptr(), yp.data_ptr(), N, K, v)
+            Wp = ops.W[perm].contiguous()
+            L.bf16(Wp.data_ptr(), ops.x.data_ptr(), yp.data_ptr(), N, K, v)
             torch.cuda.synchronize()
             assert torch.equal(yp, ops.y[perm]), "row permutation property"
         del ops
@@ -160,7 +161,9 @@ def test_fp8_every_code_exact(L):
         y.fill_(float("nan"))
         L.fp8(qd.data_ptr(), sd.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, v["id"])
         torch.cuda.synchronize()
-        assert np.array_equal(bits(y), O.f32_to_bf16(O.e4m3_decode(codes))), v
+        # compared as values: code 0x80 (-0.0) sums to +0.0, which is the same number
+        want = O.bf16_to_f32(O.f32_to_bf16(O.e4m3_decode(codes)))
+        assert np.array_equal(O.bf16_to_f32(bits(y)), want), v
 
 
 @pytest.mark.parametrize("kind", ["int4", "int4_asym"])
@@ -249,7 +252,8 @@ def test_launch_ex_explicit_configs(L, kind):
     maths = (0, 1) if kind != "fp8" else (0,)
     for R, U, Wn, math, pdl, ks, cps in [(1, 1, 4, m, 0, 1, 1) for m in maths] + \
                                          [(2, 2, 8, m, 1, 8, 2) for m in maths] + \
-                                         [(4, 1, 8, m, 1, 2, 3) for m in maths] + [(2, 1, 8, maths[-1], 1, 4, 1)]:
+                                         [(4, 1, 8, m, 1, 2, 3) for m in maths] + [(2, 1, 8, maths[-1], 1, 4, 1)] + \
+                                         [(1, 2, 8, 2, 1, 0, 0), (1, 4, 16, 2, 0, 0, 2)]:
         ops.nan_fill()
         rc = ops.call_ex(L, R, U, Wn, math, pdl, ks, cps, with_bias=True)
         assert rc == 0, (R, U, Wn, math, pdl, ks, cps, rc)
@@ -303,3 +307,41 @@ def test_dependent_chain_in_cuda_graph(L, kind):
         for y, e in zip(ys, eager):
             assert np.array_equal(bits(y), e), f"{kind}: graph/PDL chain differs from the eager chain"
     del g
+
+
+MMA_CFGS = [(1, 4), (2, 8), (4, 8), (2, 16), (4, 16)]      # (U, W) of the tensor-core kernel (math 2)
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_mma_kernel_awkward_and_real_shapes(L, kind):
+    """The tensor-core kernel (gemv_mma.cuh) through paia_gemv_launch_ex: awkward shapes (partial 64-byte steps,
+    partial 16-row tiles, fewer rows than CTAs), real decode shapes, with and without bias, PDL on and off."""
+    shapes = AWKWARD[kind] + [(4096, 4096), (6144, 4096), (3584, 18944), (512, 3584)]
+    for (N, K) in shapes:
+        ops = make(kind, N, K, seed=N * 3 + K, with_bias=True)
+        ref, refb = ops.oracle()[0], ops.oracle(with_bias=True)[0]
+        for i, (U, Wn) in enumerate(MMA_CFGS):
+            for cps in (0, 1):
+                ops.nan_fill()
+                rc = ops.call_ex(L, 1, U, Wn, 2, (i + cps) % 2, 0, cps, with_bias=bool(cps))
+                assert rc == 0, (kind, N, K, U, Wn, cps, rc)
+                torch.cuda.synchronize()
+                check(ops, bits(ops.y), refb if cps else ref, f"mma {kind} {N}x{K} U{U} W{Wn} cps{cps}")
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1e-6, 1.0, 3e3, 1e30])
+def test_fp8_mma_activation_ranges(L, scale):
+    """The FP8 tensor-core path stages x as f16 scaled by a per-launch power of two: tiny, huge and outlier-dominated
+    activations must still match the oracle."""
+    N, K = 300, 4096
+    ops = make("fp8", N, K, seed=5)
+    xf = ops.x.float() * scale
+    if scale == 1e30:
+        xf[17] = 3e38                                      # one outlier near the top of the bf16 range
+    ops.x = xf.to(torch.bfloat16)
+    ref = ops.oracle()[0]
+    for U, Wn in MMA_CFGS:
+        ops.nan_fill()
+        assert ops.call_ex(L, 1, U, Wn, 2, 1, 0, 0) == 0
+        torch.cuda.synchronize()
+        check(ops, bits(ops.y), ref, f"fp8 mma x*{scale}")

@@ -145,7 +145,7 @@ def test_mapping_exactly_once(fmt):
     Us = (1, 2, 4, 8) if fmt == "bf16" else (1, 2, 4)
     rnd = random.Random(0)
     combos = list(itertools.product(SHAPES[fmt], (4, 8), Rs, Us, (1, 2, 3)))
-    for (N, K), W, R, U, per_sm in rnd.sample(combos, 120):
+    for (N, K), W, R, U, per_sm in rnd.sample(combos, 60):
         replay(fmt, N, K, W, R, U, sms=rnd.choice((148, 7, 1)), per_sm=per_sm)
 
 
@@ -163,3 +163,65 @@ def test_choose_ks_real_shapes():
     # few rows per CTA push the K-split up, but never past the number of steps
     assert choose_ks(128, 2, 8, 1, 1) == 4
     assert choose_ks(1, 1, 8, 1, 1) == 1
+
+
+# ------------------------------------------------------------------ tensor-core kernel (gemv_mma.cuh)
+
+MMA_STEP_K = {"bf16": 32, "fp8": 64, "int4": 128, "int4_asym": 128}
+
+
+def replay_mma(fmt, N, K, W, U, sms=148, per_sm=2):
+    """Replay of gemv_mma_kernel: CTA rows, 16-row tiles, 64-byte steps split over warps, lane (g, c) loading the
+    16-byte chunk q = 4 s + c of rows g and g + 8, x reads at s * SK + c * SK/4 .. + SK/4 (padded to Kp)."""
+    SK = MMA_STEP_K[fmt]
+    nchunk = ROWBYTES[fmt](K) // 16
+    Kp = (K + SK - 1) // SK * SK
+    G = grid(N, sms, per_sm)
+    S = (nchunk + 3) // 4
+    assert S * SK == Kp, (fmt, K, S, Kp)
+    loads = np.zeros((N, nchunk), dtype=np.int32)
+    stores = np.zeros(N, dtype=np.int32)
+    for blk in range(G):
+        rb, re = blk * N // G, (blk + 1) * N // G
+        ntiles = (re - rb + 15) >> 4
+        arrivals = {}
+        for warp in range(W):
+            sb, se = S * warp // W, S * (warp + 1) // W
+            nbatch = (se - sb + U - 1) // U if (se - sb) > U else 1
+            nit = ntiles * nbatch
+            seq, lds = iteration_order(nit, nbatch)
+            assert [(t, b) for t, b, _ in seq] == [(i // nbatch, i % nbatch) for i in range(nit)]
+            for t, b, _ in seq:
+                for u in range(U):
+                    s = sb + b * U + u
+                    if s >= se:
+                        continue
+                    assert s * SK + SK <= Kp                      # x reads (all lanes c) inside the padded x
+                    if fmt.startswith("int4"):
+                        assert s < Kp // 128                      # gsum index
+                    for g in range(8):
+                        for r in (rb + t * 16 + g, rb + t * 16 + g + 8):
+                            if r >= re:
+                                continue
+                            for c in range(4):
+                                q = 4 * s + c
+                                if q < nchunk:
+                                    loads[r, q] += 1
+                if b == nbatch - 1:
+                    arrivals[t] = arrivals.get(t, 0) + 1
+                    if warp == 0:
+                        for lane in range(16):
+                            r = rb + t * 16 + lane
+                            if r < re:
+                                stores[r] += 1
+        assert all(v == W for v in arrivals.values()) and len(arrivals) == ntiles
+    assert np.all(loads == 1), f"{fmt} N={N} K={K} W={W} U={U}: loads min {loads.min()} max {loads.max()}"
+    assert np.all(stores == 1), f"{fmt} N={N} K={K} W={W} U={U}: stores"
+
+
+@pytest.mark.parametrize("fmt", list(SHAPES))
+def test_mma_mapping_exactly_once(fmt):
+    rnd = random.Random(1)
+    combos = list(itertools.product(SHAPES[fmt], (4, 8, 16), (1, 2, 4), (1, 2, 3, 4)))
+    for (N, K), W, U, per_sm in rnd.sample(combos, 60):
+        replay_mma(fmt, N, K, W, U, sms=rnd.choice((148, 7, 1)), per_sm=per_sm)
