@@ -24,6 +24,7 @@ namespace {
 constexpr int kMaxDev = 64;
 int g_sms[kMaxDev];
 size_t g_smem_optin[kMaxDev];
+size_t g_smem_sm[kMaxDev];
 std::mutex g_mu;
 struct OccKey {
     const void* fn; int dev; int threads; size_t smem;
@@ -59,6 +60,17 @@ size_t max_dyn_smem() {
     return g_smem_optin[d];
 }
 
+size_t sm_smem_bytes() {
+    const int d = cur_dev();
+    if (g_smem_sm[d] == 0) {
+        int v = 0, r = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, d);
+        cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, d);
+        g_smem_sm[d] = v > r ? (size_t)(v - r) : max_dyn_smem();
+    }
+    return g_smem_sm[d];
+}
+
 int max_ctas_per_sm(KernelFn fn, int threads, size_t smem) {
     const OccKey key{(const void*)fn, cur_dev(), threads, smem};
     std::lock_guard<std::mutex> lk(g_mu);
@@ -73,8 +85,14 @@ int max_ctas_per_sm(KernelFn fn, int threads, size_t smem) {
 
 const Variant* find_instance(int fmt, int R, int U, int W, int math) {
     int n = 0;
-    if (math == 2) {
-        const Variant* t = mma_instances(fmt, &n);
+    if (math >= 5) {                        // TMA-fed: R is the ring depth, a launch option
+        const Variant* t = tma_instances(fmt, math, &n);
+        for (int i = 0; i < n; ++i)
+            if (t[i].U == U && t[i].W == W) return &t[i];
+        return nullptr;
+    }
+    if (math >= 2) {
+        const Variant* t = mma_instances(fmt, math, &n);
         for (int i = 0; i < n; ++i)
             if (t[i].U == U && t[i].W == W) return &t[i];
         return nullptr;
@@ -293,7 +311,12 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
     p.K = K;
     p.nchunk = row_bytes(kind, K) / 16;
     p.groups = K / 128;
-    const LaunchOpts o{ks, ctas_per_sm};
+    LaunchOpts o{ks, ctas_per_sm};
+    if (math >= 5) {                        // TMA-fed kernels: R = ring stages (<= 1: auto), ks = shared-memory share
+        o.ring = R <= 1 ? 0 : R;
+        o.share = ks;
+        o.ks = 0;
+    }
     return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));
 }
 
@@ -305,7 +328,8 @@ int paia_gemv_device_error(int clear) {
         const int zero = 0;
         cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
     }
-    return v;
+    if (v) return v;
+    return tma_device_error(clear);        // bounded mbarrier waits of the TMA-fed kernels
 }
 
 }  // extern "C"

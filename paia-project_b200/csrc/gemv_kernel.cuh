@@ -55,6 +55,8 @@ struct Params {
     int nchunk;                    // 16-byte chunks per row
     int ks_log2;                   // log2(KS): warps that share a row
     int groups;                    // K / 128 (INT4 formats)
+    int kc, nch, rs, st_bytes;     // TMA kernels: bytes per row per stage, stages per tile, smem row stride, stage size
+    int ring;                      // TMA kernels: stages in the shared-memory ring
 };
 
 template <int F> struct Elems;     // weights per 16-byte chunk

@@ -15,19 +15,27 @@ using KernelFn = void (*)(const Params);
 //   H  1 = launch with programmatic dependent launch (PDL) and leave room on each SM for the next kernel
 struct Variant {
     int R, U, W, S, H;
-    int math;                 // dequantisation/FMA path of the kernel instance (see gemv_kernel.cuh)
+    int math;                 // kernel family and dequantisation path (0/1 CUDA cores, 2-4 mma from registers,
+                              // 5-7 TMA-fed mma; see gemv_kernel.cuh, gemv_mma.cuh, gemv_tma.cuh)
     KernelFn fn;
-    size_t (*smem)(int K);    // dynamic shared memory bytes for a given K
+    size_t (*smem)(int K);    // dynamic shared memory bytes for a given K (kernels without a prep step)
+    // TMA kernels: fills the stage geometry of p for the device's shared-memory capacity and returns the dynamic
+    // shared memory bytes (0 if the shape cannot be staged); threads per CTA are (W + 1) * 32 (a producer warp).
+    size_t (*prep)(Params& p, size_t cap);
 };
 
 // Launch-time knobs beyond the tuple (the _ex entry points); zero means "choose automatically".
 struct LaunchOpts {
     int ks;                   // warps per row (power of two dividing W), 0 = auto
-    int ctas_per_sm;          // 0 = auto (resident CTAs, halved under PDL)
+    int ctas_per_sm;          // 0 = auto (all resident CTAs)
+    int ring = 0;             // TMA kernels: ring stages (0 = as many as fit, else 2..16)
+    int share = 0;            // TMA kernels: size the CTA for 1/share of the SM's shared memory (0 = 1: all of it);
+                              // share 2 with one CTA per SM leaves room for the next kernel's CTA under PDL
 };
 
 int sm_count();                                              // current device, cached
 int max_ctas_per_sm(KernelFn fn, int threads, size_t smem);  // occupancy, cached; 0 if it cannot launch
+size_t sm_smem_bytes();                                      // shared memory per SM, less one CTA's reservation
 size_t max_dyn_smem();                                       // opt-in shared memory per block, current device
 
 inline int ilog2(int v) { int l = 0; while ((1 << (l + 1)) <= v) ++l; return l; }
@@ -49,9 +57,19 @@ inline int choose_ks(int nchunk, int rows_per_cta, int W, int R, int U) {
 }
 
 inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaStream_t st) {
-    const size_t smem = v.smem(p.K);
-    if (smem > max_dyn_smem()) return -2;
-    const int threads = v.W * 32;
+    size_t smem;
+    if (v.prep) {
+        const int share = o.share > 0 ? o.share : 1;
+        if (share > 4) return -2;
+        size_t cap = sm_smem_bytes() / share - (share > 1 ? 1024 : 0);
+        if (cap > max_dyn_smem()) cap = max_dyn_smem();
+        p.ring = o.ring;
+        smem = v.prep(p, cap);
+    } else {
+        smem = v.smem(p.K);
+    }
+    if (smem == 0 || smem > max_dyn_smem()) return -2;
+    const int threads = (v.prep ? v.W + 1 : v.W) * 32;
     const int occ = max_ctas_per_sm(v.fn, threads, smem);
     if (occ <= 0) return -2;
     // Full occupancy by default: under PDL the next kernel's CTAs take the SM slots that this grid's CTAs free at
@@ -61,8 +79,11 @@ inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaS
     long long G = (long long)sm_count() * per_sm;
     if (G > p.N) G = p.N;
     const int rows_per_cta = (int)((p.N + G - 1) / G);
-    int ks = o.ks > 0 ? o.ks : choose_ks(p.nchunk, rows_per_cta, v.W, v.R, v.U);
-    if (ks > v.W || (v.W % ks) != 0 || (ks & (ks - 1)) != 0) return -2;
+    int ks = 1;                                               // the tensor-core kernels split work themselves
+    if (v.math < 2) {
+        ks = o.ks > 0 ? o.ks : choose_ks(p.nchunk, rows_per_cta, v.W, v.R, v.U);
+        if (ks > v.W || (v.W % ks) != 0 || (ks & (ks - 1)) != 0) return -2;
+    }
     p.ks_log2 = ilog2(ks);
 
     cudaLaunchConfig_t cfg = {};
@@ -92,6 +113,8 @@ const Variant* table_int4(int* n);
 const Variant* table_int4a(int* n);
 // Extra kernel instances reachable only through paia_gemv_launch_ex (tuning): same tuple space, other math paths.
 const Variant* find_instance(int fmt, int R, int U, int W, int math);
-const Variant* mma_instances(int fmt, int* n);
+const Variant* mma_instances(int fmt, int math, int* n);
+const Variant* tma_instances(int fmt, int math, int* n);
+int tma_device_error(int clear);
 
 }  // namespace pb2

@@ -6,8 +6,8 @@
 // CUDA-core dot product cannot keep up with HBM3e. Here the dequantised weights go straight from registers into
 // mma.sync.m16n8k16 (A = weights, B = x in column 0, fp32 accumulate): the tensor core does the multiply and the
 // 4-lane reduction, and a lane spends about one issue slot per weight on conversion (INT4: one LOP3 per two weights;
-// FP8: one cvt per two weights; BF16: none). Weights still stream from HBM exactly once in 16-byte loads; there is no
-// shared-memory staging of weights.
+// FP8: one cvt or a few bit operations per two weights; BF16: none). Weights still stream from HBM exactly once in
+// 16-byte loads; there is no shared-memory staging of weights.
 //
 // Fragment mapping (PTX ISA, mma.m16n8k16, .f16/.bf16): lane = 4 g + c. A regs: a0 = (row g, k 2c..2c+1),
 // a1 = (row g+8, same k), a2 = (row g, k 2c+8..2c+9), a3 = (row g+8, same k); B regs: b0 = (k 2c..2c+1, col g),
@@ -18,16 +18,20 @@
 //
 // One step = 64 bytes of each of the 16 rows of a tile (lane c loads bytes 16c..16c+15 of the step):
 //   BF16  32 k per step, 2 MMAs (bf16). k slots of MMA h: (k0+4h, k0+4h+1) and (k0+4h+2, k0+4h+3), k0 = 32 s + 8 c.
-//   FP8   64 k per step, 4 MMAs (f16). Weights: cvt.rn.f16x2.e4m3x2 (exact). x is staged as f16 scaled by 2^-e with
-//         e chosen per launch from max|x| (max|x| * 2^-e in [2^14, 2^15)); y = D * 2^e * scale[row].
+//   FP8   64 k per step, 4 MMAs (f16). Weights: cvt.rn.f16x2.e4m3x2 (exact) or the bit decode below (value/256,
+//         exact). x is staged as f16 scaled by 2^-e with e chosen per launch from max|x| (max|x| * 2^-e in
+//         [2^14, 2^15)); y = ldexp(D * scale[row], e).
 //   INT4  128 k per step = one quantisation group, 8 MMAs (bf16). Word i of the chunk holds k0+8i+j at nibble j;
 //         (w >> 4j) & 0x000F000F | 0x43004300 is the bf16 pair (128 + n_{8i+j}, 128 + n_{8i+j+4}). x is staged with
 //         each 8-block permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7) so B loads match. Per group and row:
 //         acc += s * (D - 136 * sum_group(x)) (+ z * sum_group(x) for the asymmetric format).
 //
-// Tiles, split-K and grid: as in gemv_kernel.cuh the grid is persistent and CTA c owns the contiguous rows
-// [c N/G, (c+1) N/G); a tile is 16 of them (the last one masked), and the NW warps of the CTA split the tile's steps
-// evenly (warp w takes steps [w S/NW, (w+1) S/NW)), meeting in shared memory once per tile.
+// Work split (stream-K inside the CTA): the grid is persistent and CTA c owns the contiguous rows [c N/G, (c+1) N/G),
+// cut into 16-row tiles (the last one masked: its loads are clamped to the CTA's last row, its stores skipped). The
+// CTA's T tiles x S steps form one linear index space that the NW warps split into equal contiguous ranges, so every
+// warp streams the same number of bytes (+-1 step). A tile that lies inside one warp's range is finished by that warp
+// alone (no barrier); only the tiles that straddle warp boundaries (at most NW - 1 per CTA) leave partial sums in
+// shared memory, which are added in a fixed order once at the end (deterministic results).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -45,213 +49,62 @@ template <> struct MmaStep<kINT4A> { static constexpr int k = 128; };
 
 __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-                 "{%8, %9}, {%0, %1, %2, %3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-                 "{%8, %9}, {%0, %1, %2, %3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
     const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
+// e4m3 bytes b0..b3 of w -> f16 pairs holding value/256 exactly (the e4m3 exponent and mantissa bits land on the low
+// f16 exponent bits and the top mantissa bits, sign on the sign bit; subnormal codes land on f16 subnormals).
+// (b0, b2): magnitudes shift by 7, signs by 8. (b1, b3): magnitudes shift right by 1, signs stay.
+__device__ __forceinline__ uint32_t e4m3_pair02_div256(uint32_t w) {
+    return ((w << 7) & 0x3F803F80u) | ((w << 8) & 0x80008000u);
+}
+__device__ __forceinline__ uint32_t e4m3_pair13_div256(uint32_t w) {
+    return ((w >> 1) & 0x3F803F80u) | (w & 0x80008000u);
+}
 __device__ __forceinline__ uint32_t nib_pair_bf16(uint32_t w, int j) {   // (128 + n_j, 128 + n_{j+4}) as bf16x2
     return ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
 }
-__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
 
 template <int F>
 __host__ __device__ constexpr int mma_kpad(int K) { return (K + MmaStep<F>::k - 1) / MmaStep<F>::k * MmaStep<F>::k; }
 
-// Shared memory: x [Kpad] 16-bit values, then (INT4) sum of x per 128-group [Kpad/128] floats, then the cross-warp
-// reduction buffer [2][NW][16] floats, then one float (FP8: 2^e).
+// Shared memory: x [Kpad] 16-bit values, then (INT4) sum of x per 128-group [Kpad/128] floats, then the partial sums
+// of straddling tiles [NW][2][16] floats, then two words (FP8: the exponent e and 2^-e).
 template <int F, int NW>
 __host__ __device__ constexpr size_t mma_smem_bytes(int K) {
     return (size_t)mma_kpad<F>(K) * 2 + ((F == kINT4 || F == kINT4A) ? (size_t)(mma_kpad<F>(K) / 128) * 4 : 0) +
            (size_t)2 * NW * 16 * 4 + 16;
 }
 
-template <int U>
-struct MmaFrag {
-    uint4 w0[U], w1[U];      // 16-byte chunks of rows g and g+8 for U steps
-    uint32_t m0[U], m1[U];   // INT4: scale bits (INT4A: scale | zero << 16) of rows g and g+8, group = step
-    float rs, rb;            // epilogue row data for lane < 16 of warp 0 (FP8 row scale, bias)
-};
-
-template <int F, int NW, int U>
-__global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(const Params p) {
-    constexpr bool I4 = (F == kINT4 || F == kINT4A);
-    constexpr int SK = MmaStep<F>::k;
-    extern __shared__ __align__(16) uint8_t smem[];
+// Stage x for the tensor-core kernels (padded with zeros to Kpad): BF16 as is; FP8 as f16 scaled by 2^-e (e from the
+// CTA-wide max|x|, written to xscale[0] as an int, 2^-e to xscale[1]) with the 4-block order the FP8 decoder DEC
+// expects; INT4 with each 8-block permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7) plus the sum of every 128-group.
+// Called by `nthr` threads (thread index tid); `sync` is the barrier over exactly those threads; `scratch` holds
+// nthr/32 floats. Ends with x visible to the caller only after the caller's own barrier.
+template <int F, int DEC, typename Sync>
+__device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gsum, float* xscale, float* scratch, int tid,
+                                        int nthr, Sync sync) {
     const int Kp = mma_kpad<F>(p.K);
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
-    float* gsum = reinterpret_cast<float*>(smem + (size_t)Kp * 2);
-    float* red = reinterpret_cast<float*>(smem + (size_t)Kp * 2 + (I4 ? (size_t)(Kp / 128) * 4 : 0));
-    float* xscale = red + 2 * NW * 16;
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, c = lane & 3;
-    const int rb = (int)((long long)blockIdx.x * p.N / gridDim.x);
-    const int re = (int)((long long)(blockIdx.x + 1) * p.N / gridDim.x);
-    const int ntiles = (re - rb + 15) >> 4;
-    const int S = (p.nchunk + 3) >> 2;                       // 64-byte steps per row
-    const int sb = (int)((long long)S * warp / NW), se = (int)((long long)S * (warp + 1) / NW);
-    const int nbatch = (se - sb) > U ? (se - sb + U - 1) / U : 1;
-    const int nit = ntiles * nbatch;
-    const size_t rowbytes = (size_t)p.nchunk * 16;
-
-    auto load = [&](MmaFrag<U>& f, int t, int b) {
-        const int r0 = rb + t * 16 + g, r1 = r0 + 8;
-        const bool v0 = r0 < re, v1 = r1 < re;
-        const uint8_t* w0 = p.W + (size_t)r0 * rowbytes;
-        const uint8_t* w1 = p.W + (size_t)r1 * rowbytes;
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int s = sb + b * U + u;
-            const int q = 4 * s + c;                          // 16-byte chunk index within the row
-            const bool sv = s < se && q < p.nchunk;
-            f.w0[u] = (sv && v0) ? ld_stream(w0 + (size_t)q * 16) : make_uint4(0u, 0u, 0u, 0u);
-            f.w1[u] = (sv && v1) ? ld_stream(w1 + (size_t)q * 16) : make_uint4(0u, 0u, 0u, 0u);
-            if constexpr (I4) {
-                f.m0[u] = f.m1[u] = 0u;
-                if (c == 0 && s < se) {
-                    if constexpr (F == kINT4) {
-                        const __half* sp = reinterpret_cast<const __half*>(p.s);
-                        if (v0) f.m0[u] = ld_u16(sp + (size_t)r0 * p.groups + s);
-                        if (v1) f.m1[u] = ld_u16(sp + (size_t)r1 * p.groups + s);
-                    } else {
-                        const __nv_bfloat16* sp = reinterpret_cast<const __nv_bfloat16*>(p.s);
-                        const __nv_bfloat16* zp = reinterpret_cast<const __nv_bfloat16*>(p.z);
-                        if (v0) f.m0[u] = (uint32_t)ld_u16(sp + (size_t)r0 * p.groups + s) |
-                                          ((uint32_t)ld_u16(zp + (size_t)r0 * p.groups + s) << 16);
-                        if (v1) f.m1[u] = (uint32_t)ld_u16(sp + (size_t)r1 * p.groups + s) |
-                                          ((uint32_t)ld_u16(zp + (size_t)r1 * p.groups + s) << 16);
-                    }
-                }
-            }
-        }
-        if (b == 0) {
-            f.rs = 1.f;
-            f.rb = 0.f;
-            if (warp == 0 && lane < 16) {
-                const int row = rb + t * 16 + lane;
-                if (row < re) {
-                    if constexpr (F == kFP8) f.rs = ld_f32(reinterpret_cast<const float*>(p.s) + row);
-                    if (p.bias) f.rb = __uint_as_float((uint32_t)ld_u16(p.bias + row) << 16);
-                }
-            }
-        }
-    };
-
-    float D[U][4];                 // BF16/FP8: one accumulator per in-flight step (independent MMA chains)
-    float acc0 = 0.f, acc1 = 0.f;  // INT4: scaled per-group sums of rows g and g+8 (lanes c == 0)
-    float cur_rs = 1.f, cur_rb = 0.f;
-#pragma unroll
-    for (int u = 0; u < U; ++u) D[u][0] = D[u][1] = D[u][2] = D[u][3] = 0.f;
-
-    auto compute = [&](const MmaFrag<U>& f, int t, int b) {
-        if (b == 0) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) D[u][0] = D[u][1] = D[u][2] = D[u][3] = 0.f;
-            acc0 = acc1 = 0.f;
-            cur_rs = f.rs;
-            cur_rb = f.rb;
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int s = sb + b * U + u;
-            if (s < se) {                                     // warp-uniform
-                const uint4 A0 = f.w0[u], A1 = f.w1[u];
-                if constexpr (F == kBF16) {
-                    const uint16_t* xp = xs + (size_t)s * SK + 8 * c;
-                    const uint2 x01 = lds64(xp), x23 = lds64(xp + 4);
-                    mma_bf16(D[u], A0.x, A1.x, A0.y, A1.y, x01.x, x01.y);
-                    mma_bf16(D[u], A0.z, A1.z, A0.w, A1.w, x23.x, x23.y);
-                } else if constexpr (F == kFP8) {
-                    const uint16_t* xp = xs + (size_t)s * SK + 16 * c;
-                    const uint4 xa = *reinterpret_cast<const uint4*>(xp);
-                    const uint4 xb = *reinterpret_cast<const uint4*>(xp + 8);
-                    const uint32_t w0[4] = {A0.x, A0.y, A0.z, A0.w}, w1[4] = {A1.x, A1.y, A1.z, A1.w};
-                    const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-                    for (int t4 = 0; t4 < 4; ++t4)
-                        mma_f16(D[u], e4m3x2_to_f16x2(w0[t4] & 0xFFFFu), e4m3x2_to_f16x2(w1[t4] & 0xFFFFu),
-                                e4m3x2_to_f16x2(w0[t4] >> 16), e4m3x2_to_f16x2(w1[t4] >> 16),
-                                xv[2 * t4], xv[2 * t4 + 1]);
-                } else {
-                    const uint16_t* xp = xs + (size_t)s * SK + 32 * c;
-                    const uint32_t w0[4] = {A0.x, A0.y, A0.z, A0.w}, w1[4] = {A1.x, A1.y, A1.z, A1.w};
-                    float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint4 xb = *reinterpret_cast<const uint4*>(xp + 8 * i);   // permuted pairs of block i
-                        mma_bf16(d, nib_pair_bf16(w0[i], 0), nib_pair_bf16(w1[i], 0), nib_pair_bf16(w0[i], 1),
-                                 nib_pair_bf16(w1[i], 1), xb.x, xb.y);
-                        mma_bf16(d, nib_pair_bf16(w0[i], 2), nib_pair_bf16(w1[i], 2), nib_pair_bf16(w0[i], 3),
-                                 nib_pair_bf16(w1[i], 3), xb.z, xb.w);
-                    }
-                    if (c == 0) {
-                        const float sx = gsum[s];
-                        const float off = -136.f * sx;
-                        if constexpr (F == kINT4) {
-                            acc0 = fmaf(__half2float(__ushort_as_half((unsigned short)(f.m0[u] & 0xFFFFu))), d[0] + off, acc0);
-                            acc1 = fmaf(__half2float(__ushort_as_half((unsigned short)(f.m1[u] & 0xFFFFu))), d[2] + off, acc1);
-                        } else {
-                            acc0 = fmaf(bf_lo(f.m0[u]), d[0] + off, acc0);
-                            acc0 = fmaf(bf_hi(f.m0[u]), sx, acc0);
-                            acc1 = fmaf(bf_lo(f.m1[u]), d[2] + off, acc1);
-                            acc1 = fmaf(bf_hi(f.m1[u]), sx, acc1);
-                        }
-                    }
-                }
-            }
-        }
-        if (b == nbatch - 1) {
-            float s0, s1;
-            if constexpr (I4) {
-                s0 = acc0; s1 = acc1;
-            } else {
-                s0 = 0.f; s1 = 0.f;
-#pragma unroll
-                for (int u = 0; u < U; ++u) { s0 += D[u][0]; s1 += D[u][2]; }
-            }
-            float* buf = red + (size_t)(t & 1) * NW * 16;
-            if (c == 0) { buf[warp * 16 + g] = s0; buf[warp * 16 + g + 8] = s1; }
-            __syncthreads();
-            if (warp == 0 && lane < 16) {
-                float total = 0.f;
-#pragma unroll
-                for (int w = 0; w < NW; ++w) total += buf[w * 16 + lane];
-                const int row = rb + t * 16 + lane;
-                if (row < re) {
-                    float out = total;
-                    if constexpr (F == kFP8) out = (out * xscale[0]) * cur_rs;
-                    out = out + cur_rb;
-                    p.y[row] = __float2bfloat16_rn(out);
-                }
-            }
-        }
-    };
-
-    MmaFrag<U> fa, fb;
-    if (nit > 0) load(fa, 0, 0);                 // weights and their metadata: independent of the previous kernel
-
-    grid_dependency_wait();
-
-    // ---- stage x (padded with zeros to Kpad)
-    const int nthr = NW * 32;
     if constexpr (F == kBF16) {
         for (int i = tid; i < Kp / 8; i += nthr) {
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (8 * i < p.K) v = __ldg(reinterpret_cast<const uint4*>(p.x) + i);   // K % 8 == 0
             reinterpret_cast<uint4*>(xs)[i] = v;
         }
+        if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     } else if constexpr (F == kFP8) {
         // max |x| over the CTA, then x * 2^-e in f16 (exact while max|x| * 2^-e < 2^15 and values stay normal)
         float m = 0.f;
@@ -262,21 +115,21 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(const Params p) {
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) red[warp] = m;
-        __syncthreads();
+        if ((tid & 31) == 0) scratch[tid >> 5] = m;
+        sync();
         if (tid == 0) {
             float mm = 0.f;
-            for (int w = 0; w < NW; ++w) mm = fmaxf(mm, red[w]);
+            for (int w = 0; w < nthr / 32; ++w) mm = fmaxf(mm, scratch[w]);
             int e = 0;
-            if (mm > 0.f && mm <= 3.0e38f) {                    // finite and nonzero (NaN compares false)
+            if (mm > 0.f && mm <= 3.40282347e38f) {             // finite and nonzero (NaN compares false)
                 const int ex = (int)((__float_as_uint(mm) >> 23) & 0xFF) - 127;   // floor(log2) for normal mm
                 e = (ex < -126 ? -126 : ex) - 14;           // max|x| * 2^-e in [2^14, 2^15)
                 e = e < -126 ? -126 : (e > 126 ? 126 : e);  // 2^e and 2^-e both normal floats
             }
-            xscale[0] = __uint_as_float((uint32_t)(127 + e) << 23);      // 2^e
+            xscale[0] = __int_as_float(e);                               // e (applied with ldexpf)
             xscale[1] = __uint_as_float((uint32_t)(127 - e) << 23);      // 2^-e
         }
-        __syncthreads();
+        sync();
         const float inv = xscale[1];
         for (int i = tid; i < Kp / 8; i += nthr) {
             uint4 o = make_uint4(0u, 0u, 0u, 0u);
@@ -289,11 +142,16 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(const Params p) {
                     const __half2 h = __floats2half2_rn(bf_lo(vv[j]) * inv, bf_hi(vv[j]) * inv);
                     oo[j] = *reinterpret_cast<const uint32_t*>(&h);
                 }
+                // words decoded on the ALU pair k (0,2) and (1,3) of each 4-block: store x in that order
+                if (DEC == 1 || (DEC == 2 && (i & 1))) {
+                    const uint32_t a0 = __byte_perm(oo[0], oo[1], 0x5410), a1 = __byte_perm(oo[0], oo[1], 0x7632);
+                    const uint32_t a2 = __byte_perm(oo[2], oo[3], 0x5410), a3 = __byte_perm(oo[2], oo[3], 0x7632);
+                    oo[0] = a0; oo[1] = a1; oo[2] = a2; oo[3] = a3;
+                }
                 o = make_uint4(oo[0], oo[1], oo[2], oo[3]);
             }
             reinterpret_cast<uint4*>(xs)[i] = o;
         }
-        __syncthreads();                                        // red[] is reused by the tile reductions
     } else {
         // 8-element blocks permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7); sum of each 128-group (16 blocks)
         const int nb = p.K / 8;                                  // K % 128 == 0 -> nb % 16 == 0
@@ -314,26 +172,277 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(const Params p) {
             for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);   // 16-lane groups
             if (i < nb && (i & 15) == 0) gsum[i >> 4] = sum;
         }
+        if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     }
-    if constexpr (F == kBF16 || I4) {
-        if (tid == 0) { xscale[0] = 1.f; xscale[1] = 1.f; }
-    }
+}
+
+template <int U>
+struct MmaFrag {
+    uint4 w0[U], w1[U];        // 16-byte chunks of rows g and g+8 for U steps
+    uint32_t m0[U], m1[U];     // INT4: scale bits (INT4A: scale | zero << 16) of rows g and g+8, group = step
+    float rs0, rs1, rb0, rb1;  // epilogue data of rows g and g+8 (FP8 row scale, bias), loaded with a tile's step 0
+};
+
+// DEC (FP8 only): 0 = every word through cvt.rn.f16x2.e4m3x2; 1 = every word through the ALU bit decode (value/256);
+// 2 = words 0,1 of each 16-byte chunk through cvt and words 2,3 through the ALU, which splits the decode between the
+// two pipes (the hardware conversion does not run on the ALU pipe and saturates first when used alone).
+template <int F, int NW, int U, int DEC = 0>
+__global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(const Params p) {
+    constexpr bool I4 = (F == kINT4 || F == kINT4A);
+    constexpr int SK = MmaStep<F>::k;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int Kp = mma_kpad<F>(p.K);
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
+    float* gsum = reinterpret_cast<float*>(smem + (size_t)Kp * 2);
+    float* part = reinterpret_cast<float*>(smem + (size_t)Kp * 2 + (I4 ? (size_t)(Kp / 128) * 4 : 0));
+    float* xscale = part + 2 * NW * 16;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, c = lane & 3;
+    const int rb = (int)((long long)blockIdx.x * p.N / gridDim.x);
+    const int re = (int)((long long)(blockIdx.x + 1) * p.N / gridDim.x);
+    const int T = (re - rb + 15) >> 4;                      // tiles of this CTA
+    const int S = (p.nchunk + 3) >> 2;                      // 64-byte steps per row
+    const int total = T * S;
+    const int wb = (int)((long long)total * warp / NW), we = (int)((long long)total * (warp + 1) / NW);
+    const bool ragged = (p.nchunk & 3) != 0;                // the last step of a row is partial
+    const size_t rowbytes = (size_t)p.nchunk * 16;
+    const int first_tile = wb / S;
+
+    // iteration = (tile t, first step s, n steps): n <= U, never crossing a tile boundary or the end of the range
+    auto it_n = [&](int cur) {
+        const int s = cur % S;
+        int n = S - s;
+        if (n > U) n = U;
+        if (n > we - cur) n = we - cur;
+        return n;
+    };
+
+    auto load = [&](MmaFrag<U>& f, int cur) {
+        const int t = cur / S, s = cur - t * S, n = it_n(cur);
+        const int r0 = rb + t * 16 + g, r1 = r0 + 8;
+        const int r0c = r0 < re ? r0 : re - 1, r1c = r1 < re ? r1 : re - 1;   // clamped: loads stay inside W
+        const uint8_t* p0 = p.W + (size_t)r0c * rowbytes + (size_t)(4 * s + c) * 16;
+        const uint8_t* p1 = p.W + (size_t)r1c * rowbytes + (size_t)(4 * s + c) * 16;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const bool ok = u < n && (!ragged || 4 * (s + u) + c < p.nchunk);
+            f.w0[u] = ok ? ld_stream(p0 + 64 * u) : make_uint4(0u, 0u, 0u, 0u);
+            f.w1[u] = ok ? ld_stream(p1 + 64 * u) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        if constexpr (I4) {
+            const uint16_t* sp0 = reinterpret_cast<const uint16_t*>(p.s) + (size_t)r0c * p.groups + s;
+            const uint16_t* sp1 = reinterpret_cast<const uint16_t*>(p.s) + (size_t)r1c * p.groups + s;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                f.m0[u] = f.m1[u] = 0u;
+                if (u < n) {
+                    f.m0[u] = ld_u16(sp0 + u);
+                    f.m1[u] = ld_u16(sp1 + u);
+                    if constexpr (F == kINT4A) {
+                        const uint16_t* zp0 = reinterpret_cast<const uint16_t*>(p.z) + (size_t)r0c * p.groups + s;
+                        const uint16_t* zp1 = reinterpret_cast<const uint16_t*>(p.z) + (size_t)r1c * p.groups + s;
+                        f.m0[u] |= (uint32_t)ld_u16(zp0 + u) << 16;
+                        f.m1[u] |= (uint32_t)ld_u16(zp1 + u) << 16;
+                    }
+                }
+            }
+        }
+        f.rs0 = f.rs1 = 1.f;
+        f.rb0 = f.rb1 = 0.f;
+        if (s == 0) {
+            if constexpr (F == kFP8) {
+                f.rs0 = ld_f32(reinterpret_cast<const float*>(p.s) + r0c);
+                f.rs1 = ld_f32(reinterpret_cast<const float*>(p.s) + r1c);
+            }
+            if (p.bias) {
+                f.rb0 = __uint_as_float((uint32_t)ld_u16(p.bias + r0c) << 16);
+                f.rb1 = __uint_as_float((uint32_t)ld_u16(p.bias + r1c) << 16);
+            }
+        }
+    };
+
+    float D[U][4];                 // BF16/FP8: one accumulator per in-flight step (independent MMA chains)
+    float E[U][4];                 // FP8 words decoded on the ALU (value/256), folded in with a factor 256
+    float acc0 = 0.f, acc1 = 0.f;  // INT4: scaled per-group sums of rows g and g+8
+    float rs0 = 1.f, rs1 = 1.f, rb0 = 0.f, rb1 = 0.f;
+    int seg_s = -1;                // first step of the current tile segment (-1: none open)
+#pragma unroll
+    for (int u = 0; u < U; ++u) D[u][0] = D[u][1] = D[u][2] = D[u][3] = E[u][0] = E[u][1] = E[u][2] = E[u][3] = 0.f;
+
+    auto epilogue = [&](float v, float rs, float rbias) {
+        float out = v;
+        if constexpr (F == kFP8) out = ldexpf(out * rs, __float_as_int(xscale[0]));   // row scale, then 2^e
+        return __float2bfloat16_rn(out + rbias);
+    };
+
+    auto compute = [&](const MmaFrag<U>& f, int cur) {
+        const int t = cur / S, s = cur - t * S, n = it_n(cur);
+        if (seg_s < 0) {
+            seg_s = s;
+            rs0 = f.rs0; rs1 = f.rs1; rb0 = f.rb0; rb1 = f.rb1;
+        }
+        bool v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = u < n;              // warp-uniform
+        const uint16_t* xb = xs + (size_t)s * SK + c * (SK / 4);
+        if constexpr (F == kBF16) {
+            uint4 xv[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                xv[u] = v[u] ? *reinterpret_cast<const uint4*>(xb + u * SK) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (v[u]) mma_bf16(D[u], f.w0[u].x, f.w1[u].x, f.w0[u].y, f.w1[u].y, xv[u].x, xv[u].y);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (v[u]) mma_bf16(D[u], f.w0[u].z, f.w1[u].z, f.w0[u].w, f.w1[u].w, xv[u].z, xv[u].w);
+        } else if constexpr (F == kFP8) {
+            uint32_t xv[U][8];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint4 xa = v[u] ? *reinterpret_cast<const uint4*>(xb + u * SK) : make_uint4(0u, 0u, 0u, 0u);
+                const uint4 xc = v[u] ? *reinterpret_cast<const uint4*>(xb + u * SK + 8) : make_uint4(0u, 0u, 0u, 0u);
+                xv[u][0] = xa.x; xv[u][1] = xa.y; xv[u][2] = xa.z; xv[u][3] = xa.w;
+                xv[u][4] = xc.x; xv[u][5] = xc.y; xv[u][6] = xc.z; xv[u][7] = xc.w;
+            }
+#pragma unroll
+            for (int t4 = 0; t4 < 4; ++t4) {
+                const bool alu = (DEC == 1) || (DEC == 2 && t4 >= 2);   // which decoder handles word t4
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (!v[u]) continue;
+                    const uint32_t a = (&f.w0[u].x)[t4], bb = (&f.w1[u].x)[t4];
+                    if (alu)
+                        mma_f16(E[u], e4m3_pair02_div256(a), e4m3_pair02_div256(bb), e4m3_pair13_div256(a),
+                                e4m3_pair13_div256(bb), xv[u][2 * t4], xv[u][2 * t4 + 1]);
+                    else
+                        mma_f16(D[u], e4m3x2_to_f16x2(a & 0xFFFFu), e4m3x2_to_f16x2(bb & 0xFFFFu),
+                                e4m3x2_to_f16x2(a >> 16), e4m3x2_to_f16x2(bb >> 16), xv[u][2 * t4], xv[u][2 * t4 + 1]);
+                }
+            }
+        } else {
+            float d[U][4];
+#pragma unroll
+            for (int u = 0; u < U; ++u) d[u][0] = d[u][1] = d[u][2] = d[u][3] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint4 xq[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u)      // permuted pairs of 8-block i
+                    xq[u] = v[u] ? *reinterpret_cast<const uint4*>(xb + u * SK + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (!v[u]) continue;
+                    const uint32_t a = (&f.w0[u].x)[i], bb = (&f.w1[u].x)[i];
+                    mma_bf16(d[u], nib_pair_bf16(a, 0), nib_pair_bf16(bb, 0), nib_pair_bf16(a, 1),
+                             nib_pair_bf16(bb, 1), xq[u].x, xq[u].y);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (!v[u]) continue;
+                    const uint32_t a = (&f.w0[u].x)[i], bb = (&f.w1[u].x)[i];
+                    mma_bf16(d[u], nib_pair_bf16(a, 2), nib_pair_bf16(bb, 2), nib_pair_bf16(a, 3),
+                             nib_pair_bf16(bb, 3), xq[u].z, xq[u].w);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (!v[u]) continue;
+                const float sx = gsum[s + u];
+                const float off = -136.f * sx;
+                if constexpr (F == kINT4) {
+                    acc0 = fmaf(__half2float(__ushort_as_half((unsigned short)(f.m0[u] & 0xFFFFu))), d[u][0] + off, acc0);
+                    acc1 = fmaf(__half2float(__ushort_as_half((unsigned short)(f.m1[u] & 0xFFFFu))), d[u][2] + off, acc1);
+                } else {
+                    acc0 = fmaf(bf_lo(f.m0[u]), d[u][0] + off, acc0);
+                    acc0 = fmaf(bf_hi(f.m0[u]), sx, acc0);
+                    acc1 = fmaf(bf_lo(f.m1[u]), d[u][2] + off, acc1);
+                    acc1 = fmaf(bf_hi(f.m1[u]), sx, acc1);
+                }
+            }
+        }
+        // end of this warp's segment of tile t: finish the tile, or leave a partial sum for the cleanup pass
+        if (s + n == S || cur + n == we) {
+            float s0, s1;
+            if constexpr (I4) {
+                s0 = acc0; s1 = acc1;
+                acc0 = acc1 = 0.f;
+            } else {
+                s0 = 0.f; s1 = 0.f;
+#pragma unroll
+                for (int u = 0; u < U; ++u) { s0 += D[u][0]; s1 += D[u][2]; }
+                if constexpr (F == kFP8 && DEC != 0) {
+                    float e0 = 0.f, e1 = 0.f;
+#pragma unroll
+                    for (int u = 0; u < U; ++u) { e0 += E[u][0]; e1 += E[u][2]; }
+                    s0 = fmaf(256.f, e0, s0);
+                    s1 = fmaf(256.f, e1, s1);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+                    D[u][0] = D[u][1] = D[u][2] = D[u][3] = E[u][0] = E[u][1] = E[u][2] = E[u][3] = 0.f;
+            }
+            const bool whole = seg_s == 0 && s + n == S;
+            if (c == 0) {
+                const int r0 = rb + t * 16 + g, r1 = r0 + 8;
+                if (whole) {
+                    if (r0 < re) p.y[r0] = epilogue(s0, rs0, rb0);
+                    if (r1 < re) p.y[r1] = epilogue(s1, rs1, rb1);
+                } else {
+                    float* slot = part + ((size_t)warp * 2 + (t == first_tile ? 0 : 1)) * 16;
+                    slot[g] = s0;
+                    slot[g + 8] = s1;
+                }
+            }
+            seg_s = -1;
+        }
+    };
+
+    MmaFrag<U> fa, fb;
+    if (wb < we) load(fa, wb);                  // weights and their metadata: independent of the previous kernel
+
+    grid_dependency_wait();
+
+    stage_x<F, DEC>(p, xs, gsum, xscale, part, tid, NW * 32, []() { __syncthreads(); });
     __syncthreads();
     launch_dependents();
 
-    int t = 0, b = 0;
-    for (int it = 0; it < nit;) {
-        int t1 = t, b1 = b + 1;
-        if (b1 == nbatch) { b1 = 0; ++t1; }
-        if (it + 1 < nit) load(fb, t1, b1);
-        compute(fa, t, b);
-        ++it; t = t1; b = b1;
-        if (it >= nit) break;
-        int t2 = t, b2 = b + 1;
-        if (b2 == nbatch) { b2 = 0; ++t2; }
-        if (it + 1 < nit) load(fa, t2, b2);
-        compute(fb, t, b);
-        ++it; t = t2; b = b2;
+    for (int cur = wb; cur < we;) {
+        const int nxt = cur + it_n(cur);
+        if (nxt < we) load(fb, nxt);
+        compute(fa, cur);
+        cur = nxt;
+        if (cur >= we) break;
+        const int nxt2 = cur + it_n(cur);
+        if (nxt2 < we) load(fa, nxt2);
+        compute(fb, cur);
+        cur = nxt2;
+    }
+
+    // Tiles that straddle warp boundaries: add the partial sums of every warp that touched them, in warp order.
+    __syncthreads();
+    for (int j = tid; j < (NW - 1) * 16; j += NW * 32) {
+        const int w = 1 + j / 16, r = j % 16;                 // boundary between warps w-1 and w
+        const int bw = (int)((long long)total * w / NW);
+        if (bw % S == 0 || bw >= total) continue;             // the boundary does not cut a tile
+        const int t = bw / S;
+        const int bprev = (int)((long long)total * (w - 1) / NW);
+        if (bprev > t * S) continue;                          // an earlier boundary inside this tile handles it
+        float sum = 0.f;
+        for (int v2 = w - 1; v2 < NW; ++v2) {
+            const int vb = (int)((long long)total * v2 / NW), ve = (int)((long long)total * (v2 + 1) / NW);
+            if (vb >= (t + 1) * S) break;
+            if (ve <= t * S || vb >= ve) continue;
+            sum += part[((size_t)v2 * 2 + (t == vb / S ? 0 : 1)) * 16 + r];
+        }
+        const int row = rb + t * 16 + r;
+        if (row < re) {
+            float rs = 1.f, rbias = 0.f;
+            if constexpr (F == kFP8) rs = ld_f32(reinterpret_cast<const float*>(p.s) + row);
+            if (p.bias) rbias = __uint_as_float((uint32_t)ld_u16(p.bias + row) << 16);
+            p.y[row] = epilogue(sum, rs, rbias);
+        }
     }
 }
 

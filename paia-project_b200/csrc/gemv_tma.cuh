@@ -1,0 +1,465 @@
+// TMA-fed tensor-core GEMV for B200 (sm_100a): the streaming design of the decode GEMV family.
+//
+// Measured on B200: loading MMA fragments straight from HBM (each warp instruction touching 16 rows x 64 B) stops at
+// ~4.4-5.4 TB/s, while bulk copies of contiguous pieces of >= ~2 KB stream at ~6.0-6.3 TB/s with ~170-190 KB in flight
+// per SM. So a producer warp moves the weights with cp.async.bulk (1-D TMA, completion counted on an mbarrier) into
+// a ring of shared-memory stages, and consumer warps read the MMA fragments from shared memory.
+//
+//   CTA       one persistent CTA per SM (or two when the ring is small); rows [c N/G, (c+1) N/G), cut into 16-row
+//             tiles; a tile is streamed as NCH stages of 16 rows x KC bytes (KC a multiple of 64, pieces >= ~2 KB).
+//   producer  warp NC. Lane 0 waits for the slot, then lane r issues row r's bulk copy (rows beyond the CTA's range are not
+//             copied; their MMA rows compute garbage that is never stored) into a padded layout (row stride KC or
+//             KC + 64, so that the two rows a fragment load phase touches sit in different bank halves). The
+//             producer starts at launch, before the programmatic-dependency wait: weights never depend on the
+//             preceding kernel. All 32 lanes then copy the stage's metadata (INT4 scales and zeros of its rows and
+//             groups; FP8 row scales and the bias at a tile's last stage) with 4-byte cp.async, whose completion is
+//             also counted on the stage's `full` mbarrier, so no register ever waits on a load: under a saturated
+//             memory system a plain load takes as long as the whole ring's copies. 2-byte arrays are copied as the
+//             aligned words that hold them (the element parity is recomputed by the readers); a word that would
+//             reach past either end of its array is read with plain loads instead.
+//   consumers warps 0..NC-1 wait for the dependency, stage x (as gemv_mma.cuh), then for every stage take an equal
+//             share of its 64-byte steps, load A fragments from the stage (rows g and g+8, bytes 16c of each step),
+//             B fragments from x, and run the same dequantisation and mma.sync.m16n8k16 as gemv_mma.cuh. The step
+//             loop is branch-free (U steps per iteration; the remainder and the ragged last step of a row run one at a
+//             time) and keeps two accumulator chains per step. At the last stage of a tile each warp leaves its 16
+//             partial sums in shared memory and counts itself in; the last warp to arrive adds the NC partials in warp
+//             order (deterministic) and writes the 16 outputs, before releasing the stage (whose metadata it reads).
+//             No warp waits for another except through the ring.
+//   waits     every mbarrier wait gives up after ~2 s (%globaltimer), records an error code that
+//             paia_gemv_device_error() reports, and carries on without waiting, so a fault can never hang the GPU.
+#pragma once
+#include "gemv_mma.cuh"
+
+namespace pb2 {
+
+static __device__ int g_tma_error;     // first error code of a bounded wait that gave up (0 = none)
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* m, int count) {
+    asm volatile("mbarrier.init.shared.b64 [%0], %1;" :: "r"(smem_addr(m)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* m) {
+    asm volatile("mbarrier.arrive.shared.b64 _, [%0];" :: "r"(smem_addr(m)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* m, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" :: "r"(smem_addr(m)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* m, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_addr(m)), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for phase `parity` of m for at most ~2 s; on timeout record `code` and return false (the caller carries on).
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, int code) {
+    if (mbar_test(m, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_test(m, parity)) {
+        if (global_ns() - t0 > 2000000000ull) {
+            atomicCAS(&g_tma_error, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(m)) : "memory");
+}
+__device__ __forceinline__ void consumer_barrier(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
+}
+// One arrival on m once all of this thread's earlier cp.async copies have landed (counted in m's arrival count).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* m) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" :: "r"(smem_addr(m)) : "memory");
+}
+
+// Word k of the copy of elements [e0, e0 + n) of a 2-byte array a[0, T) into dst (4-byte aligned): the aligned words
+// that hold the range land in dst[2k], dst[2k + 1], so element e sits at dst[u16_parity(a + e0) + e - e0]. A word that
+// reaches outside a[0, T) is read with plain loads of its in-range halves.
+__device__ __forceinline__ int u16_parity(const void* p) { return (int)(((uintptr_t)p >> 1) & 1u); }
+__device__ __forceinline__ int u16_words(const uint16_t* a, long long e0, int n) {
+    const uintptr_t b = (uintptr_t)(a + e0);
+    return (int)(((b + 2 * (uintptr_t)n - 1) >> 2) - (b >> 2) + 1);
+}
+__device__ __forceinline__ void u16_word_copy(uint16_t* dst, const uint16_t* a, long long T, long long e0, int k) {
+    const uintptr_t w = (((uintptr_t)(a + e0)) & ~(uintptr_t)3) + 4 * (uintptr_t)k;
+    const uintptr_t lo = (uintptr_t)a, hi = (uintptr_t)(a + T);
+    if (w >= lo && w + 4 <= hi) {
+        cp_async4(dst + 2 * k, (const void*)w);
+    } else {
+        if (w >= lo && w + 2 <= hi) dst[2 * k] = ld_u16((const void*)w);
+        if (w + 2 >= lo && w + 4 <= hi) dst[2 * k + 1] = ld_u16((const void*)(w + 2));
+    }
+}
+
+constexpr int kTmaMaxRing = 16;        // ring stages at most (mbarrier region 256 bytes)
+
+// Metadata slot of a stage (bytes): FP8 row scales float[16] at 0; bias words (18 halves) at 64; INT4 scales and
+// (INT4A) zeros at 112, 16 rows x tma_meta_row(CS) halves each.
+__host__ __device__ constexpr int tma_meta_row(int cs) { return (cs + 3) & ~1; }     // >= CS + 2 halves, even
+template <int F>
+__host__ __device__ constexpr int tma_meta_bytes(int cs) {
+    return 112 + ((F == kINT4 || F == kINT4A) ? 16 * tma_meta_row(cs) * 2 * (F == kINT4A ? 2 : 1) : 0);
+}
+// Tile-partial buffers: a warp runs at most ring - 1 stages ahead of the slowest, i.e. ceil((ring - 1) / NCH) + 1
+// tiles; one more buffer keeps the last arriver's reads apart from the next writers.
+__host__ __device__ constexpr int tma_part_bufs(int ring, int nch) { return (ring - 1 + nch - 1) / nch + 2; }
+
+// Shared-memory layout (bytes): [0,256) mbarriers full[ring], empty[ring]; ring x st_bytes; metadata ring x
+// tma_meta_bytes (16-byte multiples); x Kpad x 2; INT4 group sums Kpad/128 floats; tile partials NB x NC x 16 floats;
+// NB arrival counters; x scale 16 bytes.
+template <int F, int NC>
+__host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int kc, int st_bytes) {
+    const int kp = mma_kpad<F>(K);
+    const size_t mb = (size_t)(tma_meta_bytes<F>(kc / 64) + 15) / 16 * 16;
+    const int nb = tma_part_bufs(ring < 2 ? 2 : ring, nch);
+    return 256 + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * 2 +
+           ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * 4 : 0) + (size_t)nb * NC * 16 * 4 + (size_t)nb * 4 + 16;
+}
+
+// Host: choose the stage geometry for this shape within `cap` bytes of shared memory and return the dynamic shared
+// memory size (0 when it cannot be staged). A row is split into NCH equal chunks of KC bytes (a multiple of 64, at most
+// 4096 so that a 16-row stage stays <= 64 KB; INT4 at most 2048, i.e. <= 32 groups of metadata per stage). p.ring on
+// entry is the requested ring depth (>= 2), or 0 for as many stages as fit (2..16; KC then sized for >= 3 stages).
+template <int F, int NC>
+size_t tma_prep(Params& p, size_t cap) {
+    const size_t rowbytes = (size_t)p.nchunk * 16;
+    const int want = p.ring;
+    if (want == 1 || want > kTmaMaxRing) return 0;
+    // everything but the ring and its metadata (partial buffers sized for the deepest ring and one chunk per row)
+    const size_t fixed = tma_smem_bytes<F, NC>(p.K, 0, 1, 64, 0) + (size_t)(kTmaMaxRing + 1) * (NC * 64 + 4);
+    if (fixed >= cap) return 0;
+    // a stage needs at most 16 (KC + 64) + 128 ring bytes and 112 + 2 x 2 x 16 (KC/64 + 3) + 15 metadata bytes
+    const size_t per_stage_cap = (cap - fixed) / (want >= 2 ? want : 3);
+    if (per_stage_cap < 1536 + 17 * 64) return 0;
+    long kc_max = (long)(per_stage_cap - 1536) / 17;
+    if (kc_max > 65536 / 16) kc_max = 65536 / 16;
+    if (F == kINT4 || F == kINT4A) kc_max = kc_max > 2048 ? 2048 : kc_max;
+    kc_max = kc_max / 64 * 64;
+    if (kc_max < 64) return 0;
+    const long need = (long)((rowbytes + 63) / 64 * 64);
+    const long kc0 = need < kc_max ? need : kc_max;
+    const int nch = (int)((rowbytes + kc0 - 1) / kc0);
+    long kc = (long)((rowbytes + nch - 1) / nch);
+    kc = (kc + 63) / 64 * 64;
+    p.kc = (int)kc;
+    p.nch = nch;
+    p.rs = (int)(kc % 128 == 0 ? kc + 64 : kc);
+    p.st_bytes = (16 * p.rs + 127) / 128 * 128;
+    int ring = want;
+    if (ring == 0) {
+        const size_t per_stage = (size_t)p.st_bytes + (size_t)(tma_meta_bytes<F>((int)kc / 64) + 15) / 16 * 16;
+        const size_t fit = (cap - fixed) / per_stage;
+        ring = fit > (size_t)kTmaMaxRing ? kTmaMaxRing : (int)fit;
+        if (ring < 2) return 0;
+    }
+    p.ring = ring;
+    const size_t total = tma_smem_bytes<F, NC>(p.K, ring, nch, p.kc, p.st_bytes);
+    return total <= cap ? total : 0;
+}
+
+// Accumulators of one consumer warp: two chains per unrolled step (BF16: the two k-halves of a step; FP8: even and odd
+// 4-byte words; INT4: even and odd 32-weight quarters), so consecutive mma.sync never wait on each other.
+template <int U>
+struct TmaAcc {
+    float a[U][2][4];
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) a[u][h][0] = a[u][h][1] = a[u][h][2] = a[u][h][3] = 0.f;
+    }
+};
+
+// NU consecutive 64-byte steps (stage-local step sl, global step gs) of rows g and g + 8 through the tensor cores.
+// CHECK: zero the 16-byte chunks beyond the row (only the ragged last step of a BF16/FP8 row needs it).
+// INT4: the per-group fold s (D - 136 sum x) (+ z sum x) goes into acc0/acc1 (row g / row g + 8).
+template <int F, int DEC, int NU, bool CHECK, int U>
+__device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1, const uint8_t* r0p, const uint8_t* r1p,
+                                          const uint16_t* xs, const float* gsum, const uint16_t* sc0,
+                                          const uint16_t* sc1, const uint16_t* zr0, const uint16_t* zr1, int sl, int gs,
+                                          int c, int nchunk) {
+    constexpr int SK = MmaStep<F>::k;
+    uint4 w0[NU], w1[NU];
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+        w0[u] = *reinterpret_cast<const uint4*>(r0p + 64 * (sl + u));
+        w1[u] = *reinterpret_cast<const uint4*>(r1p + 64 * (sl + u));
+        if (CHECK && 4 * (gs + u) + c >= nchunk) w0[u] = w1[u] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    const uint16_t* xb = xs + (size_t)gs * SK + c * (SK / 4);
+    if constexpr (F == kBF16) {
+        uint4 xv[NU];
+#pragma unroll
+        for (int u = 0; u < NU; ++u) xv[u] = *reinterpret_cast<const uint4*>(xb + u * SK);
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            mma_bf16(A.a[u][0], w0[u].x, w1[u].x, w0[u].y, w1[u].y, xv[u].x, xv[u].y);
+            mma_bf16(A.a[u][1], w0[u].z, w1[u].z, w0[u].w, w1[u].w, xv[u].z, xv[u].w);
+        }
+    } else if constexpr (F == kFP8) {
+        uint4 xa[NU], xc[NU];
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            xa[u] = *reinterpret_cast<const uint4*>(xb + u * SK);
+            xc[u] = *reinterpret_cast<const uint4*>(xb + u * SK + 8);
+        }
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            const uint32_t xv[8] = {xa[u].x, xa[u].y, xa[u].z, xa[u].w, xc[u].x, xc[u].y, xc[u].z, xc[u].w};
+#pragma unroll
+            for (int t4 = 0; t4 < 4; ++t4) {
+                const uint32_t a = (&w0[u].x)[t4], b = (&w1[u].x)[t4];
+                const bool alu = (DEC == 1) || (DEC == 2 && t4 >= 2);
+                float (&d)[4] = A.a[u][DEC == 2 ? (alu ? 1 : 0) : (t4 & 1)];
+                if (alu)
+                    mma_f16(d, e4m3_pair02_div256(a), e4m3_pair02_div256(b), e4m3_pair13_div256(a),
+                            e4m3_pair13_div256(b), xv[2 * t4], xv[2 * t4 + 1]);
+                else
+                    mma_f16(d, e4m3x2_to_f16x2(a & 0xFFFFu), e4m3x2_to_f16x2(b & 0xFFFFu), e4m3x2_to_f16x2(a >> 16),
+                            e4m3x2_to_f16x2(b >> 16), xv[2 * t4], xv[2 * t4 + 1]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 xq = *reinterpret_cast<const uint4*>(xb + u * SK + 8 * q);
+                const uint32_t a = (&w0[u].x)[q], b = (&w1[u].x)[q];
+                mma_bf16(d[q & 1], nib_pair_bf16(a, 0), nib_pair_bf16(b, 0), nib_pair_bf16(a, 1), nib_pair_bf16(b, 1),
+                         xq.x, xq.y);
+                mma_bf16(d[q & 1], nib_pair_bf16(a, 2), nib_pair_bf16(b, 2), nib_pair_bf16(a, 3), nib_pair_bf16(b, 3),
+                         xq.z, xq.w);
+            }
+            // every lane holds rows g and g + 8 (all 8 MMA columns carry the same x), so all lanes fold alike
+            const float sx = gsum[gs + u];
+            const float off = -136.f * sx;
+            const float r0 = d[0][0] + d[1][0] + off, r1 = d[0][2] + d[1][2] + off;
+            if constexpr (F == kINT4) {
+                acc0 = fmaf(__half2float(__ushort_as_half(sc0[sl + u])), r0, acc0);
+                acc1 = fmaf(__half2float(__ushort_as_half(sc1[sl + u])), r1, acc1);
+            } else {
+                acc0 = fmaf(bf_lo(sc0[sl + u]), r0, fmaf(bf_lo(zr0[sl + u]), sx, acc0));
+                acc1 = fmaf(bf_lo(sc1[sl + u]), r1, fmaf(bf_lo(zr1[sl + u]), sx, acc1));
+            }
+        }
+    }
+}
+
+template <int F, int NC, int U, int DEC = 0>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params p) {
+    constexpr bool I4 = (F == kINT4 || F == kINT4A);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int KC = p.kc, NCH = p.nch, RS = p.rs;
+    const int ST = p.ring;                                    // 2..16 stages (the host checks)
+    const int NB = tma_part_bufs(ST, NCH);
+    const int CS = KC >> 6, MR = tma_meta_row(CS);
+    const int MB = (tma_meta_bytes<F>(CS) + 15) & ~15;
+    const int S = (p.nchunk + 3) >> 2;                        // 64-byte steps per row
+    const int SF = p.nchunk >> 2;                             // steps whose four 16-byte chunks are all in the row
+    const size_t rowbytes = (size_t)p.nchunk * 16;
+    const int Kp = mma_kpad<F>(p.K);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + ST;
+    uint8_t* ring = smem + 256;
+    uint8_t* meta = ring + (size_t)ST * p.st_bytes;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(meta + (size_t)ST * MB);
+    float* gsum = reinterpret_cast<float*>(xs + Kp);
+    float* part = gsum + (I4 ? Kp / 128 : 0);
+    int* cnt = reinterpret_cast<int*>(part + (size_t)NB * NC * 16);
+    float* xscale = reinterpret_cast<float*>(cnt + NB);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rb = (int)((long long)blockIdx.x * p.N / gridDim.x);
+    const int re = (int)((long long)(blockIdx.x + 1) * p.N / gridDim.x);
+    const int T = (re - rb + 15) >> 4;
+    const int nst = T * NCH;                                  // stages this CTA streams
+
+    if (tid == 0) {
+        // full: the producer's expect_tx arrival, 32 lanes' cp.async arrivals and its closing arrival
+        for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 34); mbar_init(&empty[s], NC); }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (tid < NB) cnt[tid] = 0;
+    __syncthreads();
+
+    if (warp == NC) {
+        // ------------------------------------------------------------ producer warp
+        const long long NG = (long long)p.N * p.groups;
+        int s = 0, t = 0, j = 0;
+        uint32_t ph = 0;                                      // parity of the slot's previous release
+        for (int i = 0; i < nst; ++i) {
+            const int r0 = rb + 16 * t;
+            const int nrows = re - r0 < 16 ? re - r0 : 16;
+            const bool last = j == NCH - 1;
+            const int nsteps = last ? S - j * CS : CS;
+            const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
+            if (lane == 0) {
+                if (i >= ST) mbar_wait(&empty[s], ph, 1);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before the copies
+                mbar_arrive_expect_tx(&full[s], (uint32_t)nrows * bytes);
+            }
+            __syncwarp();                                     // the slot is free and its byte count announced
+            if (lane < nrows)
+                bulk_copy_g2s(ring + (size_t)s * p.st_bytes + (size_t)lane * RS,
+                              p.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s]);
+            uint8_t* ms = meta + (size_t)s * MB;
+            if (last) {
+                if constexpr (F == kFP8) {
+                    if (lane < nrows)
+                        cp_async4(reinterpret_cast<float*>(ms) + lane, reinterpret_cast<const float*>(p.s) + r0 + lane);
+                }
+                if (p.bias) {
+                    const int nw = u16_words(reinterpret_cast<const uint16_t*>(p.bias), r0, nrows);
+                    if (lane < nw)
+                        u16_word_copy(reinterpret_cast<uint16_t*>(ms + 64), reinterpret_cast<const uint16_t*>(p.bias),
+                                      p.N, r0, lane);
+                }
+            }
+            if constexpr (I4) {
+                // rows x words of this stage's scale (and zero) runs, spread over the lanes; every row copies the
+                // (nsteps + 2) / 2 words that hold its run for either element parity
+                uint16_t* msc = reinterpret_cast<uint16_t*>(ms + 112);
+                const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s);
+                const uint16_t* za = reinterpret_cast<const uint16_t*>(p.z);
+                const int wpr = (nsteps + 2) >> 1;
+                int rr = lane / wpr, k = lane - rr * wpr;
+                const int drr = 32 / wpr, dk = 32 - drr * wpr;
+                while (rr < nrows) {
+                    const long long e0 = (long long)(r0 + rr) * p.groups + (long long)j * CS;
+                    if (k < u16_words(sa, e0, nsteps)) u16_word_copy(msc + rr * MR, sa, NG, e0, k);
+                    if constexpr (F == kINT4A)
+                        if (k < u16_words(za, e0, nsteps)) u16_word_copy(msc + (16 + rr) * MR, za, NG, e0, k);
+                    rr += drr;
+                    k += dk;
+                    if (k >= wpr) { k -= wpr; ++rr; }
+                }
+            }
+            cp_async_arrive(&full[s]);
+            __syncwarp();                                     // plain-load halves stored before the closing arrival
+            if (lane == 0) mbar_arrive(&full[s]);
+            if (++s == ST) { s = 0; if (i >= ST) ph ^= 1u; }    // waits from round 1 on: parity 0, 1, 0, ...
+            if (++j == NCH) { j = 0; ++t; }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumer warps
+    grid_dependency_wait();
+    stage_x<F, DEC>(p, xs, gsum, xscale, part, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+    consumer_barrier(1, NC * 32);
+    if (tid == 0) launch_dependents();
+
+    const int g = lane >> 2, c = lane & 3;
+    // accumulator chains scaled by 1 (cvt decode, BF16) or 256 (FP8 ALU decode holds value / 256)
+    constexpr float f0 = (F == kFP8 && DEC == 1) ? 256.f : 1.f;
+    constexpr float f1 = (F == kFP8 && DEC >= 1) ? 256.f : 1.f;
+    TmaAcc<U> A;
+    A.zero();
+    float acc0 = 0.f, acc1 = 0.f;
+    const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s);
+    const uint16_t* za = reinterpret_cast<const uint16_t*>(p.z);
+    int s = 0, t = 0, j = 0, b = 0;
+    uint32_t ph = 0;
+    for (int i = 0; i < nst; ++i) {
+        const int r0 = rb + 16 * t;
+        const bool last = j == NCH - 1;
+        mbar_wait(&full[s], ph, 2);
+        const int nsteps = last ? S - j * CS : CS;
+        const int sa0 = warp * nsteps / NC, sb0 = (warp + 1) * nsteps / NC;
+        const uint8_t* st = ring + (size_t)s * p.st_bytes;
+        const uint8_t* ms = meta + (size_t)s * MB;
+        const uint8_t* r0p = st + (size_t)g * RS + 16 * c;
+        const uint8_t* r1p = r0p + (size_t)8 * RS;
+        // INT4: this lane's scale (and zero) runs of rows g and g + 8, element parity folded in
+        const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(ms + 112) + g * MR;
+        const uint16_t* sc1 = sc0 + 8 * MR;
+        const uint16_t* zr0 = sc0 + 16 * MR;
+        const uint16_t* zr1 = sc1 + 16 * MR;
+        if constexpr (I4) {
+            const long long e0 = (long long)(r0 + g) * p.groups + (long long)j * CS;
+            const long long e1 = e0 + 8LL * p.groups;
+            sc0 += u16_parity(sa + e0);
+            sc1 += u16_parity(sa + e1);
+            if constexpr (F == kINT4A) {
+                zr0 += u16_parity(za + e0);
+                zr1 += u16_parity(za + e1);
+            }
+        }
+        const int gb = j * CS;                                // global step of stage-local step 0
+        const int sfull = SF - gb < sb0 ? SF - gb : sb0;      // steps below sfull are whole
+        int sl = sa0;
+        for (; sl + U <= sfull; sl += U)
+            tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk);
+        for (; sl < sfull; ++sl)
+            tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk);
+        for (; sl < sb0; ++sl)                                // the ragged last step of the row
+            tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk);
+
+        if (last) {
+            // tile end: this warp's partial sums of rows g, g + 8 -> buffer b; the last warp in adds them in order
+            float s0, s1;
+            if constexpr (I4) {
+                s0 = acc0; s1 = acc1;
+                acc0 = acc1 = 0.f;
+            } else {
+                s0 = 0.f; s1 = 0.f;
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    s0 += A.a[u][0][0] * f0 + A.a[u][1][0] * f1;
+                    s1 += A.a[u][0][2] * f0 + A.a[u][1][2] * f1;
+                }
+                A.zero();
+            }
+            float* buf = part + (size_t)b * NC * 16;
+            if (c == 0) { buf[warp * 16 + g] = s0; buf[warp * 16 + g + 8] = s1; }
+            __syncwarp();
+            int prior = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                prior = atomicAdd(&cnt[b], 1);
+            }
+            prior = __shfl_sync(0xffffffffu, prior, 0);
+            if (prior == NC - 1) {                            // last arriver: all NC partials are in
+                __threadfence_block();
+                if (lane < 16) {
+                    float total = 0.f;
+#pragma unroll
+                    for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
+                    const int row = r0 + lane;
+                    if (row < re) {
+                        float out = total;
+                        if constexpr (F == kFP8)
+                            out = ldexpf(out * reinterpret_cast<const float*>(ms)[lane], __float_as_int(xscale[0]));
+                        if (p.bias) {
+                            const uint16_t* bw = reinterpret_cast<const uint16_t*>(ms + 64);
+                            out += __uint_as_float((uint32_t)bw[u16_parity(p.bias + r0) + lane] << 16);
+                        }
+                        p.y[row] = __float2bfloat16_rn(out);
+                    }
+                }
+                if (lane == 0) cnt[b] = 0;
+                __syncwarp();
+            }
+            if (++b == NB) b = 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == ST) { s = 0; ph ^= 1u; }
+        if (++j == NCH) { j = 0; ++t; }
+    }
+}
+
+}  // namespace pb2

@@ -1,0 +1,53 @@
+// TMA-fed tensor-core kernel instances (gemv_tma.cuh). math 5 = default weight decode of the format, and for FP8
+// math 6 = ALU bit decode, math 7 = split cvt/ALU decode. Tuple knobs: W = consumer warps (plus one producer warp),
+// U = 64-byte steps per consumer iteration. The ring depth and the shared-memory share are launch options.
+#include "gemv_launch.cuh"
+#include "gemv_tma.cuh"
+
+namespace pb2 {
+
+#define PB2_TMA(F, NC, U, H, M, DEC) {0, U, NC, 0, H, M, &gemv_tma_kernel<F, NC, U, DEC>, nullptr, &tma_prep<F, NC>},
+#define PB2_TMA_H(F, NC, U, M, DEC) PB2_TMA(F, NC, U, 0, M, DEC) PB2_TMA(F, NC, U, 1, M, DEC)
+#define PB2_TMA_U(F, NC, M, DEC) PB2_TMA_H(F, NC, 2, M, DEC) PB2_TMA_H(F, NC, 4, M, DEC)
+#define PB2_TMA_NC(F, M, DEC) PB2_TMA_U(F, 4, M, DEC) PB2_TMA_U(F, 8, M, DEC) PB2_TMA_U(F, 16, M, DEC)
+static const Variant kBf16[] = {PB2_TMA_NC(kBF16, 5, 0)};
+static const Variant kFp8[] = {PB2_TMA_NC(kFP8, 5, 0)};
+static const Variant kFp8Alu[] = {PB2_TMA_NC(kFP8, 6, 1)};
+static const Variant kFp8Split[] = {PB2_TMA_NC(kFP8, 7, 2)};
+static const Variant kInt4[] = {PB2_TMA_NC(kINT4, 5, 0)};
+static const Variant kInt4a[] = {PB2_TMA_NC(kINT4A, 5, 0)};
+#undef PB2_TMA_NC
+#undef PB2_TMA_U
+#undef PB2_TMA_H
+#undef PB2_TMA
+
+#define PB2_N(t) (int)(sizeof(t) / sizeof(t[0]))
+const Variant* tma_instances(int fmt, int math, int* n) {
+    *n = 0;
+    if (fmt == kFP8) {
+        if (math == 5) { *n = PB2_N(kFp8); return kFp8; }
+        if (math == 6) { *n = PB2_N(kFp8Alu); return kFp8Alu; }
+        if (math == 7) { *n = PB2_N(kFp8Split); return kFp8Split; }
+        return nullptr;
+    }
+    if (math != 5) return nullptr;
+    switch (fmt) {
+        case kBF16: *n = PB2_N(kBf16); return kBf16;
+        case kINT4: *n = PB2_N(kInt4); return kInt4;
+        case kINT4A: *n = PB2_N(kInt4a); return kInt4a;
+        default: return nullptr;
+    }
+}
+#undef PB2_N
+
+// Error word of the bounded mbarrier waits (1 producer gave up on a free stage, 2 consumer gave up on a full stage).
+int tma_device_error(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_tma_error, sizeof(int)) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
+    if (clear && v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_tma_error, &zero, sizeof(int));
+    }
+    return v;
+}
+}  // namespace pb2

@@ -312,10 +312,14 @@ def test_dependent_chain_in_cuda_graph(L, kind):
 MMA_CFGS = [(1, 4), (2, 8), (4, 8), (2, 16), (4, 16)]      # (U, W) of the tensor-core kernel (math 2)
 
 
-@pytest.mark.parametrize("kind", KINDS)
-def test_mma_kernel_awkward_and_real_shapes(L, kind):
+MMA_MATHS = [("bf16", 2), ("fp8", 2), ("fp8", 3), ("fp8", 4), ("int4", 2), ("int4_asym", 2)]
+
+
+@pytest.mark.parametrize("kind,math", MMA_MATHS)
+def test_mma_kernel_awkward_and_real_shapes(L, kind, math):
     """The tensor-core kernel (gemv_mma.cuh) through paia_gemv_launch_ex: awkward shapes (partial 64-byte steps,
-    partial 16-row tiles, fewer rows than CTAs), real decode shapes, with and without bias, PDL on and off."""
+    partial 16-row tiles, fewer rows than CTAs), real decode shapes, with and without bias, PDL on and off; for FP8
+    every weight decoder (math 2: cvt, 3: ALU bit decode, 4: split)."""
     shapes = AWKWARD[kind] + [(4096, 4096), (6144, 4096), (3584, 18944), (512, 3584)]
     for (N, K) in shapes:
         ops = make(kind, N, K, seed=N * 3 + K, with_bias=True)
@@ -323,7 +327,7 @@ def test_mma_kernel_awkward_and_real_shapes(L, kind):
         for i, (U, Wn) in enumerate(MMA_CFGS):
             for cps in (0, 1):
                 ops.nan_fill()
-                rc = ops.call_ex(L, 1, U, Wn, 2, (i + cps) % 2, 0, cps, with_bias=bool(cps))
+                rc = ops.call_ex(L, 1, U, Wn, math, (i + cps) % 2, 0, cps, with_bias=bool(cps))
                 assert rc == 0, (kind, N, K, U, Wn, cps, rc)
                 torch.cuda.synchronize()
                 check(ops, bits(ops.y), refb if cps else ref, f"mma {kind} {N}x{K} U{U} W{Wn} cps{cps}")
@@ -341,7 +345,113 @@ def test_fp8_mma_activation_ranges(L, scale):
     ops.x = xf.to(torch.bfloat16)
     ref = ops.oracle()[0]
     for U, Wn in MMA_CFGS:
+        for math in (2, 3, 4):
+            ops.nan_fill()
+            assert ops.call_ex(L, 1, U, Wn, math, 1, 0, 0) == 0
+            torch.cuda.synchronize()
+            check(ops, bits(ops.y), ref, f"fp8 mma{math} x*{scale}")
+
+
+@pytest.mark.parametrize("math", [2, 3, 4])
+def test_fp8_mma_every_code_exact(L, math):
+    """Every finite e4m3 code (subnormal codes included, which the ALU decode turns into f16 subnormals) through the
+    tensor-core FP8 kernel: row c holds code c once, x = 1, scale = 1, so y is the code's value exactly."""
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.uint8)
+    N, K = len(codes), 64
+    q = np.zeros((N, K), np.uint8)
+    q[np.arange(N), np.arange(N) % K] = codes
+    ops = make("fp8", N, K)
+    ops.W = torch.from_numpy(q).cuda()
+    ops.s = torch.ones(N, device="cuda")
+    ops.x = torch.ones(K, dtype=torch.bfloat16, device="cuda")
+    want = O.bf16_to_f32(O.f32_to_bf16(O.e4m3_decode(codes)))
+    for U, Wn in MMA_CFGS:
         ops.nan_fill()
-        assert ops.call_ex(L, 1, U, Wn, 2, 1, 0, 0) == 0
+        assert ops.call_ex(L, 1, U, Wn, math, 1, 0, 0) == 0
         torch.cuda.synchronize()
-        check(ops, bits(ops.y), ref, f"fp8 mma x*{scale}")
+        assert np.array_equal(O.bf16_to_f32(bits(ops.y)), want), (math, U, Wn)
+
+
+# (ring stages (0 = as many as fit), U, NC consumer warps, shared-memory share) of the TMA-fed kernel, math 5-7
+TMA_CFGS = [(2, 2, 4, 1), (3, 4, 8, 1), (0, 2, 8, 2), (0, 4, 4, 1), (16, 2, 8, 1), (0, 2, 16, 1)]
+
+
+TMA_MATHS = [("bf16", 5), ("fp8", 5), ("fp8", 6), ("fp8", 7), ("int4", 5), ("int4_asym", 5)]
+
+
+@pytest.mark.parametrize("kind,math", TMA_MATHS)
+def test_tma_kernel_awkward_and_real_shapes(L, kind, math):
+    """The TMA-fed tensor-core kernel (gemv_tma.cuh) through paia_gemv_launch_ex: awkward shapes (ragged last chunk of
+    a row, partial 16-row tiles, fewer rows than CTAs, rows split into several stages), real decode shapes, with and
+    without bias, PDL on and off, one and two CTAs per SM; no bounded wait may give up."""
+    shapes = AWKWARD[kind] + [(4096, 4096), (6144, 4096), (3584, 18944), (512, 3584), (37, 28672)]
+    L.device_error(1)
+    for (N, K) in shapes:
+        ops = make(kind, N, K, seed=N * 5 + K, with_bias=True)
+        ref, refb = ops.oracle()[0], ops.oracle(with_bias=True)[0]
+        for i, (ring, U, NC, share) in enumerate(TMA_CFGS):
+            if ring == 16 and K > 4096:
+                continue                                       # 16 stages of long rows do not fit
+            for cps in (0, 1):
+                ops.nan_fill()
+                rc = ops.call_ex(L, ring, U, NC, math, (i + cps) % 2, share, cps, with_bias=bool(cps))
+                assert rc == 0, (kind, N, K, ring, U, NC, share, cps, rc)
+                torch.cuda.synchronize()
+                check(ops, bits(ops.y), refb if cps else ref,
+                      f"tma {kind} {N}x{K} ring{ring} U{U} NC{NC} share{share} cps{cps}")
+    assert L.device_error(1) == 0
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp8", "int4", "int4_asym"])
+def test_tma_kernel_long_rows(L, kind):
+    """Rows longer than a stage (K up to the C ABI's maximum of 98304): each row is streamed as several chunks, and the
+    ring shrinks to fit next to x in shared memory."""
+    for K in (65536, 98304):
+        N = 40
+        ops = make(kind, N, K, seed=K + 1, with_bias=True)
+        refb = ops.oracle(with_bias=True)[0]
+        for ring, U, NC, share in ((2, 2, 4, 1), (0, 4, 8, 1), (0, 2, 8, 2)):
+            ops.nan_fill()
+            rc = ops.call_ex(L, ring, U, NC, 5, 1, share, 0, with_bias=True)
+            if share == 2 and 2 * K > 115200:
+                assert rc == -2                                # x alone (2 K bytes) exceeds half an SM
+                continue
+            assert rc == 0, (kind, K, ring, share, rc)
+            torch.cuda.synchronize()
+            check(ops, bits(ops.y), refb, f"tma {kind} K={K} ring{ring} share{share}")
+    assert L.device_error(1) == 0
+
+
+@pytest.mark.parametrize("scale", [1e-30, 1.0, 1e30])
+def test_fp8_tma_activation_ranges(L, scale):
+    N, K = 300, 4096
+    ops = make("fp8", N, K, seed=6)
+    xf = ops.x.float() * scale
+    if scale == 1e30:
+        xf[17] = 3e38
+    ops.x = xf.to(torch.bfloat16)
+    ref = ops.oracle()[0]
+    for ring, U, NC, share in TMA_CFGS:
+        for math in (5, 6, 7):
+            ops.nan_fill()
+            assert ops.call_ex(L, ring, U, NC, math, 1, share, 0) == 0
+            torch.cuda.synchronize()
+            check(ops, bits(ops.y), ref, f"fp8 tma{math} x*{scale}")
+
+
+@pytest.mark.parametrize("math", [5, 6, 7])
+def test_fp8_tma_every_code_exact(L, math):
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.uint8)
+    N, K = len(codes), 64
+    q = np.zeros((N, K), np.uint8)
+    q[np.arange(N), np.arange(N) % K] = codes
+    ops = make("fp8", N, K)
+    ops.W = torch.from_numpy(q).cuda()
+    ops.s = torch.ones(N, device="cuda")
+    ops.x = torch.ones(K, dtype=torch.bfloat16, device="cuda")
+    want = O.bf16_to_f32(O.f32_to_bf16(O.e4m3_decode(codes)))
+    for ring, U, NC, share in TMA_CFGS:
+        ops.nan_fill()
+        assert ops.call_ex(L, ring, U, NC, math, 1, share, 0) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(O.bf16_to_f32(bits(ops.y)), want), (math, ring, U, NC, share)

@@ -171,8 +171,10 @@ MMA_STEP_K = {"bf16": 32, "fp8": 64, "int4": 128, "int4_asym": 128}
 
 
 def replay_mma(fmt, N, K, W, U, sms=148, per_sm=2):
-    """Replay of gemv_mma_kernel: CTA rows, 16-row tiles, 64-byte steps split over warps, lane (g, c) loading the
-    16-byte chunk q = 4 s + c of rows g and g + 8, x reads at s * SK + c * SK/4 .. + SK/4 (padded to Kp)."""
+    """Replay of gemv_mma_kernel (stream-K inside the CTA): CTA rows [rb, re) cut into 16-row tiles, the T x S
+    (tile, step) space split into NW equal warp ranges, iterations of <= U steps that never cross a tile, loads of
+    chunk q = 4 s + c of rows g and g + 8 (clamped to the CTA's last row), whole tiles stored by their warp, and the
+    straddling tiles finished by the cleanup pass from the partial-sum slots."""
     SK = MMA_STEP_K[fmt]
     nchunk = ROWBYTES[fmt](K) // 16
     Kp = (K + SK - 1) // SK * SK
@@ -183,40 +185,79 @@ def replay_mma(fmt, N, K, W, U, sms=148, per_sm=2):
     stores = np.zeros(N, dtype=np.int32)
     for blk in range(G):
         rb, re = blk * N // G, (blk + 1) * N // G
-        ntiles = (re - rb + 15) >> 4
-        arrivals = {}
+        T = (re - rb + 15) >> 4
+        total = T * S
+        contrib = {}                                          # (tile, row) -> steps summed into it
+        slots = {}
         for warp in range(W):
-            sb, se = S * warp // W, S * (warp + 1) // W
-            nbatch = (se - sb + U - 1) // U if (se - sb) > U else 1
-            nit = ntiles * nbatch
-            seq, lds = iteration_order(nit, nbatch)
-            assert [(t, b) for t, b, _ in seq] == [(i // nbatch, i % nbatch) for i in range(nit)]
-            for t, b, _ in seq:
-                for u in range(U):
-                    s = sb + b * U + u
-                    if s >= se:
-                        continue
-                    assert s * SK + SK <= Kp                      # x reads (all lanes c) inside the padded x
-                    if fmt.startswith("int4"):
-                        assert s < Kp // 128                      # gsum index
-                    for g in range(8):
-                        for r in (rb + t * 16 + g, rb + t * 16 + g + 8):
-                            if r >= re:
-                                continue
+            wb, we = total * warp // W, total * (warp + 1) // W
+            first_tile = wb // S if S else 0
+
+            def it_n(cur):
+                return min(S - cur % S, U, we - cur)
+
+            cur, seg_s = wb, -1
+            prev_next = None
+            while cur < we:
+                t, s, n = cur // S, cur % S, it_n(cur)
+                assert 1 <= n <= U and s + n <= S
+                if prev_next is not None:
+                    assert prev_next == cur                   # the prefetched iteration is the next computed one
+                for g in range(8):
+                    for r in (rb + t * 16 + g, rb + t * 16 + g + 8):
+                        rc = min(r, re - 1)
+                        assert rb <= rc < re
+                        for u in range(n):
+                            assert (s + u) * SK + SK <= Kp        # x reads inside the padded x
+                            if fmt.startswith("int4"):
+                                assert s + u < Kp // 128          # gsum / scale group index
                             for c in range(4):
-                                q = 4 * s + c
+                                q = 4 * (s + u) + c
                                 if q < nchunk:
-                                    loads[r, q] += 1
-                if b == nbatch - 1:
-                    arrivals[t] = arrivals.get(t, 0) + 1
-                    if warp == 0:
-                        for lane in range(16):
-                            r = rb + t * 16 + lane
+                                    assert 0 <= rc * nchunk + q < N * nchunk
+                                    if r < re:
+                                        loads[r, q] += 1
+                if seg_s < 0:
+                    seg_s = s
+                if s + n == S or cur + n == we:
+                    whole = seg_s == 0 and s + n == S
+                    for g in range(16):
+                        r = rb + t * 16 + g
+                        if whole:
                             if r < re:
                                 stores[r] += 1
-        assert all(v == W for v in arrivals.values()) and len(arrivals) == ntiles
+                        else:
+                            slot = (warp, 0 if t == first_tile else 1)
+                            assert (slot, g) not in slots, "a partial slot written twice"
+                            slots[(slot, g)] = t
+                    seg_s = -1
+                prev_next = cur + n
+                cur += n
+        # cleanup pass: straddling tiles, summed from the slots of the warps that touched them
+        for w in range(1, W):
+            bw = total * w // W
+            if bw % S == 0 or bw >= total:
+                continue
+            t = bw // S
+            if total * (w - 1) // W > t * S:
+                continue
+            for r in range(16):
+                used = 0
+                for v2 in range(w - 1, W):
+                    vb, ve = total * v2 // W, total * (v2 + 1) // W
+                    if vb >= (t + 1) * S:
+                        break
+                    if ve <= t * S or vb >= ve:
+                        continue
+                    slot = (v2, 0 if t == vb // S else 1)
+                    assert slots.get((slot, r)) == t, (blk, w, t, v2, slot)
+                    used += 1
+                assert used >= 2
+                row = rb + t * 16 + r
+                if row < re:
+                    stores[row] += 1
     assert np.all(loads == 1), f"{fmt} N={N} K={K} W={W} U={U}: loads min {loads.min()} max {loads.max()}"
-    assert np.all(stores == 1), f"{fmt} N={N} K={K} W={W} U={U}: stores"
+    assert np.all(stores == 1), f"{fmt} N={N} K={K} W={W} U={U}: stores min {stores.min()} max {stores.max()}"
 
 
 @pytest.mark.parametrize("fmt", list(SHAPES))
@@ -225,3 +266,233 @@ def test_mma_mapping_exactly_once(fmt):
     combos = list(itertools.product(SHAPES[fmt], (4, 8, 16), (1, 2, 4), (1, 2, 3, 4)))
     for (N, K), W, U, per_sm in rnd.sample(combos, 60):
         replay_mma(fmt, N, K, W, U, sms=rnd.choice((148, 7, 1)), per_sm=per_sm)
+
+
+# ------------------------------------------------------------------ TMA-fed tensor-core kernel (gemv_tma.cuh)
+
+SMEM_CAP = 232448                                             # B200 opt-in shared memory per block
+SM_SMEM = 232448                                              # per SM, less one CTA's reservation
+
+
+def share_cap(share):
+    return min(SMEM_CAP, SM_SMEM // share - (1024 if share > 1 else 0))
+
+
+def tma_meta_row(cs):
+    return (cs + 3) & ~1
+
+
+def tma_meta_bytes(fmt, cs):
+    i4 = 16 * tma_meta_row(cs) * 2 * (2 if fmt == "int4_asym" else 1) if fmt.startswith("int4") else 0
+    return (112 + i4 + 15) // 16 * 16
+
+
+def tma_part_bufs(ring, nch):
+    return (ring - 1 + nch - 1) // nch + 2
+
+
+def tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes):
+    SK = MMA_STEP_K[fmt]
+    kp = (K + SK - 1) // SK * SK
+    nb = tma_part_bufs(max(ring, 2), nch)
+    return (256 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * 2
+            + (kp // 128 * 4 if fmt.startswith("int4") else 0) + nb * NC * 16 * 4 + nb * 4 + 16)
+
+
+def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP):
+    """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged."""
+    rowbytes = ROWBYTES[fmt](K)
+    if ring == 1 or ring > 16:
+        return None
+    fixed = tma_smem_bytes(fmt, NC, K, 0, 1, 64, 0) + 17 * (NC * 64 + 4)
+    if fixed >= cap:
+        return None
+    per_stage_cap = (cap - fixed) // (ring if ring >= 2 else 3)
+    if per_stage_cap < 1536 + 17 * 64:
+        return None
+    kc_max = min((per_stage_cap - 1536) // 17, 65536 // 16)
+    if fmt.startswith("int4"):
+        kc_max = min(kc_max, 2048)
+    kc_max = kc_max // 64 * 64
+    if kc_max < 64:
+        return None
+    need = (rowbytes + 63) // 64 * 64
+    kc0 = min(need, kc_max)
+    nch = (rowbytes + kc0 - 1) // kc0
+    kc = ((rowbytes + nch - 1) // nch + 63) // 64 * 64
+    rs = kc + 64 if kc % 128 == 0 else kc
+    st_bytes = (16 * rs + 127) // 128 * 128
+    if ring == 0:
+        ring = min(16, (cap - fixed) // (st_bytes + tma_meta_bytes(fmt, kc // 64)))
+        if ring < 2:
+            return None
+    total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes)
+    return (kc, nch, rs, st_bytes, ring, total) if total <= cap else None
+
+
+def meta_copy_u16(mod, T, e0, n, slot):
+    """Mirror of u16_words / u16_word_copy for a 2-byte array at byte address `mod` (mod 4) with T elements: every word
+    copied with cp.async lies inside the array, partial words are read half by half inside it, the copy fits its
+    shared-memory slot of `slot` halves, and every element of [e0, e0 + n) lands at parity + (e - e0)."""
+    b = mod + 2 * e0
+    nw = ((b + 2 * n - 1) >> 2) - (b >> 2) + 1
+    assert 1 <= nw <= 32 and 2 * nw <= slot
+    lo, hi = mod, mod + 2 * T
+    got = {}
+    for k in range(nw):
+        w = (b & ~3) + 4 * k
+        halves = [w, w + 2] if (w >= lo and w + 4 <= hi) else [h for h in (w, w + 2) if h >= lo and h + 2 <= hi]
+        for h in halves:
+            assert lo <= h and h + 2 <= hi
+            got[2 * k + (h - w) // 2] = (h - mod) // 2                # smem half index -> element
+    par = (b >> 1) & 1
+    for e in range(e0, e0 + n):
+        assert got.get(par + e - e0) == e, (mod, T, e0, n, e)
+
+
+def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
+    """Replay of gemv_tma_kernel: per CTA the producer streams T x NCH stages through a ring of ST stages (one bulk copy
+    per valid row, KC bytes except the ragged last chunk) while the consumers split each stage's 64-byte steps into NC
+    equal ranges of <= U-step iterations. Checks copies in bounds of W and of the stage, every (row, chunk) copied and
+    consumed exactly once, metadata indices (INT4 scales per row and group, FP8 row scales, bias) in range, every
+    output stored once, and that the full/empty mbarrier protocol (metadata one stage behind) always makes progress."""
+    cap = share_cap(share)
+    geo = tma_prep(fmt, NC, K, ring, cap)
+    assert geo is not None, (fmt, K, NC, ring, share)
+    KC, NCH, RS, ST_BYTES, ST, smem = geo
+    assert smem <= cap and KC % 64 == 0 and RS % 16 == 0 and ST_BYTES % 128 == 0 and 2 <= ST <= 16
+    assert 16 * RS <= ST_BYTES
+    CS = KC // 64
+    if fmt.startswith("int4"):
+        assert CS <= 32                                       # 2 x 16 metadata words per producer lane pair
+    SK = MMA_STEP_K[fmt]
+    rowbytes = ROWBYTES[fmt](K)
+    nchunk = rowbytes // 16
+    S = (nchunk + 3) // 4
+    Kp = (K + SK - 1) // SK * SK
+    groups = K // 128
+    assert NCH * KC >= rowbytes and (NCH - 1) * KC < rowbytes
+    G = grid(N, sms, per_sm)
+    copied = np.zeros((N, nchunk), dtype=np.int32)
+    consumed = np.zeros((N, nchunk), dtype=np.int32)
+    stores = np.zeros(N, dtype=np.int32)
+    for blk in range(G):
+        rb, re = blk * N // G, (blk + 1) * N // G
+        T = (re - rb + 15) >> 4
+        nst = T * NCH
+        # --- producer: copies and metadata
+        for i in range(nst):
+            t, j = divmod(i, NCH)
+            r0 = rb + 16 * t
+            nrows = min(re - r0, 16)
+            assert 1 <= nrows <= 16
+            nsteps = S - j * CS if j == NCH - 1 else CS
+            assert 1 <= nsteps <= CS
+            nbytes = rowbytes - j * KC if j == NCH - 1 else KC
+            assert 16 <= nbytes <= KC and nbytes % 16 == 0 and j * KC % 16 == 0
+            assert nrows * nbytes < 2 ** 20                       # mbarrier transaction count range
+            for rr in range(nrows):
+                src = (r0 + rr) * rowbytes + j * KC
+                assert 0 <= src and src + nbytes <= N * rowbytes and src % 16 == 0
+                assert rr * RS + nbytes <= ST_BYTES
+                copied[r0 + rr, j * KC // 16: j * KC // 16 + nbytes // 16] += 1
+            if fmt.startswith("int4"):
+                MR = tma_meta_row(CS)
+                for rr in range(nrows):
+                    e0 = (r0 + rr) * groups + j * CS
+                    for mod in (0, 2):                             # array base address 0 or 2 modulo 4
+                        meta_copy_u16(mod, N * groups, e0, nsteps, MR)
+            if j == 0:
+                for lane in range(min(nrows, 32)):
+                    assert 0 <= r0 + lane < N                      # FP8 row scales (4-byte cp.async)
+                for mod in (0, 2):
+                    meta_copy_u16(mod, N, r0, nrows, 18)           # bias words
+        # --- consumers: steps of each stage, loads inside the stage, x inside Kp
+        for i in range(nst):
+            t, j = divmod(i, NCH)
+            r0 = rb + 16 * t
+            nsteps = S - j * CS if j == NCH - 1 else CS
+            covered = np.zeros(nsteps, dtype=np.int32)
+            rend = min(r0 + 16, re)
+            assert (8 + 7) * RS + 64 * (nsteps - 1) + 16 * 3 + 16 <= ST_BYTES   # rows g, g+8, last step, lane c=3
+            assert ((j * CS + nsteps) * SK) <= Kp                               # x reads inside the padded x
+            if fmt.startswith("int4"):
+                assert j * CS + nsteps <= Kp // 128 and nsteps <= CS            # gsum and metadata indices
+            for warp in range(NC):
+                sa, sb = warp * nsteps // NC, (warp + 1) * nsteps // NC
+                its = list(range(sa, sb, U))
+                assert all(1 <= min(sb - sl, U) <= U for sl in its)
+                covered[sa:sb] += 1
+                q0, q1 = 4 * (j * CS + sa), min(4 * (j * CS + sb), nchunk)
+                if q1 > q0:
+                    consumed[r0:rend, q0:q1] += 1
+            assert np.all(covered == 1)
+            if j == NCH - 1:
+                for g in range(16):
+                    if r0 + g < re:
+                        stores[r0 + g] += 1
+        # --- mbarrier protocol: the producer may fill stage i once stage i - ring is released by all NC warps; a
+        # stage is readable once filled (copies and metadata complete on its full barrier). Consumers run at most
+        # ring - 1 stages ahead of the slowest warp, so the tile-partial buffers in use stay below NB.
+        NB = tma_part_bufs(ST, NCH)
+        assert (ST - 1 + NCH - 1) // NCH + 1 < NB
+        released = [0] * nst
+        issued, consumed_upto, steps = 0, 0, 0
+        while consumed_upto < nst:
+            steps += 1
+            assert steps < 4 * nst + 16, "mbarrier protocol stalled"
+            progressed = False
+            if issued < nst and (issued < ST or released[issued - ST] == NC):
+                issued += 1
+                progressed = True
+            if consumed_upto < issued:
+                released[consumed_upto] = NC
+                consumed_upto += 1
+                progressed = True
+            assert progressed, "deadlock"
+        # producer/consumer mbarrier parities follow the rounds of the ring: wait k of slot s has parity k & 1
+        ph, s = 0, 0
+        for i in range(nst):
+            if i >= ST:
+                assert ph == ((i // ST) - 1) & 1
+            s += 1
+            if s == ST:
+                s = 0
+                if i >= ST:
+                    ph ^= 1
+    assert np.all(copied == 1), f"{fmt} N={N} K={K}: copies min {copied.min()} max {copied.max()}"
+    assert np.all(consumed == 1), f"{fmt} N={N} K={K}: consumed min {consumed.min()} max {consumed.max()}"
+    assert np.all(stores == 1)
+
+
+TMA_SHAPES = dict(SHAPES)
+TMA_SHAPES["bf16"] = SHAPES["bf16"] + [(37, 65536), (20, 98304), (5, 8200)]
+TMA_SHAPES["fp8"] = SHAPES["fp8"] + [(37, 98304), (3, 28672)]
+TMA_SHAPES["int4"] = SHAPES["int4"] + [(9, 98304), (17, 28672)]
+TMA_SHAPES["int4_asym"] = TMA_SHAPES["int4"]
+
+
+@pytest.mark.parametrize("fmt", list(TMA_SHAPES))
+def test_tma_mapping_exactly_once(fmt):
+    rnd = random.Random(2)
+    combos = list(itertools.product(TMA_SHAPES[fmt], (4, 8), (0, 2, 3, 16), (2, 4), (1, 2)))
+    for (N, K), NC, ring, U, share in rnd.sample(combos, 16):
+        if tma_prep(fmt, NC, K, ring, share_cap(share)) is None:
+            assert K > 16384 or ring == 16, (fmt, K, ring, share)   # only long rows or deep rings may not fit
+            continue
+        replay_tma(fmt, N, K, NC, ring, U, sms=rnd.choice((148, 7, 1)), per_sm=rnd.choice((1, 2)), share=share)
+
+
+def test_tma_prep_geometry():
+    # real decode shapes stage with >= ~2 KB per row piece and fit in one CTA per SM
+    for fmt, K in (("bf16", 4096), ("bf16", 8192), ("bf16", 14336), ("fp8", 4096), ("fp8", 8192), ("fp8", 28672),
+                   ("int4", 4096), ("int4", 8192), ("int4", 14336)):
+        for share in (1, 2):
+            geo = tma_prep(fmt, 8, K, 0, share_cap(share))
+            assert geo is not None
+            kc, nch, rs, st_bytes, ring, smem = geo
+            assert kc >= min(ROWBYTES[fmt](K), 1024 // share) and ring >= 2
+            assert smem <= share_cap(share)
+    # the largest K the C ABI accepts still stages (smaller pieces)
+    for fmt in ("bf16", "fp8", "int4"):
+        assert tma_prep(fmt, 8, 98304, 2) is not None
