@@ -57,6 +57,7 @@ struct Params {
     int groups;                    // K / 128 (INT4 formats)
     int kc, nch, rs, st_bytes;     // TMA kernels: bytes per row per stage, stages per tile, smem row stride, stage size
     int ring;                      // TMA kernels: stages in the shared-memory ring
+    int pre;                       // TMA kernels: stages streamed before x is staged (0 = the whole ring)
 };
 
 template <int F> struct Elems;     // weights per 16-byte chunk

@@ -31,6 +31,7 @@ struct LaunchOpts {
     int ring = 0;             // TMA kernels: ring stages (0 = as many as fit, else 2..16)
     int share = 0;            // TMA kernels: size the CTA for 1/share of the SM's shared memory (0 = 1: all of it);
                               // share 2 with one CTA per SM leaves room for the next kernel's CTA under PDL
+    int pre = 0;              // TMA kernels: stages streamed before x is staged (0 = the whole ring)
 };
 
 int sm_count();                                              // current device, cached
@@ -64,12 +65,13 @@ inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaS
         size_t cap = sm_smem_bytes() / share - (share > 1 ? 1024 : 0);
         if (cap > max_dyn_smem()) cap = max_dyn_smem();
         p.ring = o.ring;
+        p.pre = o.pre;
         smem = v.prep(p, cap);
     } else {
         smem = v.smem(p.K);
     }
     if (smem == 0 || smem > max_dyn_smem()) return -2;
-    const int threads = (v.prep ? v.W + 1 : v.W) * 32;
+    const int threads = (v.prep ? v.W + 2 : v.W) * 32;     // TMA kernels: + producer and epilogue warps
     const int occ = max_ctas_per_sm(v.fn, threads, smem);
     if (occ <= 0) return -2;
     // Full occupancy by default: under PDL the next kernel's CTAs take the SM slots that this grid's CTAs free at

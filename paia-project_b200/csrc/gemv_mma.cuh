@@ -61,6 +61,14 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// D += A . B with e4m3 A (16 x 32) and B (32 x 8), fp32 accumulation (exact products).
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
     const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
@@ -77,6 +85,18 @@ __device__ __forceinline__ uint32_t e4m3_pair13_div256(uint32_t w) {
 __device__ __forceinline__ uint32_t nib_pair_bf16(uint32_t w, int j) {   // (128 + n_j, 128 + n_{j+4}) as bf16x2
     return ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
 }
+// D += A . B with u8 A (16 x 32) and s8 B (32 x 8), exact int32 accumulation.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// f16 pairs straight from the nibbles: 0x6400 is 1024.0 and the f16 mantissa has 10 bits, so the low nibble of each
+// half gives 1024 + n and the second nibble 1024 + 16 n, one LOP3 each.
+__device__ __forceinline__ uint32_t nib_lo_f16(uint32_t w) { return (w & 0x000F000Fu) | 0x64006400u; }
+__device__ __forceinline__ uint32_t nib_hi_f16(uint32_t w) { return (w & 0x00F000F0u) | 0x64006400u; }
 
 template <int F>
 __host__ __device__ constexpr int mma_kpad(int K) { return (K + MmaStep<F>::k - 1) / MmaStep<F>::k * MmaStep<F>::k; }
@@ -89,30 +109,123 @@ __host__ __device__ constexpr size_t mma_smem_bytes(int K) {
            (size_t)2 * NW * 16 * 4 + 16;
 }
 
+// Visit the 16-byte blocks i = tid + k nthr < n (k = 0, 1, ...) of x with four blocks' loads in flight per thread
+// (one dependent memory round per four blocks instead of one per block); blocks at or past K / 8 read as zeros.
+// CACHE 1 keeps the first round's four blocks in `c`, CACHE 2 takes them from `c` instead of loading them again (a
+// second pass over x then costs no memory round when K <= 32 nthr).
+template <int CACHE = 0, typename Fn>
+__device__ __forceinline__ void x_blocks(const Params& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
+    const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
+    const int nx = p.K / 8;
+    for (int i0 = tid, r = 0; i0 < n; i0 += 4 * nthr, ++r) {
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = i0 + k * nthr;
+            if (CACHE == 2 && r == 0) v[k] = c[k];
+            else v[k] = i < nx ? __ldg(x4 + i) : make_uint4(0u, 0u, 0u, 0u);
+            if (CACHE == 1 && r == 0) c[k] = v[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (i0 + k * nthr < n) fn(i0 + k * nthr, v[k]);
+    }
+}
+// As x_blocks, but every thread calls fn(i, v) in every round (i may be >= n; v is then zero), so fn may use
+// warp shuffles; blocks i0 + tid of a round belong to consecutive lanes.
+template <int CACHE = 0, typename Fn>
+__device__ __forceinline__ void x_blocks_all(const Params& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
+    const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
+    const int nx = p.K / 8;
+    for (int i0 = 0, r = 0; i0 < n; i0 += 4 * nthr, ++r) {
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = i0 + k * nthr + tid;
+            if (CACHE == 2 && r == 0) v[k] = c[k];
+            else v[k] = i < nx ? __ldg(x4 + i) : make_uint4(0u, 0u, 0u, 0u);
+            if (CACHE == 1 && r == 0) c[k] = v[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (i0 + k * nthr < n) fn(i0 + k * nthr + tid, v[k]);
+    }
+}
+
 // Stage x for the tensor-core kernels (padded with zeros to Kpad): BF16 as is; FP8 as f16 scaled by 2^-e (e from the
 // CTA-wide max|x|, written to xscale[0] as an int, 2^-e to xscale[1]) with the 4-block order the FP8 decoder DEC
 // expects; INT4 with each 8-block permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7) plus the sum of every 128-group.
 // Called by `nthr` threads (thread index tid); `sync` is the barrier over exactly those threads; `scratch` holds
 // nthr/32 floats. Ends with x visible to the caller only after the caller's own barrier.
-template <int F, int DEC, typename Sync>
+template <int F, int DEC, int GST = 1, typename Sync>
 __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gsum, float* xscale, float* scratch, int tid,
                                         int nthr, Sync sync) {
+    // INT4 group sums are written GST words apart (the integer path needs 8 words per group)
+    static_assert(!(F == kINT4 || F == kINT4A) || DEC != 2 || GST == 8, "integer INT4 staging needs 8 words per group");
     const int Kp = mma_kpad<F>(p.K);
     if constexpr (F == kBF16) {
-        for (int i = tid; i < Kp / 8; i += nthr) {
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (8 * i < p.K) v = __ldg(reinterpret_cast<const uint4*>(p.x) + i);   // K % 8 == 0
-            reinterpret_cast<uint4*>(xs)[i] = v;
-        }
+        x_blocks(p, tid, nthr, Kp / 8, [&](int i, uint4 v) { reinterpret_cast<uint4*>(xs)[i] = v; });   // K % 8 == 0
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
+    } else if constexpr (F == kFP8 && DEC == 3) {
+        // x * 2^-e (max|x| * 2^-e in [128, 256)) split into two e4m3 terms hi + lo, bytes in natural order: hi at xs,
+        // lo at xs + Kpad bytes. hi = RN(v) keeps 4 significant bits and lo = RN(v - hi) the next 4, so hi + lo == v
+        // exactly for |v| >= 2^-2 (bf16 carries 8 significant bits); smaller values keep an absolute error below
+        // 2^-10, i.e. < 2^-17 of max|x|.
+        float m = 0.f;
+        uint4 xc[4] = {};
+        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+            m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
+                               fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
+        }, xc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((tid & 31) == 0) scratch[tid >> 5] = m;
+        sync();
+        if (tid == 0) {
+            float mm = 0.f;
+            for (int w = 0; w < nthr / 32; ++w) mm = fmaxf(mm, scratch[w]);
+            int e = 0;
+            if (mm > 0.f && mm <= 3.40282347e38f) {
+                const int ex = (int)((__float_as_uint(mm) >> 23) & 0xFF) - 127;
+                e = (ex < -126 ? -126 : ex) - 7;
+                e = e < -126 ? -126 : (e > 126 ? 126 : e);
+            }
+            xscale[0] = __int_as_float(e);
+            xscale[1] = __uint_as_float((uint32_t)(127 - e) << 23);
+        }
+        sync();
+        const float inv = xscale[1];
+        uint8_t* xh = reinterpret_cast<uint8_t*>(xs);
+        uint8_t* xl = xh + Kp;
+        x_blocks<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
+            uint2 h = make_uint2(0u, 0u), l = make_uint2(0u, 0u);
+            if (8 * i < p.K) {
+                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+                uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float a = bf_lo(vv[j]) * inv, b = bf_hi(vv[j]) * inv;
+                    const __nv_fp8x2_storage_t hp = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+                    const float2 hf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(hp, __NV_E4M3)));
+                    const __nv_fp8x2_storage_t lp =
+                        __nv_cvt_float2_to_fp8x2(make_float2(a - hf.x, b - hf.y), __NV_SATFINITE, __NV_E4M3);
+                    hw[j >> 1] |= (uint32_t)hp << (16 * (j & 1));
+                    lw[j >> 1] |= (uint32_t)lp << (16 * (j & 1));
+                }
+                h = make_uint2(hw[0], hw[1]);
+                l = make_uint2(lw[0], lw[1]);
+            }
+            reinterpret_cast<uint2*>(xh)[i] = h;
+            reinterpret_cast<uint2*>(xl)[i] = l;
+        }, xc);
     } else if constexpr (F == kFP8) {
         // max |x| over the CTA, then x * 2^-e in f16 (exact while max|x| * 2^-e < 2^15 and values stay normal)
         float m = 0.f;
-        for (int i = tid; i < p.K / 8; i += nthr) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x) + i);
+        uint4 xc[4] = {};
+        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }
+        }, xc);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -131,10 +244,9 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
         }
         sync();
         const float inv = xscale[1];
-        for (int i = tid; i < Kp / 8; i += nthr) {
+        x_blocks<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             uint4 o = make_uint4(0u, 0u, 0u, 0u);
             if (8 * i < p.K) {
-                const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x) + i);
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
                 uint32_t oo[4];
 #pragma unroll
@@ -151,15 +263,151 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
                 o = make_uint4(oo[0], oo[1], oo[2], oo[3]);
             }
             reinterpret_cast<uint4*>(xs)[i] = o;
+        }, xc);
+    } else if constexpr (DEC == 2) {
+        // INT4 for the integer MMA: v = x * 2^s rounded to an integer below 2^20 in magnitude (exact for every element
+        // within 2^12 of max|x|, bf16 carrying 8 significant bits; smaller ones keep an error below 2^-21 max|x|),
+        // split into three balanced base-128 digits d0 + 128 d1 + 128^2 d2, each an int8 plane of Kpad bytes at
+        // xs + d Kpad with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
+        // Per 128-group g: the digit sums S_d (int) at gsum[8g + d] and sum(v) (float) at gsum[8g + 4].
+        // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
+        float m = 0.f;
+        bool bad = false;
+        uint4 xc[4] = {};
+        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                bad |= ((vv[j] & 0x7F800000u) == 0x7F800000u) || ((vv[j] & 0x7F80u) == 0x7F80u);
+                m = fmaxf(m, fmaxf(fabsf(bf_lo(vv[j])), fabsf(bf_hi(vv[j]))));
+            }
+        }, xc);
+        if (__any_sync(0xffffffffu, bad)) m = __int_as_float(0x7F800000);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((tid & 31) == 0) scratch[tid >> 5] = m;
+        sync();
+        if (tid == 0) {
+            float mm = 0.f;
+            for (int w = 0; w < nthr / 32; ++w) mm = fmaxf(mm, scratch[w]);
+            int sh = 0;
+            float inv = 1.f;
+            if (!(mm <= 3.40282347e38f)) {
+                inv = __int_as_float(0x7FC00000);                         // NaN or infinity in x
+            } else if (mm > 0.f) {
+                const int ex = (int)((__float_as_uint(mm) >> 23) & 0xFF) - 127;   // floor(log2) (subnormal: -127)
+                sh = 19 - (ex < -126 ? -126 : ex);                        // max|x| * 2^sh in [2^19, 2^20)
+                sh = sh > 126 ? 126 : sh;                                 // 2^-sh stays a normal float
+                inv = __uint_as_float((uint32_t)(127 - sh) << 23);
+            }
+            xscale[0] = __int_as_float(sh);
+            xscale[1] = inv;
         }
+        sync();
+        const int sh = __float_as_int(xscale[0]);
+        // 2^sh as a product of two normal floats (|sh| <= 126)
+        const float up = __uint_as_float((uint32_t)(127 + (sh > 0 ? sh / 2 : 0)) << 23);
+        const float up2 = __uint_as_float((uint32_t)(127 + (sh > 0 ? sh - sh / 2 : sh)) << 23);
+        uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
+        int* gi = reinterpret_cast<int*>(gsum);
+        x_blocks_all<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
+            // blocks past K / 8 arrive as zeros and stage as zero digits
+            float sd[3] = {0.f, 0.f, 0.f};
+            if (i < Kp / 8) {
+                uint32_t dw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float xf = (j & 1) ? bf_hi(vv[j >> 1]) : bf_lo(vv[j >> 1]);
+                    // digits in float arithmetic: every step is exact (integers below 2^24)
+                    const float q0 = rintf((xf * up) * up2);
+                    const float q1 = rintf(q0 * 0.0078125f);
+                    const float q2 = rintf(q1 * 0.0078125f);
+                    const float d0 = fmaf(q1, -128.f, q0), d1 = fmaf(q2, -128.f, q1);
+                    sd[0] += d0; sd[1] += d1; sd[2] += q2;
+                    const int slot = (j & 1) ? 4 + (j >> 1) : (j >> 1);   // evens first, then odds
+                    const int sft = 8 * (slot & 3);
+                    dw[0][slot >> 2] |= (uint32_t)(__float2int_rn(d0) & 0xFF) << sft;
+                    dw[1][slot >> 2] |= (uint32_t)(__float2int_rn(d1) & 0xFF) << sft;
+                    dw[2][slot >> 2] |= (uint32_t)(__float2int_rn(q2) & 0xFF) << sft;
+                }
+#pragma unroll
+                for (int d = 0; d < 3; ++d)
+                    *reinterpret_cast<uint2*>(planes + (size_t)d * Kp + 8 * (size_t)i) = make_uint2(dw[d][0], dw[d][1]);
+            }
+#pragma unroll
+            for (int d = 0; d < 3; ++d)
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) sd[d] += __shfl_xor_sync(0xffffffffu, sd[d], o);   // 16-lane groups
+            if (i < Kp / 8 && (i & 15) == 0) {
+                const int gg = i >> 4;
+#pragma unroll
+                for (int d = 0; d < 3; ++d) gi[8 * gg + d] = (int)sd[d];
+                gsum[8 * gg + 4] = sd[0] + 128.f * sd[1] + 16384.f * sd[2];
+            }
+        }, xc);
+    } else if constexpr (DEC == 1) {
+        // INT4 for the f16 nibble decode: x * 2^-e in f16 (max|x| * 2^-e in [2^13, 2^14)), 8-element blocks stored as
+        // pairs (x0,x4),(x2,x6),(x1,x5),(x3,x7) (even k feed the "1024 + n" MMA, odd k the "1024 + 16 n" MMA); per
+        // 128-group g: gsum[GST g] = 1032 S_even + 72 S_odd (the decode and symmetric offsets), gsum[GST g + 1] =
+        // S_even + S_odd, over the f16 values the MMA sees.
+        float m = 0.f;
+        uint4 xc[4] = {};
+        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+            m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
+                               fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
+        }, xc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((tid & 31) == 0) scratch[tid >> 5] = m;
+        sync();
+        if (tid == 0) {
+            float mm = 0.f;
+            for (int w = 0; w < nthr / 32; ++w) mm = fmaxf(mm, scratch[w]);
+            int e = 0;
+            if (mm > 0.f && mm <= 3.40282347e38f) {
+                const int ex = (int)((__float_as_uint(mm) >> 23) & 0xFF) - 127;
+                e = (ex < -126 ? -126 : ex) - 13;
+                e = e < -126 ? -126 : (e > 126 ? 126 : e);
+            }
+            xscale[0] = __int_as_float(e);
+            xscale[1] = __uint_as_float((uint32_t)(127 - e) << 23);
+        }
+        sync();
+        const float inv = xscale[1];
+        const int nb = p.K / 8;                                  // K % 128 == 0 -> nb % 16 == 0
+        x_blocks_all<2>(p, tid, nthr, nb, [&](int i, uint4 v) {
+            float se = 0.f, so = 0.f;
+            if (i < nb) {
+                const __half2 h01 = __floats2half2_rn(bf_lo(v.x) * inv, bf_hi(v.x) * inv);
+                const __half2 h23 = __floats2half2_rn(bf_lo(v.y) * inv, bf_hi(v.y) * inv);
+                const __half2 h45 = __floats2half2_rn(bf_lo(v.z) * inv, bf_hi(v.z) * inv);
+                const __half2 h67 = __floats2half2_rn(bf_lo(v.w) * inv, bf_hi(v.w) * inv);
+                const uint32_t u01 = *reinterpret_cast<const uint32_t*>(&h01), u23 = *reinterpret_cast<const uint32_t*>(&h23);
+                const uint32_t u45 = *reinterpret_cast<const uint32_t*>(&h45), u67 = *reinterpret_cast<const uint32_t*>(&h67);
+                reinterpret_cast<uint4*>(xs)[i] = make_uint4(__byte_perm(u01, u45, 0x5410), __byte_perm(u23, u67, 0x5410),
+                                                             __byte_perm(u01, u45, 0x7632), __byte_perm(u23, u67, 0x7632));
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                const float2 f45 = __half22float2(h45), f67 = __half22float2(h67);
+                se = (f01.x + f23.x) + (f45.x + f67.x);
+                so = (f01.y + f23.y) + (f45.y + f67.y);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {                    // 16-lane groups
+                se += __shfl_xor_sync(0xffffffffu, se, o);
+                so += __shfl_xor_sync(0xffffffffu, so, o);
+            }
+            if (i < nb && (i & 15) == 0) {
+                gsum[GST * (i >> 4)] = 1032.f * se + 72.f * so;
+                gsum[GST * (i >> 4) + 1] = se + so;
+            }
+        }, xc);
     } else {
         // 8-element blocks permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7); sum of each 128-group (16 blocks)
         const int nb = p.K / 8;                                  // K % 128 == 0 -> nb % 16 == 0
-        for (int i0 = 0; i0 < nb; i0 += nthr) {
-            const int i = i0 + tid;
+        x_blocks_all(p, tid, nthr, nb, [&](int i, uint4 v) {
             float sum = 0.f;
             if (i < nb) {
-                const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x) + i);
                 const uint32_t pr0 = (v.x & 0xFFFFu) | (v.z << 16);            // (x0, x4)
                 const uint32_t pr1 = (v.x >> 16) | (v.z & 0xFFFF0000u);        // (x1, x5)
                 const uint32_t pr2 = (v.y & 0xFFFFu) | (v.w << 16);            // (x2, x6)
@@ -170,8 +418,8 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
             }
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);   // 16-lane groups
-            if (i < nb && (i & 15) == 0) gsum[i >> 4] = sum;
-        }
+            if (i < nb && (i & 15) == 0) gsum[GST * (i >> 4)] = sum;
+        });
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     }
 }

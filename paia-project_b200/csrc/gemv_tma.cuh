@@ -19,12 +19,14 @@
 //             reach past either end of its array is read with plain loads instead.
 //   consumers warps 0..NC-1 wait for the dependency, stage x (as gemv_mma.cuh), then for every stage take an equal
 //             share of its 64-byte steps, load A fragments from the stage (rows g and g+8, bytes 16c of each step),
-//             B fragments from x, and run the same dequantisation and mma.sync.m16n8k16 as gemv_mma.cuh. The step
-//             loop is branch-free (U steps per iteration; the remainder and the ragged last step of a row run one at a
-//             time) and keeps two accumulator chains per step. At the last stage of a tile each warp leaves its 16
-//             partial sums in shared memory and counts itself in; the last warp to arrive adds the NC partials in warp
-//             order (deterministic) and writes the 16 outputs, before releasing the stage (whose metadata it reads).
-//             No warp waits for another except through the ring.
+//             B fragments from x, and run the dequantisation and mma.sync of the format. The step loop is
+//             branch-free (U steps per iteration; the remainder and the ragged last step of a row run one at a time)
+//             and keeps two accumulator chains per step. At the last stage of a tile each warp leaves its 16 partial
+//             sums in a shared-memory buffer and arrives on the buffer's `tile_done` mbarrier; no consumer waits
+//             for another except through the ring.
+//   epilogue  warp NC+1 adds each tile's NC partials in warp order (deterministic), applies the row scale, the x
+//             scale and the bias (loaded from global memory while the tile is computed), writes the 16 outputs and
+//             frees the buffer (`part_free`), so the tile-end work never stalls the consumers.
 //   waits     every mbarrier wait gives up after ~2 s (%globaltimer), records an error code that
 //             paia_gemv_device_error() reports, and carries on without waiting, so a fault can never hang the GPU.
 #pragma once
@@ -44,6 +46,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* m) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* m, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" :: "r"(smem_addr(m)), "r"(bytes) : "memory");
 }
+// try_wait may suspend the thread for a system-dependent time before it reports an incomplete phase.
 __device__ __forceinline__ bool mbar_test(uint64_t* m, uint32_t parity) {
     uint32_t ok;
     asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
@@ -66,6 +69,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, int code
         }
     }
     return true;
+}
+// Weights are read exactly once: mark their L2 lines evict-first so activations and outputs stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_copy_g2s_ef(void* dst, const void* src, uint32_t bytes, uint64_t* m, uint64_t pol) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(m)), "l"(pol) : "memory");
 }
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -102,7 +115,10 @@ __device__ __forceinline__ void u16_word_copy(uint16_t* dst, const uint16_t* a, 
     }
 }
 
-constexpr int kTmaMaxRing = 16;        // ring stages at most (mbarrier region 256 bytes)
+constexpr int kTmaMaxRing = 16;        // ring stages at most
+constexpr int kTmaMaxParts = kTmaMaxRing + 1;   // tile-partial buffers at most
+// mbarriers: full[16], empty[16], tile_done[17], part_free[17], x_ready (67 x 8 bytes, padded to 640)
+constexpr int kTmaBarBytes = 640;
 
 // Metadata slot of a stage (bytes): FP8 row scales float[16] at 0; bias words (18 halves) at 64; INT4 scales and
 // (INT4A) zeros at 112, 16 rows x tma_meta_row(CS) halves each.
@@ -111,33 +127,37 @@ template <int F>
 __host__ __device__ constexpr int tma_meta_bytes(int cs) {
     return 112 + ((F == kINT4 || F == kINT4A) ? 16 * tma_meta_row(cs) * 2 * (F == kINT4A ? 2 : 1) : 0);
 }
-// Tile-partial buffers: a warp runs at most ring - 1 stages ahead of the slowest, i.e. ceil((ring - 1) / NCH) + 1
-// tiles; one more buffer keeps the last arriver's reads apart from the next writers.
+// INT4 per-group sums in shared memory: 8 words per group for the integer path (four digit sums and sum x), else 2.
+__host__ __device__ constexpr int tma_gsum_words(int dec) { return dec == 2 ? 8 : 2; }
+// Tile-partial buffers: consumers run at most ring - 1 stages ahead of the slowest, i.e. ceil((ring - 1) / NCH) + 1
+// tiles; one more lets the epilogue warp lag a tile before a consumer waits for a free buffer.
 __host__ __device__ constexpr int tma_part_bufs(int ring, int nch) { return (ring - 1 + nch - 1) / nch + 2; }
 
-// Shared-memory layout (bytes): [0,256) mbarriers full[ring], empty[ring]; ring x st_bytes; metadata ring x
-// tma_meta_bytes (16-byte multiples); x Kpad x 2; INT4 group sums Kpad/128 floats; tile partials NB x NC x 16 floats;
-// NB arrival counters; x scale 16 bytes.
-template <int F, int NC>
+// Shared-memory layout (bytes): [0,640) mbarriers; ring x st_bytes; metadata ring x
+// tma_meta_bytes (16-byte multiples); x Kpad x 2 (INT4 integer path: Kpad x 3); INT4 group sums 8 words per group; tile partials
+// NB x NC x 16 floats; x scale 16 bytes.
+template <int F, int NC, int DEC>
 __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int kc, int st_bytes) {
     const int kp = mma_kpad<F>(K);
     const size_t mb = (size_t)(tma_meta_bytes<F>(kc / 64) + 15) / 16 * 16;
     const int nb = tma_part_bufs(ring < 2 ? 2 : ring, nch);
-    return 256 + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * 2 +
-           ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * 4 : 0) + (size_t)nb * NC * 16 * 4 + (size_t)nb * 4 + 16;
+    // x: 2 bytes per element (3 for the INT4 integer path's digit planes)
+    constexpr size_t xb = ((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2;
+    return kTmaBarBytes + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * xb +
+           ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * tma_gsum_words(DEC) * 4 : 0) + (size_t)nb * NC * 16 * 4 + 16;
 }
 
 // Host: choose the stage geometry for this shape within `cap` bytes of shared memory and return the dynamic shared
 // memory size (0 when it cannot be staged). A row is split into NCH equal chunks of KC bytes (a multiple of 64, at most
 // 4096 so that a 16-row stage stays <= 64 KB; INT4 at most 2048, i.e. <= 32 groups of metadata per stage). p.ring on
 // entry is the requested ring depth (>= 2), or 0 for as many stages as fit (2..16; KC then sized for >= 3 stages).
-template <int F, int NC>
+template <int F, int NC, int DEC>
 size_t tma_prep(Params& p, size_t cap) {
     const size_t rowbytes = (size_t)p.nchunk * 16;
     const int want = p.ring;
     if (want == 1 || want > kTmaMaxRing) return 0;
-    // everything but the ring and its metadata (partial buffers sized for the deepest ring and one chunk per row)
-    const size_t fixed = tma_smem_bytes<F, NC>(p.K, 0, 1, 64, 0) + (size_t)(kTmaMaxRing + 1) * (NC * 64 + 4);
+    // everything but the ring and its metadata (partial buffers sized for a 4-stage ring; checked again below)
+    const size_t fixed = tma_smem_bytes<F, NC, DEC>(p.K, 0, 1, 64, 0) + (size_t)3 * (NC * 64 + 4);
     if (fixed >= cap) return 0;
     // a stage needs at most 16 (KC + 64) + 128 ring bytes and 112 + 2 x 2 x 16 (KC/64 + 3) + 15 metadata bytes
     const size_t per_stage_cap = (cap - fixed) / (want >= 2 ? want : 3);
@@ -163,8 +183,10 @@ size_t tma_prep(Params& p, size_t cap) {
         ring = fit > (size_t)kTmaMaxRing ? kTmaMaxRing : (int)fit;
         if (ring < 2) return 0;
     }
+    size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, nch, p.kc, p.st_bytes);
+    while (want == 0 && total > cap && ring > 2)               // deeper rings need more partial buffers
+        total = tma_smem_bytes<F, NC, DEC>(p.K, --ring, nch, p.kc, p.st_bytes);
     p.ring = ring;
-    const size_t total = tma_smem_bytes<F, NC>(p.K, ring, nch, p.kc, p.st_bytes);
     return total <= cap ? total : 0;
 }
 
@@ -188,7 +210,7 @@ template <int F, int DEC, int NU, bool CHECK, int U>
 __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1, const uint8_t* r0p, const uint8_t* r1p,
                                           const uint16_t* xs, const float* gsum, const uint16_t* sc0,
                                           const uint16_t* sc1, const uint16_t* zr0, const uint16_t* zr1, int sl, int gs,
-                                          int c, int nchunk) {
+                                          int c, int nchunk, int xlo_off) {
     constexpr int SK = MmaStep<F>::k;
     uint4 w0[NU], w1[NU];
 #pragma unroll
@@ -206,6 +228,20 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
         for (int u = 0; u < NU; ++u) {
             mma_bf16(A.a[u][0], w0[u].x, w1[u].x, w0[u].y, w1[u].y, xv[u].x, xv[u].y);
             mma_bf16(A.a[u][1], w0[u].z, w1[u].z, w0[u].w, w1[u].w, xv[u].z, xv[u].w);
+        }
+    } else if constexpr (F == kFP8 && DEC == 3) {
+        // e4m3 weights straight into the tensor cores. x = hi + lo (two e4m3 terms) rides in MMA columns 0 (hi) and
+        // 1 (lo): lanes of group g = 1 supply B column 1, all others column 0's hi bytes, so one mma.sync per 32
+        // weights and row yields both dot products (columns 2-7 repeat hi and are never read).
+        const int grp = (int)(threadIdx.x & 31) >> 2;
+        const uint8_t* xb8 = reinterpret_cast<const uint8_t*>(xs) + (size_t)gs * 64 + 16 * c + (grp == 1 ? xlo_off : 0);
+        uint4 xv[NU];
+#pragma unroll
+        for (int u = 0; u < NU; ++u) xv[u] = *reinterpret_cast<const uint4*>(xb8 + 64 * u);
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            mma_e4m3(A.a[u][0], w0[u].x, w1[u].x, w0[u].y, w1[u].y, xv[u].x, xv[u].y);
+            mma_e4m3(A.a[u][1], w0[u].z, w1[u].z, w0[u].w, w1[u].w, xv[u].z, xv[u].w);
         }
     } else if constexpr (F == kFP8) {
         uint4 xa[NU], xc[NU];
@@ -230,6 +266,67 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
                             e4m3x2_to_f16x2(b >> 16), xv[2 * t4], xv[2 * t4 + 1]);
             }
         }
+    } else if constexpr (DEC == 2) {
+        // INT4, integer MMA: nibbles -> u8 (one LOP3 for the low nibbles, a shift and a LOP3 for the high ones),
+        // against x as three int8 digit planes; lane group g reads plane g (g < 3), so MMA column d carries digit d
+        // and one m16n8k32 yields the three exact digit dot products of 32 weights of 16 rows. Per group:
+        // sum_d (D_d - 8 S_d) 128^d, lanes c = 0 / 1 holding digits 0-1 / 2 (column 3 and c = 2, 3 are unused).
+        const int grp = (int)(threadIdx.x & 31) >> 2;
+        const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp < 3 ? grp : 0) * xlo_off +
+                            (size_t)gs * 128 + 32 * c;
+        const int* gi = reinterpret_cast<const int*>(gsum);
+        const float flo = c == 0 ? 1.f : (c == 1 ? 16384.f : 0.f);
+        const float fhi = c == 0 ? 128.f : 0.f;
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            const uint4 xa = *reinterpret_cast<const uint4*>(xp + 128 * u);
+            const uint4 xq = *reinterpret_cast<const uint4*>(xp + 128 * u + 16);
+            const uint32_t bx[8] = {xa.x, xa.y, xa.z, xa.w, xq.x, xq.y, xq.z, xq.w};
+            int de[4] = {0, 0, 0, 0}, dq[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t a = (&w0[u].x)[q], b = (&w1[u].x)[q];
+                mma_u8s8((q & 1) ? dq : de, a & 0x0F0F0F0Fu, b & 0x0F0F0F0Fu, (a >> 4) & 0x0F0F0F0Fu,
+                         (b >> 4) & 0x0F0F0F0Fu, bx[2 * q], bx[2 * q + 1]);
+            }
+            const int gidx = 8 * (gs + u);
+            const int slo = gi[gidx + 2 * (c & 1)], shi = c == 0 ? gi[gidx + 1] : 0;
+            const float r0 = (float)(de[0] + dq[0] - 8 * slo) * flo + (float)(de[1] + dq[1] - 8 * shi) * fhi;
+            const float r1 = (float)(de[2] + dq[2] - 8 * slo) * flo + (float)(de[3] + dq[3] - 8 * shi) * fhi;
+            if constexpr (F == kINT4) {
+                acc0 = fmaf(__half2float(__ushort_as_half(sc0[sl + u])), r0, acc0);
+                acc1 = fmaf(__half2float(__ushort_as_half(sc1[sl + u])), r1, acc1);
+            } else {
+                const float sx = c == 0 ? gsum[gidx + 4] : 0.f;   // zero term once per row (lane c = 0)
+                acc0 = fmaf(bf_lo(sc0[sl + u]), r0, fmaf(bf_lo(zr0[sl + u]), sx, acc0));
+                acc1 = fmaf(bf_lo(sc1[sl + u]), r1, fmaf(bf_lo(zr1[sl + u]), sx, acc1));
+            }
+        }
+    } else if constexpr (DEC == 1) {
+        // INT4, f16 decode: even k as 1024 + n, odd k as 1024 + 16 n (one LOP3 per pair, one shift per word), each
+        // parity in its own MMA chain; fold (D_even + D_odd / 16 - C_g) per group, C_g from the x staging
+#pragma unroll
+        for (int u = 0; u < NU; ++u) {
+            float de[4] = {0.f, 0.f, 0.f, 0.f}, dq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 xq = *reinterpret_cast<const uint4*>(xb + u * SK + 8 * q);
+                const uint32_t a = (&w0[u].x)[q], b = (&w1[u].x)[q];
+                const uint32_t a8 = a >> 8, b8 = b >> 8;
+                mma_f16(de, nib_lo_f16(a), nib_lo_f16(b), nib_lo_f16(a8), nib_lo_f16(b8), xq.x, xq.y);
+                mma_f16(dq, nib_hi_f16(a), nib_hi_f16(b), nib_hi_f16(a8), nib_hi_f16(b8), xq.z, xq.w);
+            }
+            const float cg = gsum[2 * (gs + u)];
+            const float r0 = fmaf(dq[0], 0.0625f, de[0]) - cg, r1 = fmaf(dq[2], 0.0625f, de[2]) - cg;
+            if constexpr (F == kINT4) {
+                acc0 = fmaf(__half2float(__ushort_as_half(sc0[sl + u])), r0, acc0);
+                acc1 = fmaf(__half2float(__ushort_as_half(sc1[sl + u])), r1, acc1);
+            } else {
+                const float sx = gsum[2 * (gs + u) + 1];
+                acc0 = fmaf(bf_lo(sc0[sl + u]), r0, fmaf(bf_lo(zr0[sl + u]), sx, acc0));
+                acc1 = fmaf(bf_lo(sc1[sl + u]), r1, fmaf(bf_lo(zr1[sl + u]), sx, acc1));
+            }
+        }
     } else {
 #pragma unroll
         for (int u = 0; u < NU; ++u) {
@@ -244,7 +341,7 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
                          xq.z, xq.w);
             }
             // every lane holds rows g and g + 8 (all 8 MMA columns carry the same x), so all lanes fold alike
-            const float sx = gsum[gs + u];
+            const float sx = gsum[2 * (gs + u)];
             const float off = -136.f * sx;
             const float r0 = d[0][0] + d[1][0] + off, r1 = d[0][2] + d[1][2] + off;
             if constexpr (F == kINT4) {
@@ -259,7 +356,7 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
 }
 
 template <int F, int NC, int U, int DEC = 0>
-__global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params p) {
+__global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params p) {
     constexpr bool I4 = (F == kINT4 || F == kINT4A);
     extern __shared__ __align__(128) uint8_t smem[];
     const int KC = p.kc, NCH = p.nch, RS = p.rs;
@@ -272,14 +369,17 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params
     const size_t rowbytes = (size_t)p.nchunk * 16;
     const int Kp = mma_kpad<F>(p.K);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + ST;
-    uint8_t* ring = smem + 256;
+    uint64_t* empty = full + kTmaMaxRing;
+    uint64_t* tdone = empty + kTmaMaxRing;                    // tile t's NC partials are in buffer t mod NB
+    uint64_t* pfree = tdone + kTmaMaxParts;                   // the epilogue warp has read buffer t mod NB
+    uint64_t* xready = pfree + kTmaMaxParts;                  // the consumers have staged x
+    uint8_t* ring = smem + kTmaBarBytes;
     uint8_t* meta = ring + (size_t)ST * p.st_bytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(meta + (size_t)ST * MB);
-    float* gsum = reinterpret_cast<float*>(xs + Kp);
-    float* part = gsum + (I4 ? Kp / 128 : 0);
-    int* cnt = reinterpret_cast<int*>(part + (size_t)NB * NC * 16);
-    float* xscale = reinterpret_cast<float*>(cnt + NB);
+    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)Kp * ((I4 && DEC == 2) ? 3 : 2));
+    constexpr int GW = tma_gsum_words(DEC);
+    float* part = gsum + (I4 ? GW * (Kp / 128) : 0);
+    float* xscale = part + (size_t)NB * NC * 16;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rb = (int)((long long)blockIdx.x * p.N / gridDim.x);
@@ -290,14 +390,22 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params
     if (tid == 0) {
         // full: the producer's expect_tx arrival, 32 lanes' cp.async arrivals and its closing arrival
         for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 34); mbar_init(&empty[s], NC); }
+        for (int b = 0; b < NB; ++b) { mbar_init(&tdone[b], NC); mbar_init(&pfree[b], 1); }
+        mbar_init(xready, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (tid < NB) cnt[tid] = 0;
     __syncthreads();
 
     if (warp == NC) {
         // ------------------------------------------------------------ producer warp
         const long long NG = (long long)p.N * p.groups;
+        const int pre = (p.pre > 0 && p.pre < ST) ? p.pre : -1;    // -1: never wait
+        const uint64_t wpol = l2_evict_first();
+        // INT4 whole-row stages whose scale (zero) runs start and end on 16-byte boundaries: one bulk copy per tile
+        bool meta_bulk = false;
+        if constexpr (I4)
+            meta_bulk = NCH == 1 && (p.groups & 7) == 0 && (((uintptr_t)p.s & 15) == 0) &&
+                        (F == kINT4 || ((uintptr_t)p.z & 15) == 0);
         int s = 0, t = 0, j = 0;
         uint32_t ph = 0;                                      // parity of the slot's previous release
         for (int i = 0; i < nst; ++i) {
@@ -306,45 +414,56 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params
             const bool last = j == NCH - 1;
             const int nsteps = last ? S - j * CS : CS;
             const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
+            const uint32_t mbytes = meta_bulk ? (uint32_t)(2 * nrows * p.groups) : 0u;   // per metadata array
             if (lane == 0) {
+                // x is read right after the dependency wait: streaming only `pre` stages until it is staged keeps
+                // the x loads from queueing behind a whole ring of this SM's copies
+                if (i == pre) mbar_wait(xready, 0, 5);
                 if (i >= ST) mbar_wait(&empty[s], ph, 1);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before the copies
-                mbar_arrive_expect_tx(&full[s], (uint32_t)nrows * bytes);
+                mbar_arrive_expect_tx(&full[s], (uint32_t)nrows * bytes + (F == kINT4A ? 2 : 1) * mbytes);
+                if (meta_bulk) {
+                    uint8_t* mdst = meta + (size_t)s * MB + 112;
+                    const size_t moff = (size_t)r0 * p.groups * 2;
+                    bulk_copy_g2s(mdst, reinterpret_cast<const uint8_t*>(p.s) + moff, mbytes, &full[s]);
+                    if constexpr (F == kINT4A)
+                        bulk_copy_g2s(mdst + 32 * MR, reinterpret_cast<const uint8_t*>(p.z) + moff, mbytes, &full[s]);
+                }
             }
             __syncwarp();                                     // the slot is free and its byte count announced
             if (lane < nrows)
-                bulk_copy_g2s(ring + (size_t)s * p.st_bytes + (size_t)lane * RS,
-                              p.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s]);
+                bulk_copy_g2s_ef(ring + (size_t)s * p.st_bytes + (size_t)lane * RS,
+                                 p.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s], wpol);
             uint8_t* ms = meta + (size_t)s * MB;
-            if (last) {
-                if constexpr (F == kFP8) {
-                    if (lane < nrows)
-                        cp_async4(reinterpret_cast<float*>(ms) + lane, reinterpret_cast<const float*>(p.s) + r0 + lane);
-                }
-                if (p.bias) {
-                    const int nw = u16_words(reinterpret_cast<const uint16_t*>(p.bias), r0, nrows);
-                    if (lane < nw)
-                        u16_word_copy(reinterpret_cast<uint16_t*>(ms + 64), reinterpret_cast<const uint16_t*>(p.bias),
-                                      p.N, r0, lane);
-                }
-            }
             if constexpr (I4) {
-                // rows x words of this stage's scale (and zero) runs, spread over the lanes; every row copies the
-                // (nsteps + 2) / 2 words that hold its run for either element parity
                 uint16_t* msc = reinterpret_cast<uint16_t*>(ms + 112);
                 const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s);
                 const uint16_t* za = reinterpret_cast<const uint16_t*>(p.z);
-                const int wpr = (nsteps + 2) >> 1;
-                int rr = lane / wpr, k = lane - rr * wpr;
-                const int drr = 32 / wpr, dk = 32 - drr * wpr;
-                while (rr < nrows) {
-                    const long long e0 = (long long)(r0 + rr) * p.groups + (long long)j * CS;
-                    if (k < u16_words(sa, e0, nsteps)) u16_word_copy(msc + rr * MR, sa, NG, e0, k);
-                    if constexpr (F == kINT4A)
-                        if (k < u16_words(za, e0, nsteps)) u16_word_copy(msc + (16 + rr) * MR, za, NG, e0, k);
-                    rr += drr;
-                    k += dk;
-                    if (k >= wpr) { k -= wpr; ++rr; }
+                if (NCH == 1) {
+                    // whole rows per stage: the tile's scales (zeros) are one contiguous run of nrows x G halves
+                    const long long e0 = (long long)r0 * p.groups;
+                    const int n = nrows * p.groups;
+                    if (!meta_bulk) {
+                        const int nw = u16_words(sa, e0, n);
+                        for (int k = lane; k < nw; k += 32) u16_word_copy(msc, sa, NG, e0, k);
+                        if constexpr (F == kINT4A)
+                            for (int k = lane; k < nw; k += 32) u16_word_copy(msc + 16 * MR, za, NG, e0, k);
+                    }
+                } else {
+                    // rows x words of this stage's scale (and zero) runs, spread over the lanes; every row copies
+                    // the (nsteps + 2) / 2 words that hold its run for either element parity
+                    const int wpr = (nsteps + 2) >> 1;
+                    int rr = lane / wpr, k = lane - rr * wpr;
+                    const int drr = 32 / wpr, dk = 32 - drr * wpr;
+                    while (rr < nrows) {
+                        const long long e0 = (long long)(r0 + rr) * p.groups + (long long)j * CS;
+                        if (k < u16_words(sa, e0, nsteps)) u16_word_copy(msc + rr * MR, sa, NG, e0, k);
+                        if constexpr (F == kINT4A)
+                            if (k < u16_words(za, e0, nsteps)) u16_word_copy(msc + (16 + rr) * MR, za, NG, e0, k);
+                        rr += drr;
+                        k += dk;
+                        if (k >= wpr) { k -= wpr; ++rr; }
+                    }
                 }
             }
             cp_async_arrive(&full[s]);
@@ -356,23 +475,64 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params
         return;
     }
 
+    if (warp == NC + 1) {
+        // ------------------------------------------------------------ epilogue warp
+        // Lane r < 16 owns row r of each tile: its row scale and bias are loaded before the wait for the tile's
+        // partials (so their latency hides behind the tile's compute); then the NC partials are added in warp order
+        // (deterministic), scaled, and stored; the buffer is handed back to the consumers.
+        grid_dependency_wait();                               // y is written only after the preceding grid is done
+        int b = 0;
+        uint32_t bph = 0;
+        for (int t = 0; t < T; ++t) {
+            const int row = rb + 16 * t + lane;
+            const bool mine = lane < 16 && row < re;
+            float rs = 1.f, rbias = 0.f;
+            if (mine) {
+                if constexpr (F == kFP8) rs = ld_f32(reinterpret_cast<const float*>(p.s) + row);
+                if (p.bias) rbias = __uint_as_float((uint32_t)ld_u16(p.bias + row) << 16);
+            }
+            mbar_wait(&tdone[b], bph, 3);
+            if (mine) {
+                const float* buf = part + (size_t)b * NC * 16;
+                float total = 0.f;
+#pragma unroll
+                for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
+                float out = total;
+                if constexpr (F == kFP8)                      // row scale, then 2^e (a normal power of two)
+                    out = out * rs * __uint_as_float((uint32_t)(__float_as_int(xscale[0]) + 127) << 23);
+                if constexpr (I4 && DEC == 1)                 // x was staged as x * 2^-e
+                    out = out * __uint_as_float((uint32_t)(__float_as_int(xscale[0]) + 127) << 23);
+                if constexpr (I4 && DEC == 2)                 // x was staged as integers x * 2^s
+                    out = out * xscale[1];
+                p.y[row] = __float2bfloat16_rn(out + rbias);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfree[b]);
+            if (++b == NB) { b = 0; bph ^= 1u; }
+        }
+        return;
+    }
+
     // ---------------------------------------------------------------- consumer warps
     grid_dependency_wait();
-    stage_x<F, DEC>(p, xs, gsum, xscale, part, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+    stage_x<F, DEC, tma_gsum_words(DEC)>(p, xs, gsum, xscale, part, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
     consumer_barrier(1, NC * 32);
-    if (tid == 0) launch_dependents();
+    if (tid == 0) {
+        launch_dependents();
+        mbar_arrive(xready);
+    }
 
     const int g = lane >> 2, c = lane & 3;
     // accumulator chains scaled by 1 (cvt decode, BF16) or 256 (FP8 ALU decode holds value / 256)
     constexpr float f0 = (F == kFP8 && DEC == 1) ? 256.f : 1.f;
-    constexpr float f1 = (F == kFP8 && DEC >= 1) ? 256.f : 1.f;
+    constexpr float f1 = (F == kFP8 && (DEC == 1 || DEC == 2)) ? 256.f : 1.f;
     TmaAcc<U> A;
     A.zero();
     float acc0 = 0.f, acc1 = 0.f;
     const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s);
     const uint16_t* za = reinterpret_cast<const uint16_t*>(p.z);
     int s = 0, t = 0, j = 0, b = 0;
-    uint32_t ph = 0;
+    uint32_t ph = 0, bph = 0;
     for (int i = 0; i < nst; ++i) {
         const int r0 = rb + 16 * t;
         const bool last = j == NCH - 1;
@@ -384,76 +544,69 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_tma_kernel(const Params
         const uint8_t* r0p = st + (size_t)g * RS + 16 * c;
         const uint8_t* r1p = r0p + (size_t)8 * RS;
         // INT4: this lane's scale (and zero) runs of rows g and g + 8, element parity folded in
-        const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(ms + 112) + g * MR;
-        const uint16_t* sc1 = sc0 + 8 * MR;
-        const uint16_t* zr0 = sc0 + 16 * MR;
-        const uint16_t* zr1 = sc1 + 16 * MR;
+        const uint16_t* msc = reinterpret_cast<const uint16_t*>(ms + 112);
+        const uint16_t *sc0 = msc, *sc1 = msc, *zr0 = msc, *zr1 = msc;
         if constexpr (I4) {
-            const long long e0 = (long long)(r0 + g) * p.groups + (long long)j * CS;
-            const long long e1 = e0 + 8LL * p.groups;
-            sc0 += u16_parity(sa + e0);
-            sc1 += u16_parity(sa + e1);
-            if constexpr (F == kINT4A) {
-                zr0 += u16_parity(za + e0);
-                zr1 += u16_parity(za + e1);
+            if (NCH == 1) {                                   // the tile's run: row rr at rr x G (+ run parity)
+                const long long e0 = (long long)r0 * p.groups;
+                sc0 = msc + u16_parity(sa + e0) + g * p.groups;
+                sc1 = sc0 + 8 * p.groups;
+                if constexpr (F == kINT4A) {
+                    zr0 = msc + 16 * MR + u16_parity(za + e0) + g * p.groups;
+                    zr1 = zr0 + 8 * p.groups;
+                }
+            } else {                                          // per-row runs: row rr at rr x MR (+ row parity)
+                const long long e0 = (long long)(r0 + g) * p.groups + (long long)j * CS;
+                const long long e1 = e0 + 8LL * p.groups;
+                sc0 = msc + g * MR + u16_parity(sa + e0);
+                sc1 = msc + (g + 8) * MR + u16_parity(sa + e1);
+                if constexpr (F == kINT4A) {
+                    zr0 = msc + (16 + g) * MR + u16_parity(za + e0);
+                    zr1 = msc + (24 + g) * MR + u16_parity(za + e1);
+                }
             }
         }
         const int gb = j * CS;                                // global step of stage-local step 0
         const int sfull = SF - gb < sb0 ? SF - gb : sb0;      // steps below sfull are whole
         int sl = sa0;
+#pragma unroll 2
         for (; sl + U <= sfull; sl += U)
-            tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk);
+            tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp);
         for (; sl < sfull; ++sl)
-            tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk);
+            tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp);
         for (; sl < sb0; ++sl)                                // the ragged last step of the row
-            tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk);
+            tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp);
 
         if (last) {
-            // tile end: this warp's partial sums of rows g, g + 8 -> buffer b; the last warp in adds them in order
+            // tile end: this warp's partial sums of rows g, g + 8 -> buffer b for the epilogue warp
             float s0, s1;
             if constexpr (I4) {
                 s0 = acc0; s1 = acc1;
+                if constexpr (DEC == 2) {                         // digits 0-1 (lane c = 0) + digit 2 (c = 1)
+                    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+                    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+                }
                 acc0 = acc1 = 0.f;
             } else {
                 s0 = 0.f; s1 = 0.f;
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    s0 += A.a[u][0][0] * f0 + A.a[u][1][0] * f1;
-                    s1 += A.a[u][0][2] * f0 + A.a[u][1][2] * f1;
+                    if constexpr (F == kFP8 && DEC == 3) {        // columns 0 (x hi) + 1 (x lo)
+                        s0 += (A.a[u][0][0] + A.a[u][0][1]) + (A.a[u][1][0] + A.a[u][1][1]);
+                        s1 += (A.a[u][0][2] + A.a[u][0][3]) + (A.a[u][1][2] + A.a[u][1][3]);
+                    } else {
+                        s0 += A.a[u][0][0] * f0 + A.a[u][1][0] * f1;
+                        s1 += A.a[u][0][2] * f0 + A.a[u][1][2] * f1;
+                    }
                 }
                 A.zero();
             }
+            if (t >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile t - NB
             float* buf = part + (size_t)b * NC * 16;
             if (c == 0) { buf[warp * 16 + g] = s0; buf[warp * 16 + g + 8] = s1; }
             __syncwarp();
-            int prior = 0;
-            if (lane == 0) {
-                __threadfence_block();
-                prior = atomicAdd(&cnt[b], 1);
-            }
-            prior = __shfl_sync(0xffffffffu, prior, 0);
-            if (prior == NC - 1) {                            // last arriver: all NC partials are in
-                __threadfence_block();
-                if (lane < 16) {
-                    float total = 0.f;
-#pragma unroll
-                    for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
-                    const int row = r0 + lane;
-                    if (row < re) {
-                        float out = total;
-                        if constexpr (F == kFP8)
-                            out = ldexpf(out * reinterpret_cast<const float*>(ms)[lane], __float_as_int(xscale[0]));
-                        if (p.bias) {
-                            const uint16_t* bw = reinterpret_cast<const uint16_t*>(ms + 64);
-                            out += __uint_as_float((uint32_t)bw[u16_parity(p.bias + r0) + lane] << 16);
-                        }
-                        p.y[row] = __float2bfloat16_rn(out);
-                    }
-                }
-                if (lane == 0) cnt[b] = 0;
-                __syncwarp();
-            }
-            if (++b == NB) b = 0;
+            if (lane == 0) mbar_arrive(&tdone[b]);             // release: this warp's partials of tile t
+            if (++b == NB) { b = 0; bph ^= 1u; }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);

@@ -1,12 +1,14 @@
 // TMA-fed tensor-core kernel instances (gemv_tma.cuh). math 5 = default weight decode of the format, and for FP8
-// math 6 = ALU bit decode, math 7 = split cvt/ALU decode. Tuple knobs: W = consumer warps (plus one producer warp),
+// math 6 = ALU bit decode, math 7 = split cvt/ALU decode, math 8 = e4m3 weights straight into e4m3 mma against x
+// split into two e4m3 terms; for INT4 math 6 = f16 nibble decode (1024 + n / 1024 + 16 n), math 7 = u8 nibbles
+// against x as int8 digits in an integer MMA (exact group sums). Tuple knobs: W = consumer warps (plus one producer warp),
 // U = 64-byte steps per consumer iteration. The ring depth and the shared-memory share are launch options.
 #include "gemv_launch.cuh"
 #include "gemv_tma.cuh"
 
 namespace pb2 {
 
-#define PB2_TMA(F, NC, U, H, M, DEC) {0, U, NC, 0, H, M, &gemv_tma_kernel<F, NC, U, DEC>, nullptr, &tma_prep<F, NC>},
+#define PB2_TMA(F, NC, U, H, M, DEC) {0, U, NC, 0, H, M, &gemv_tma_kernel<F, NC, U, DEC>, nullptr, &tma_prep<F, NC, DEC>},
 #define PB2_TMA_H(F, NC, U, M, DEC) PB2_TMA(F, NC, U, 0, M, DEC) PB2_TMA(F, NC, U, 1, M, DEC)
 #define PB2_TMA_U(F, NC, M, DEC) PB2_TMA_H(F, NC, 2, M, DEC) PB2_TMA_H(F, NC, 4, M, DEC)
 #define PB2_TMA_NC(F, M, DEC) PB2_TMA_U(F, 4, M, DEC) PB2_TMA_U(F, 8, M, DEC) PB2_TMA_U(F, 16, M, DEC)
@@ -14,8 +16,13 @@ static const Variant kBf16[] = {PB2_TMA_NC(kBF16, 5, 0)};
 static const Variant kFp8[] = {PB2_TMA_NC(kFP8, 5, 0)};
 static const Variant kFp8Alu[] = {PB2_TMA_NC(kFP8, 6, 1)};
 static const Variant kFp8Split[] = {PB2_TMA_NC(kFP8, 7, 2)};
+static const Variant kFp8Mma8[] = {PB2_TMA_NC(kFP8, 8, 3)};
 static const Variant kInt4[] = {PB2_TMA_NC(kINT4, 5, 0)};
 static const Variant kInt4a[] = {PB2_TMA_NC(kINT4A, 5, 0)};
+static const Variant kInt4F16[] = {PB2_TMA_NC(kINT4, 6, 1)};
+static const Variant kInt4aF16[] = {PB2_TMA_NC(kINT4A, 6, 1)};
+static const Variant kInt4I8[] = {PB2_TMA_NC(kINT4, 7, 2)};
+static const Variant kInt4aI8[] = {PB2_TMA_NC(kINT4A, 7, 2)};
 #undef PB2_TMA_NC
 #undef PB2_TMA_U
 #undef PB2_TMA_H
@@ -28,6 +35,17 @@ const Variant* tma_instances(int fmt, int math, int* n) {
         if (math == 5) { *n = PB2_N(kFp8); return kFp8; }
         if (math == 6) { *n = PB2_N(kFp8Alu); return kFp8Alu; }
         if (math == 7) { *n = PB2_N(kFp8Split); return kFp8Split; }
+        if (math == 8) { *n = PB2_N(kFp8Mma8); return kFp8Mma8; }
+        return nullptr;
+    }
+    if (math == 6) {
+        if (fmt == kINT4) { *n = PB2_N(kInt4F16); return kInt4F16; }
+        if (fmt == kINT4A) { *n = PB2_N(kInt4aF16); return kInt4aF16; }
+        return nullptr;
+    }
+    if (math == 7) {
+        if (fmt == kINT4) { *n = PB2_N(kInt4I8); return kInt4I8; }
+        if (fmt == kINT4A) { *n = PB2_N(kInt4aI8); return kInt4aI8; }
         return nullptr;
     }
     if (math != 5) return nullptr;

@@ -8,6 +8,7 @@ import pytest
 import torch
 
 import oracle as O
+from test_kernel_mapping import share_cap, tma_prep
 from gpu_cases import DEFAULT, KINDS, Operands, bits, check, lib, make, variant_id
 from paia_gemv import quant, synthetic
 
@@ -376,7 +377,15 @@ def test_fp8_mma_every_code_exact(L, math):
 TMA_CFGS = [(2, 2, 4, 1), (3, 4, 8, 1), (0, 2, 8, 2), (0, 4, 4, 1), (16, 2, 8, 1), (0, 2, 16, 1)]
 
 
-TMA_MATHS = [("bf16", 5), ("fp8", 5), ("fp8", 6), ("fp8", 7), ("int4", 5), ("int4_asym", 5)]
+def tma_fits(kind, math, NC, N, K, ring, share):
+    """Whether the TMA kernel can stage this shape (the CPU mirror of its shared-memory plan); else the C ABI
+    returns -2."""
+    dec = 2 if (kind.startswith("int4") and math == 7) else 0
+    return tma_prep(kind, NC, K, ring, share_cap(share), dec) is not None
+
+
+TMA_MATHS = [("bf16", 5), ("fp8", 5), ("fp8", 6), ("fp8", 7), ("fp8", 8), ("int4", 5), ("int4", 6), ("int4", 7),
+             ("int4_asym", 5), ("int4_asym", 6), ("int4_asym", 7)]
 
 
 @pytest.mark.parametrize("kind,math", TMA_MATHS)
@@ -395,6 +404,9 @@ def test_tma_kernel_awkward_and_real_shapes(L, kind, math):
             for cps in (0, 1):
                 ops.nan_fill()
                 rc = ops.call_ex(L, ring, U, NC, math, (i + cps) % 2, share, cps, with_bias=bool(cps))
+                if not tma_fits(kind, math, NC, N, K, ring, share):
+                    assert rc == -2, (kind, N, K, ring, share, rc)
+                    continue
                 assert rc == 0, (kind, N, K, ring, U, NC, share, cps, rc)
                 torch.cuda.synchronize()
                 check(ops, bits(ops.y), refb if cps else ref,
@@ -432,14 +444,14 @@ def test_fp8_tma_activation_ranges(L, scale):
     ops.x = xf.to(torch.bfloat16)
     ref = ops.oracle()[0]
     for ring, U, NC, share in TMA_CFGS:
-        for math in (5, 6, 7):
+        for math in (5, 6, 7, 8):
             ops.nan_fill()
             assert ops.call_ex(L, ring, U, NC, math, 1, share, 0) == 0
             torch.cuda.synchronize()
             check(ops, bits(ops.y), ref, f"fp8 tma{math} x*{scale}")
 
 
-@pytest.mark.parametrize("math", [5, 6, 7])
+@pytest.mark.parametrize("math", [5, 6, 7, 8])
 def test_fp8_tma_every_code_exact(L, math):
     codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.uint8)
     N, K = len(codes), 64

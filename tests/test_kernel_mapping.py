@@ -291,20 +291,21 @@ def tma_part_bufs(ring, nch):
     return (ring - 1 + nch - 1) // nch + 2
 
 
-def tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes):
+def tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec=0):
     SK = MMA_STEP_K[fmt]
     kp = (K + SK - 1) // SK * SK
     nb = tma_part_bufs(max(ring, 2), nch)
-    return (256 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * 2
-            + (kp // 128 * 4 if fmt.startswith("int4") else 0) + nb * NC * 16 * 4 + nb * 4 + 16)
+    i4 = fmt.startswith("int4")
+    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * (3 if i4 and dec == 2 else 2)
+            + (kp // 128 * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * 4 + 16)
 
 
-def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP):
+def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0):
     """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged."""
     rowbytes = ROWBYTES[fmt](K)
     if ring == 1 or ring > 16:
         return None
-    fixed = tma_smem_bytes(fmt, NC, K, 0, 1, 64, 0) + 17 * (NC * 64 + 4)
+    fixed = tma_smem_bytes(fmt, NC, K, 0, 1, 64, 0, dec) + 3 * (NC * 64 + 4)
     if fixed >= cap:
         return None
     per_stage_cap = (cap - fixed) // (ring if ring >= 2 else 3)
@@ -322,21 +323,25 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP):
     kc = ((rowbytes + nch - 1) // nch + 63) // 64 * 64
     rs = kc + 64 if kc % 128 == 0 else kc
     st_bytes = (16 * rs + 127) // 128 * 128
+    auto_ring = ring == 0
     if ring == 0:
         ring = min(16, (cap - fixed) // (st_bytes + tma_meta_bytes(fmt, kc // 64)))
         if ring < 2:
             return None
-    total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes)
+    total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec)
+    while auto_ring and total > cap and ring > 2:
+        ring -= 1
+        total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec)
     return (kc, nch, rs, st_bytes, ring, total) if total <= cap else None
 
 
-def meta_copy_u16(mod, T, e0, n, slot):
+def meta_copy_u16(mod, T, e0, n, slot, lanes=32):
     """Mirror of u16_words / u16_word_copy for a 2-byte array at byte address `mod` (mod 4) with T elements: every word
     copied with cp.async lies inside the array, partial words are read half by half inside it, the copy fits its
     shared-memory slot of `slot` halves, and every element of [e0, e0 + n) lands at parity + (e - e0)."""
     b = mod + 2 * e0
     nw = ((b + 2 * n - 1) >> 2) - (b >> 2) + 1
-    assert 1 <= nw <= 32 and 2 * nw <= slot
+    assert 1 <= nw and (lanes is None or nw <= lanes) and 2 * nw <= slot
     lo, hi = mod, mod + 2 * T
     got = {}
     for k in range(nw):
@@ -398,10 +403,18 @@ def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
                 copied[r0 + rr, j * KC // 16: j * KC // 16 + nbytes // 16] += 1
             if fmt.startswith("int4"):
                 MR = tma_meta_row(CS)
-                for rr in range(nrows):
-                    e0 = (r0 + rr) * groups + j * CS
-                    for mod in (0, 2):                             # array base address 0 or 2 modulo 4
-                        meta_copy_u16(mod, N * groups, e0, nsteps, MR)
+                if NCH == 1:                                       # the tile's contiguous run, words over 32 lanes
+                    assert S <= CS and 16 * groups + 2 <= 16 * MR
+                    for mod in (0, 2):
+                        meta_copy_u16(mod, N * groups, r0 * groups, nrows * groups, 16 * MR, lanes=None)
+                    if groups % 8 == 0:                            # the bulk-copy form of the same run
+                        assert (2 * r0 * groups) % 16 == 0 and (2 * nrows * groups) % 16 == 0
+                        assert (112 + 32 * MR) % 16 == 0 and MR % 2 == 0
+                else:
+                    for rr in range(nrows):
+                        e0 = (r0 + rr) * groups + j * CS
+                        for mod in (0, 2):                         # array base address 0 or 2 modulo 4
+                            meta_copy_u16(mod, N * groups, e0, nsteps, MR)
             if j == 0:
                 for lane in range(min(nrows, 32)):
                     assert 0 <= r0 + lane < N                      # FP8 row scales (4-byte cp.async)
