@@ -168,7 +168,7 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     } else if constexpr (F == kFP8 && DEC == 3) {
         // x * 2^-e (max|x| * 2^-e in [128, 256)) split into two e4m3 terms hi + lo, bytes in natural order: hi at xs,
-        // lo at xs + Kpad bytes. hi = RN(v) keeps 4 significant bits and lo = RN(v - hi) the next 4, so hi + lo == v
+        // lo at xs + Kpad + 64 bytes. hi = RN(v) keeps 4 significant bits and lo = RN(v - hi) the next 4, so hi + lo == v
         // exactly for |v| >= 2^-2 (bf16 carries 8 significant bits); smaller values keep an absolute error below
         // 2^-10, i.e. < 2^-17 of max|x|.
         float m = 0.f;
@@ -196,7 +196,7 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
         sync();
         const float inv = xscale[1];
         uint8_t* xh = reinterpret_cast<uint8_t*>(xs);
-        uint8_t* xl = xh + Kp;
+        uint8_t* xl = xh + Kp + 64;          // +64: hi and lo reads of one quarter-warp fall in different banks
         x_blocks<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             uint2 h = make_uint2(0u, 0u), l = make_uint2(0u, 0u);
             if (8 * i < p.K) {
@@ -268,7 +268,7 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
         // INT4 for the integer MMA: v = x * 2^s rounded to an integer below 2^20 in magnitude (exact for every element
         // within 2^12 of max|x|, bf16 carrying 8 significant bits; smaller ones keep an error below 2^-21 max|x|),
         // split into three balanced base-128 digits d0 + 128 d1 + 128^2 d2, each an int8 plane of Kpad bytes at
-        // xs + d Kpad with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
+        // xs + d (Kpad + 16) with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
         // Per 128-group g: the digit sums S_d (int) at gsum[8g + d] and sum(v) (float) at gsum[8g + 4].
         // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
         float m = 0.f;
@@ -333,7 +333,8 @@ __device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gs
                 }
 #pragma unroll
                 for (int d = 0; d < 3; ++d)
-                    *reinterpret_cast<uint2*>(planes + (size_t)d * Kp + 8 * (size_t)i) = make_uint2(dw[d][0], dw[d][1]);
+                    *reinterpret_cast<uint2*>(planes + (size_t)d * (Kp + 16) + 8 * (size_t)i) =
+                        make_uint2(dw[d][0], dw[d][1]);   // planes Kpad + 16 apart: no bank conflicts between them
             }
 #pragma unroll
             for (int d = 0; d < 3; ++d)

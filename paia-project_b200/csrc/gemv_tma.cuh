@@ -127,15 +127,16 @@ template <int F>
 __host__ __device__ constexpr int tma_meta_bytes(int cs) {
     return 112 + ((F == kINT4 || F == kINT4A) ? 16 * tma_meta_row(cs) * 2 * (F == kINT4A ? 2 : 1) : 0);
 }
-// INT4 per-group sums in shared memory: 8 words per group for the integer path (four digit sums and sum x), else 2.
+// INT4 per-group sums in shared memory: 8 words per group for the integer path (digit sums and sum x), else 2.
 __host__ __device__ constexpr int tma_gsum_words(int dec) { return dec == 2 ? 8 : 2; }
 // Tile-partial buffers: consumers run at most ring - 1 stages ahead of the slowest, i.e. ceil((ring - 1) / NCH) + 1
 // tiles; one more lets the epilogue warp lag a tile before a consumer waits for a free buffer.
 __host__ __device__ constexpr int tma_part_bufs(int ring, int nch) { return (ring - 1 + nch - 1) / nch + 2; }
 
-// Shared-memory layout (bytes): [0,640) mbarriers; ring x st_bytes; metadata ring x
-// tma_meta_bytes (16-byte multiples); x Kpad x 2 (INT4 integer path: Kpad x 3); INT4 group sums 8 words per group; tile partials
-// NB x NC x 16 floats; x scale 16 bytes.
+// Shared-memory layout (bytes): [0,640) mbarriers; ring x st_bytes; metadata ring x tma_meta_bytes (16-byte
+// multiples); x: Kpad x 2 (INT4 integer path: Kpad x 3) + 64 (FP8 lo plane at Kpad + 64, INT4 planes Kpad + 16
+// apart); INT4 group sums
+// (tma_gsum_words per group); tile partials NB x NC x 16 floats; x scale 16 bytes.
 template <int F, int NC, int DEC>
 __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int kc, int st_bytes) {
     const int kp = mma_kpad<F>(K);
@@ -143,7 +144,7 @@ __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int k
     const int nb = tma_part_bufs(ring < 2 ? 2 : ring, nch);
     // x: 2 bytes per element (3 for the INT4 integer path's digit planes)
     constexpr size_t xb = ((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2;
-    return kTmaBarBytes + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * xb +
+    return kTmaBarBytes + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * xb + 64 +
            ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * tma_gsum_words(DEC) * 4 : 0) + (size_t)nb * NC * 16 * 4 + 16;
 }
 
@@ -234,7 +235,7 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
         // 1 (lo): lanes of group g = 1 supply B column 1, all others column 0's hi bytes, so one mma.sync per 32
         // weights and row yields both dot products (columns 2-7 repeat hi and are never read).
         const int grp = (int)(threadIdx.x & 31) >> 2;
-        const uint8_t* xb8 = reinterpret_cast<const uint8_t*>(xs) + (size_t)gs * 64 + 16 * c + (grp == 1 ? xlo_off : 0);
+        const uint8_t* xb8 = reinterpret_cast<const uint8_t*>(xs) + (size_t)gs * 64 + 16 * c + (grp == 1 ? xlo_off + 48 : 0);
         uint4 xv[NU];
 #pragma unroll
         for (int u = 0; u < NU; ++u) xv[u] = *reinterpret_cast<const uint4*>(xb8 + 64 * u);
@@ -272,7 +273,8 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
         // and one m16n8k32 yields the three exact digit dot products of 32 weights of 16 rows. Per group:
         // sum_d (D_d - 8 S_d) 128^d, lanes c = 0 / 1 holding digits 0-1 / 2 (column 3 and c = 2, 3 are unused).
         const int grp = (int)(threadIdx.x & 31) >> 2;
-        const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp < 3 ? grp : 0) * xlo_off +
+        // (lanes of group 3, an unused column, read plane 1 so that no quarter-warp meets a bank twice)
+        const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp < 3 ? grp : 1) * xlo_off +
                             (size_t)gs * 128 + 32 * c;
         const int* gi = reinterpret_cast<const int*>(gsum);
         const float flo = c == 0 ? 1.f : (c == 1 ? 16384.f : 0.f);
@@ -376,7 +378,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
     uint8_t* ring = smem + kTmaBarBytes;
     uint8_t* meta = ring + (size_t)ST * p.st_bytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(meta + (size_t)ST * MB);
-    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)Kp * ((I4 && DEC == 2) ? 3 : 2));
+    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)Kp * ((I4 && DEC == 2) ? 3 : 2) + 64);
     constexpr int GW = tma_gsum_words(DEC);
     float* part = gsum + (I4 ? GW * (Kp / 128) : 0);
     float* xscale = part + (size_t)NB * NC * 16;
@@ -571,11 +573,11 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
         int sl = sa0;
 #pragma unroll 2
         for (; sl + U <= sfull; sl += U)
-            tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp);
+            tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp + 16);
         for (; sl < sfull; ++sl)
-            tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp);
+            tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp + 16);
         for (; sl < sb0; ++sl)                                // the ragged last step of the row
-            tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp);
+            tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp + 16);
 
         if (last) {
             // tile end: this warp's partial sums of rows g, g + 8 -> buffer b for the epilogue warp
