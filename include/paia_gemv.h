@@ -56,6 +56,14 @@ int paia_gemv_int4_naive(const void* Wq, const void* scales, const void* x, void
 int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, void* y, void* scratch_bf16, int N, int K,
                            void* stream);
 
+/* No reference counterpart. paia_gemv_int4_unfused with library-owned scratch: the bf16 dequantised weights go to a
+ * file-scope device array of 16 Mi elements (32 MiB), so the call allocates nothing. N * K above 16777216 (e.g. more
+ * than 4096 x 4096) returns -2; other checks and codes as paia_gemv_int4_unfused (a >0 cudaError_t also when the
+ * array's address cannot be looked up). Overlapping calls (two streams or threads) share the array and race; make
+ * the first call on each device before any stream capture (it looks the address up with a runtime call). */
+int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
+                                  void* stream);
+
 /* ---- B200 additions (no reference kernel; the reference's survey of this path proposes them) ---- */
 
 /* Library identification string. */

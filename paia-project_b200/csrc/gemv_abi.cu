@@ -282,6 +282,37 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
     return paia_gemv_bf16(scratch_bf16, x, y, N, K, default_bf16_variant(), stream);
 }
 
+// Unfused INT4 with library-owned scratch. The scratch is a file-scope device array (module-load storage, not an
+// allocation in this call); its device address is looked up once per device with cudaGetSymbolAddress. Calls that
+// overlap in time (two streams, or two host threads) share the array and race; the first call on a device should
+// come before any stream capture, since the lookup is a host-side runtime call.
+namespace {
+constexpr size_t kStaticScratchElems = (size_t)16 << 20;       // 16 Mi bf16 = 32 MiB (e.g. N x K = 4096 x 4096)
+static __device__ __align__(256) __nv_bfloat16 g_static_scratch[kStaticScratchElems];
+void* g_static_scratch_addr[kMaxDev];
+}  // namespace
+
+int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
+                                  void* stream) {
+    if (N <= 0 || K <= 0 || (size_t)N * (size_t)K > kStaticScratchElems) return -2;   // too big for the scratch
+    const int d = cur_dev();
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_static_scratch_addr[d]) {
+            void* a = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&a, g_static_scratch);
+            if (e != cudaSuccess || !a) {
+                (void)cudaGetLastError();
+                return e != cudaSuccess ? (int)e : (int)cudaErrorInvalidSymbol;
+            }
+            g_static_scratch_addr[d] = a;
+        }
+        scratch = g_static_scratch_addr[d];
+    }
+    return paia_gemv_int4_unfused(Wq, scales, x, y, scratch, N, K, stream);
+}
+
 // ------------------------------------------------------------------ B200 additions
 
 const char* paia_gemv_version(void) { return "paia-gemv-b200 1.0 (sm_100a)"; }

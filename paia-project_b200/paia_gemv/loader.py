@@ -62,6 +62,8 @@ class GemvLib:
         lib.paia_gemv_int4_naive.argtypes = [P, P, P, P, I, I, P]
         lib.paia_gemv_int4_unfused.restype = I
         lib.paia_gemv_int4_unfused.argtypes = [P, P, P, P, P, I, I, P]
+        lib.paia_gemv_int4_unfused_static.restype = I
+        lib.paia_gemv_int4_unfused_static.argtypes = [P, P, P, P, I, I, P]
         # --- B200 additions
         lib.paia_gemv_int4_asym.restype = I
         lib.paia_gemv_int4_asym.argtypes = [P, P, P, P, P, I, I, I, P]
@@ -130,6 +132,17 @@ class GemvLib:
     def int4_naive(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, stream=None):
         self._check(self._lib.paia_gemv_int4_naive(Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, self._st(stream)),
                     "paia_gemv_int4_naive")
+
+    STATIC_SCRATCH_ELEMS = 16 << 20
+
+    def int4_unfused_static(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, stream=None):
+        """int4_unfused with the library's own 32 MiB scratch (no allocation per call). N * K must not exceed 16 Mi;
+        concurrent calls race on the shared scratch."""
+        if N * K > self.STATIC_SCRATCH_ELEMS:
+            raise RuntimeError(f"paia_gemv_int4_unfused_static: N*K = {N * K} exceeds the static scratch of "
+                               f"{self.STATIC_SCRATCH_ELEMS} elements; use int4_unfused with a caller scratch")
+        self._check(self._lib.paia_gemv_int4_unfused_static(Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, self._st(stream)),
+                    "paia_gemv_int4_unfused_static")
 
     def int4_unfused(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, scratch_ptr, N, K, stream=None):
         self._check(self._lib.paia_gemv_int4_unfused(Wq_ptr, scales_ptr, x_ptr, y_ptr, scratch_ptr, N, K,
