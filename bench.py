@@ -655,6 +655,58 @@ def run_sweep(args):
     return 0
 
 
+def run_families(args):
+    """Per real shape and format: GB/s of each kernel family (TMA-fed tensor-core, register-fed tensor-core,
+    CUDA-core instance of the default tuple) through paia_gemv_launch_ex, graph mode over L2-rotated copies. The table
+    behind the default path's per-shape choice."""
+    import ctypes
+    import itertools
+    import torch
+    from paia_gemv import load_lib, synthetic, timing
+    lib = load_lib()
+    f = lib._lib.paia_gemv_launch_ex
+    P = ctypes.c_void_p
+    f.argtypes = [ctypes.c_int] * 8 + [P] * 6 + [ctypes.c_int, ctypes.c_int, P]
+    f.restype = ctypes.c_int
+    kid = {"bf16": 0, "fp8": 1, "int4": 2, "int4_asym": 3}
+    dflt = {"bf16": (2, 4, 4), "fp8": (2, 2, 4), "int4": (4, 2, 4), "int4_asym": (4, 2, 4)}
+    tma_math = {"bf16": 5, "fp8": 8, "int4": 7, "int4_asym": 7}
+    shapes = sorted({s for m in synthetic.SHAPES.values() for s in m.values()})
+    g = torch.Generator(device="cuda").manual_seed(0)
+    l2 = timing.l2_bytes()
+    for kind in args.kinds.split(","):
+        for (N, K) in shapes:
+            first = Gemv(lib, kind, N, K, g, "cmp", random_codes=True)
+            n = timing.plan_rotation(first.weight_bytes(), l2)
+            copies = [first] + [Gemv(lib, kind, N, K, g, "cmp", random_codes=True) for _ in range(n - 1)]
+            xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in range(n)]
+            ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in range(n)]
+            R, U, W = dflt[kind]
+            cfgs = [("tma", 0, 2, 8, tma_math[kind])] + ([("tma_m5", 0, 2, 8, 5)] if kind.startswith("int4") else [])
+            cfgs += [(f"mma2_U{u}W{w}", 1, u, w, 2) for u, w in itertools.product((2, 4), (8, 16))]
+            cfgs += [("core_m0", R, U, W, 0), ("core_m1", R, U, W, 1)]
+            for name, r_, u_, w_, m in cfgs:
+                def mk(i, r_=r_, u_=u_, w_=w_, m=m):
+                    c = copies[i]
+                    a = (kid[kind], r_, u_, w_, m, 1, 0, 0, P(c.W.data_ptr()),
+                         P(c.s.data_ptr() if c.s is not None else 0), P(c.z.data_ptr() if c.z is not None else 0),
+                         P(xs[i].data_ptr()), None, P(ys[i].data_ptr()), N, K)
+                    return lambda: f(*a, P(torch.cuda.current_stream().cuda_stream))
+                calls = [mk(i) for i in range(n)]
+                rc = calls[0]()
+                torch.cuda.synchronize()
+                rec = {"kind": kind, "N": N, "K": K, "cfg": name}
+                if rc:
+                    rec["rc"] = rc
+                else:
+                    us = timing.median(timing.time_graph(calls, samples=7, target_ms=1.0))
+                    rec.update(us=round(us, 3), GBps=round(first.weight_bytes() / us / 1e3, 1))
+                print(json.dumps(rec), flush=True)
+            del copies, xs, ys, first
+            torch.cuda.empty_cache()
+    return 0
+
+
 def run_one(args):
     """A few launches of one shape through the default path (the C ABI call a user makes), for profilers: no timing."""
     import torch
@@ -687,6 +739,7 @@ def main():
     ap.add_argument("--kinds", default="bf16,fp8,int4,int4_asym")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--one", default=None, help="profiling aid: KIND:NxK, e.g. fp8:28672x4096 (default variant)")
+    ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -700,6 +753,8 @@ def main():
         return run_sweep(args)
     if args.one:
         return run_one(args)
+    if args.families:
+        return run_families(args)
     return run_main(args, rank, world, local_rank)
 
 
