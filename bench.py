@@ -707,6 +707,94 @@ def run_families(args):
     return 0
 
 
+def run_tp(args, rank, world, local_rank):
+    """row-sharded TP GEMV over the ranks of this launch (torchrun, one process per GPU). For
+    Llama-3.1-8B lm_head 128256x4096 and gate_up 28672x4096 in FP8 W8A16 and INT4 (asymmetric) g128: per-call device
+    time of the fused path (peer-store epilogue + bounded arrival wait) and of the NCCL all-gather baseline, CUDA
+    events around a CUDA graph (fused) or an eager loop (NCCL) over L2-rotated weight shards, max over ranks. One
+    JSON line per shape, format and path; GB/s = full weight bytes / time."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from paia_gemv import load_lib, synthetic, timing, tp
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29541")
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    lib = load_lib()
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    l2 = timing.l2_bytes()
+    out = []
+    for kind in ("fp8", "int4_asym"):
+        for name in ("lm_head", "gate_up_fused"):
+            N, K = synthetic.SHAPES["llama31_8b"][name]
+            r0, r1 = tp.shard_rows(N, world, rank)
+            nl = r1 - r0
+            first = Gemv(lib, kind, nl, K, g, name, random_codes=True)
+            n = timing.plan_rotation(first.weight_bytes(), l2)
+            shards = [first] + [Gemv(lib, kind, nl, K, g, name, random_codes=True) for _ in range(n - 1)]
+            bufs = tp.TpBuffers(lib, N, torch.device("cuda", local_rank))
+            sg = [tp.ShardedGemv(lib, kind, c.W, c.s, c.z, None, N, K, buffers=bufs) for c in shards]
+            gx = torch.Generator(device="cuda").manual_seed(7)                 # x is replicated
+            x = torch.randn(K, device="cuda", generator=gx).to(torch.bfloat16)
+            full_bytes = first.weight_bytes() * world
+            reps = max(n, 64 // n * n)
+
+            def fused_round():
+                for c in sg:
+                    c.fused(x)
+            # correctness on this rank: fused y == NCCL y, bit for bit, for the first shard
+            yf = sg[0].fused(x).clone()
+            yn = sg[0].nccl(x).clone()
+            torch.cuda.synchronize()
+            same = bool(torch.equal(yf.view(torch.int16), yn.view(torch.int16)))
+            graph = capture(fused_round)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps // n):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us_fused = e0.elapsed_time(e1) * 1e3 / (reps // n * n)
+            dist.barrier()
+            for i in range(2 * n):
+                sg[i % n].nccl(x)
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0.record()
+            for i in range(reps):
+                sg[i % n].nccl(x)
+            e1.record()
+            torch.cuda.synchronize()
+            us_nccl = e0.elapsed_time(e1) * 1e3 / reps
+            t = torch.tensor([us_fused, us_nccl, 0.0 if same else 1.0], device="cuda")
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            err = lib.device_error(1)
+            del graph
+            bufs.close()
+            if rank == 0:
+                for path, us in (("fused_peer_store", t[0].item()), ("nccl_all_gather", t[1].item())):
+                    out.append({"config": "tp_row_sharded", "kind": kind, "layer": name, "N": N, "K": K,
+                                "n_gpus": world, "rows_per_rank": nl, "path": path, "us": round(us, 3),
+                                "GBps": round(full_bytes / us / 1e3, 1), "fused_equals_nccl": t[2].item() == 0.0,
+                                "device_error": err, "timing": "max over ranks, CUDA events, rotated shards"})
+                    print(json.dumps(out[-1]), flush=True)
+            del sg, shards, first
+            torch.cuda.empty_cache()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_one(args):
     """A few launches of one shape through the default path (the C ABI call a user makes), for profilers: no timing."""
     import torch
@@ -740,6 +828,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--one", default=None, help="profiling aid: KIND:NxK, e.g. fp8:28672x4096 (default variant)")
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
+    ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
     ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -755,6 +844,8 @@ def main():
         return run_one(args)
     if args.families:
         return run_families(args)
+    if args.tp:
+        return run_tp(args, rank, world, local_rank)
     return run_main(args, rank, world, local_rank)
 
 

@@ -27,6 +27,8 @@
 #ifndef PAIA_GEMV_H
 #define PAIA_GEMV_H
 
+#include <stddef.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -63,6 +65,31 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
  * the first call on each device before any stream capture (it looks the address up with a runtime call). */
 int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
                                   void* stream);
+
+/* ---- Row-sharded tensor parallelism (no reference kernel; BASELINE config 5, survey row 8e) ----
+ * Rank `rank` of `world` (<= 8) holds rows [rank N_local, (rank+1) N_local) of W (and their scales/zeros/bias) and
+ * computes them with the TMA-fed kernel, storing every output to every rank's full-size y (world * N_local bf16;
+ * y_all[r] = rank r's buffer as mapped in this process, e.g. through CUDA IPC) at rank * N_local + row. Each CTA then
+ * adds 1 to every rank's arrival counter (flag_all[r] = &counters_r[0], counters_r two zero-initialised uint32 in
+ * rank r's memory, 8-byte aligned) with system-scope atomics. paia_gemv_tp_ctas gives the CTAs per launch (each
+ * launch adds per_call = world * ctas to every counter); paia_gemv_tp_wait advances the local call epoch
+ * (counters[1], in device memory, so captured CUDA graphs stay correct) and makes the stream wait until
+ * counters[0] reaches epoch * per_call (wrap-safe compare), giving up after ~1 s with error code 6 in
+ * paia_gemv_device_error(). Same argument checks and codes as the per-format calls; -2 also for a bad
+ * world/rank/pointer or a shape the TMA kernel cannot stage. */
+int paia_gemv_tp(int kind, const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                 void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
+                 void* stream);
+int paia_gemv_tp_ctas(int kind, int N_local, int K);
+/* Setup of the buffers other ranks map: a zero-filled device allocation (cudaMalloc), its 64-byte CUDA IPC handle,
+ * and the mapping of a peer's handle in this process (usable from kernels on the current device; peer access is
+ * enabled lazily). Codes: 0, -2 bad argument, >0 cudaError_t. Not for use inside a captured stream. */
+int paia_gemv_tp_alloc(size_t bytes, void** ptr);
+int paia_gemv_tp_free(void* ptr);
+int paia_gemv_ipc_handle(const void* ptr, void* handle64);
+int paia_gemv_ipc_open(const void* handle64, void** ptr);
+int paia_gemv_ipc_close(void* ptr);
+int paia_gemv_tp_wait(unsigned int* counters, unsigned int per_call, void* stream);
 
 /* ---- B200 additions (no reference kernel; the reference's survey of this path proposes them) ---- */
 

@@ -8,6 +8,7 @@
 // (CUDA-graph capturable). Its only static state is a per-device cache of SM counts and occupancies.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 #include "gemv_launch.cuh"
@@ -251,6 +252,51 @@ int default_bf16_variant() {   // (R, U, W, S, H) = (2, 4, 4, 0, 1), looked up b
 __device__ int g_device_error;   // written only by kernels whose bounded waits gave up (tensor-parallel path)
 }  // namespace
 
+namespace pb2tp {   // tensor-parallel helpers (named, outside the C linkage block: they hold a kernel)
+// The TMA-fed kernel every TP launch uses (the only one with the peer-store epilogue): the format's default decode.
+const Variant* tp_instance(int fmt, const Params& p, Variant* out) {
+    static const int maths[4][2] = {{5, 0}, {8, 0}, {7, 5}, {7, 5}};
+    for (int k = 0; k < 2; ++k) {
+        const int math = maths[fmt][k];
+        if (!math) break;
+        const Variant* inst = find_instance(fmt, 0, 2, 8, math);
+        if (!inst) continue;
+        long long G = 0;
+        *out = *inst;
+        out->H = 1;
+        const LaunchOpts o{0, 0};
+        if (launch_variant(*out, p, o, nullptr, &G) == 0) return out;
+    }
+    return nullptr;
+}
+
+// One thread advances this rank's call epoch (counters[1]) and waits (bounded, ~1 s) until the arrival counter
+// (counters[0], incremented by every rank's CTAs) reaches epoch * per_call (wrap-safe); on timeout it records error
+// code 6 and returns, so the host reads an error instead of a hang. The epoch lives in device memory, so a captured
+// CUDA graph of TP calls stays correct on every replay.
+__global__ void tp_wait_kernel(unsigned int* counters, unsigned int per_call) {
+    if (threadIdx.x != 0) return;
+    const unsigned int epoch = counters[1] + 1u;
+    counters[1] = epoch;
+    const unsigned int expected = epoch * per_call;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counters) : "memory");
+        if ((int)(v - expected) >= 0) return;
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 1000000000ull) {
+            atomicCAS(&g_device_error, 0, 6);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+}  // namespace pb2tp
+
+
 extern "C" {
 
 // ------------------------------------------------------------------ the reference's ABI
@@ -328,6 +374,102 @@ int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void
         scratch = g_static_scratch_addr[d];
     }
     return paia_gemv_int4_unfused(Wq, scales, x, y, scratch, N, K, stream);
+}
+
+// ------------------------------------------------------------------ row-sharded tensor parallelism
+
+int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const void* x, const void* bias,
+                 void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
+                 void* stream) {
+    if (kind < 0 || kind > 3 || world < 1 || world > 8 || rank < 0 || rank >= world || !y_all || !flag_all) return -2;
+    for (int r = 0; r < world; ++r)
+        if (!y_all[r] || !flag_all[r] || !aligned(y_all[r], 2) || !aligned(flag_all[r], 4)) return -2;
+    const int rc = check_args(kind, Wq, s, z, x, bias, y_all[rank], N_local, K);
+    if (rc) return rc;
+    Params p{};
+    p.W = static_cast<const uint8_t*>(Wq);
+    p.s = s;
+    p.z = z;
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.bias = static_cast<const __nv_bfloat16*>(bias);
+    p.y = static_cast<__nv_bfloat16*>(y_all[rank]) + (size_t)rank * N_local;
+    p.N = N_local;
+    p.K = K;
+    p.nchunk = row_bytes(kind, K) / 16;
+    p.groups = K / 128;
+    p.tp_world = world;
+    p.tp_off = rank * N_local;
+    for (int r = 0; r < world; ++r) {
+        p.tp_y[r] = static_cast<__nv_bfloat16*>(y_all[r]);
+        p.tp_flag[r] = flag_all[r];
+    }
+    Variant v;
+    if (!pb2tp::tp_instance(kind, p, &v)) return -2;
+    const LaunchOpts o{0, 0};
+    return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));
+}
+
+// Buffers that other ranks map (full-size y and the arrival counters): plain device allocations, so that their
+// CUDA IPC handles name exactly these bytes; zero-filled. Setup-time calls, never inside a GEMV.
+int paia_gemv_tp_alloc(size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return -2;
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    return 0;
+}
+int paia_gemv_tp_free(void* ptr) {
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    return 0;
+}
+// 64-byte CUDA IPC handle of a paia_gemv_tp_alloc buffer, and its mapping in another process (peer access enabled
+// lazily by the driver: the mapped pointer is usable from kernels on the calling process's current device).
+int paia_gemv_ipc_handle(const void* ptr, void* handle64) {
+    if (!ptr || !handle64) return -2;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    memcpy(handle64, &h, sizeof(h));
+    return 0;
+}
+int paia_gemv_ipc_open(const void* handle64, void** ptr) {
+    if (!handle64 || !ptr) return -2;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    *ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    return 0;
+}
+int paia_gemv_ipc_close(void* ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    return 0;
+}
+
+int paia_gemv_tp_ctas(int kind, int N_local, int K) {
+    if (kind < 0 || kind > 3 || N_local <= 0 || K <= 0) return -2;
+    Params p{};
+    p.N = N_local;
+    p.K = K;
+    p.nchunk = row_bytes(kind, K) / 16;
+    p.groups = K / 128;
+    Variant v;
+    if (!pb2tp::tp_instance(kind, p, &v)) return -2;
+    long long G = 0;
+    const LaunchOpts o{0, 0};
+    if (launch_variant(v, p, o, nullptr, &G)) return -2;
+    return (int)G;
+}
+
+int paia_gemv_tp_wait(unsigned int* counters, unsigned int per_call, void* stream) {
+    if (!counters || !aligned(counters, 8) || per_call == 0) return -2;
+    pb2tp::tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counters, per_call);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : (int)e;
 }
 
 // ------------------------------------------------------------------ B200 additions

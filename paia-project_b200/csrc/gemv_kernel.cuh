@@ -58,6 +58,12 @@ struct Params {
     int kc, nch, rs, st_bytes;     // TMA kernels: bytes per row per stage, stages per tile, smem row stride, stage size
     int ring;                      // TMA kernels: stages in the shared-memory ring
     int pre;                       // TMA kernels: stages streamed before x is staged (0 = the whole ring)
+    // Row-sharded tensor parallelism (TMA kernels; tp_world = 0: off). This rank computes rows [0, N) of its shard and
+    // stores each output to every rank's full-size y (peer memory over NVLink) at tp_off + row; when a CTA is done
+    // it adds 1 to every rank's arrival counter (system-scope atomics), which paia_gemv_tp_wait waits on.
+    int tp_world, tp_off;
+    __nv_bfloat16* tp_y[8];
+    unsigned int* tp_flag[8];
 };
 
 template <int F> struct Elems;     // weights per 16-byte chunk

@@ -57,7 +57,8 @@ inline int choose_ks(int nchunk, int rows_per_cta, int W, int R, int U) {
     return ks < cap ? ks : cap;
 }
 
-inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaStream_t st) {
+// grid_out != nullptr: plan only (no launch) and return the grid size in *grid_out.
+inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaStream_t st, long long* grid_out = nullptr) {
     size_t smem;
     if (v.prep) {
         const int share = o.share > 0 ? o.share : 1;
@@ -88,6 +89,10 @@ inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaS
     }
     p.ks_log2 = ilog2(ks);
 
+    if (grid_out) {
+        *grid_out = G;
+        return 0;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)G);
     cfg.blockDim = dim3((unsigned)threads);

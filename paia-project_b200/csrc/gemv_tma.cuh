@@ -506,11 +506,25 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
                     out = out * __uint_as_float((uint32_t)(__float_as_int(xscale[0]) + 127) << 23);
                 if constexpr (I4 && DEC == 2)                 // x was staged as integers x * 2^s
                     out = out * xscale[1];
-                p.y[row] = __float2bfloat16_rn(out + rbias);
+                const __nv_bfloat16 v = __float2bfloat16_rn(out + rbias);
+                if (p.tp_world == 0) {
+                    p.y[row] = v;
+                } else {
+                    for (int r = 0; r < p.tp_world; ++r) p.tp_y[r][p.tp_off + row] = v;   // peer stores
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfree[b]);
             if (++b == NB) { b = 0; bph ^= 1u; }
+        }
+        if (p.tp_world > 0) {
+            // this CTA's outputs are on every rank: make them visible system-wide, then count the CTA in everywhere
+            __threadfence_system();
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_system();
+                for (int r = 0; r < p.tp_world; ++r) atomicAdd_system(p.tp_flag[r], 1u);
+            }
         }
         return;
     }

@@ -64,6 +64,24 @@ class GemvLib:
         lib.paia_gemv_int4_unfused.argtypes = [P, P, P, P, P, I, I, P]
         lib.paia_gemv_int4_unfused_static.restype = I
         lib.paia_gemv_int4_unfused_static.argtypes = [P, P, P, P, I, I, P]
+        lib.paia_gemv_launch_ex.restype = I
+        lib.paia_gemv_launch_ex.argtypes = [I] * 8 + [P] * 6 + [I, I, P]
+        lib.paia_gemv_tp.restype = I
+        lib.paia_gemv_tp.argtypes = [I, P, P, P, P, P, ctypes.POINTER(P), ctypes.POINTER(P), I, I, I, I, P]
+        lib.paia_gemv_tp_ctas.restype = I
+        lib.paia_gemv_tp_ctas.argtypes = [I, I, I]
+        lib.paia_gemv_tp_alloc.restype = I
+        lib.paia_gemv_tp_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(P)]
+        lib.paia_gemv_tp_free.restype = I
+        lib.paia_gemv_tp_free.argtypes = [P]
+        lib.paia_gemv_ipc_handle.restype = I
+        lib.paia_gemv_ipc_handle.argtypes = [P, ctypes.c_char_p]
+        lib.paia_gemv_ipc_open.restype = I
+        lib.paia_gemv_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(P)]
+        lib.paia_gemv_ipc_close.restype = I
+        lib.paia_gemv_ipc_close.argtypes = [P]
+        lib.paia_gemv_tp_wait.restype = I
+        lib.paia_gemv_tp_wait.argtypes = [P, ctypes.c_uint, P]
         # --- B200 additions
         lib.paia_gemv_int4_asym.restype = I
         lib.paia_gemv_int4_asym.argtypes = [P, P, P, P, P, I, I, I, P]
@@ -182,6 +200,51 @@ class GemvLib:
         out = VariantEx()
         self._check(self._lib.paia_gemv_variant_info_ex(_KINDS[kind], v, ctypes.byref(out)), "paia_gemv_variant_info_ex")
         return {f: getattr(out, f) for f in _EX_FIELDS}
+
+    def launch_ex(self, kind, R, U, W, math, pdl, ks, ctas_per_sm, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr,
+                  y_ptr, N, K, stream=None):
+        """Any compiled kernel instance (tuning and comparisons): math 0/1 CUDA-core, 2-4 register-fed MMA, 5-8
+        TMA-fed MMA (R = ring stages, 0 = auto; ks = shared-memory share | stages-before-x << 8)."""
+        self._check(self._lib.paia_gemv_launch_ex(_KINDS[kind], R, U, W, math, pdl, ks, ctas_per_sm, Wq_ptr,
+                                                  scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K,
+                                                  self._st(stream)), "paia_gemv_launch_ex")
+
+    # --- row-sharded tensor parallelism (paia_gemv.tp drives these)
+    def tp(self, kind, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptrs, flag_ptrs, world, rank, N_local, K,
+           stream=None):
+        self._check(self._lib.paia_gemv_tp(_KINDS[kind], Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptrs,
+                                           flag_ptrs, world, rank, N_local, K, self._st(stream)), "paia_gemv_tp")
+
+    def tp_ctas(self, kind, N_local, K):
+        n = self._lib.paia_gemv_tp_ctas(_KINDS[kind], N_local, K)
+        if n <= 0:
+            raise RuntimeError(f"paia_gemv_tp_ctas failed with code {n} ({kind} {N_local}x{K})")
+        return n
+
+    def tp_alloc(self, nbytes):
+        p = ctypes.c_void_p()
+        self._check(self._lib.paia_gemv_tp_alloc(nbytes, ctypes.byref(p)), "paia_gemv_tp_alloc")
+        return p.value
+
+    def tp_free(self, ptr):
+        self._check(self._lib.paia_gemv_tp_free(ptr), "paia_gemv_tp_free")
+
+    def ipc_handle(self, ptr):
+        buf = ctypes.create_string_buffer(64)
+        self._check(self._lib.paia_gemv_ipc_handle(ptr, buf), "paia_gemv_ipc_handle")
+        return buf.raw
+
+    def ipc_open(self, handle):
+        p = ctypes.c_void_p()
+        self._check(self._lib.paia_gemv_ipc_open(bytes(handle), ctypes.byref(p)), "paia_gemv_ipc_open")
+        return p.value
+
+    def ipc_close(self, ptr):
+        self._check(self._lib.paia_gemv_ipc_close(ptr), "paia_gemv_ipc_close")
+
+    def tp_wait(self, counters_ptr, per_call, stream=None):
+        self._check(self._lib.paia_gemv_tp_wait(counters_ptr, per_call & 0xFFFFFFFF, self._st(stream)),
+                    "paia_gemv_tp_wait")
 
     def device_error(self, clear=True):
         """The device-side error word (0 = none) written by kernels whose bounded waits gave up."""

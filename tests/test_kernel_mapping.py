@@ -296,7 +296,7 @@ def tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec=0):
     kp = (K + SK - 1) // SK * SK
     nb = tma_part_bufs(max(ring, 2), nch)
     i4 = fmt.startswith("int4")
-    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * (3 if i4 and dec == 2 else 2)
+    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * (3 if i4 and dec == 2 else 2) + 64
             + (kp // 128 * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * 4 + 16)
 
 
