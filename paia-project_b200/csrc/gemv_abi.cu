@@ -172,26 +172,17 @@ bool is_default_tuple(int fmt, const Variant& v) {
 }
 
 // B200 path behind the default tuples, chosen per shape from the kernel-family comparison on B200 (every real
-// Llama-3.1-8B / Qwen2.5-7B shape, each format; summary in profiles/gemv_kernel_family_compare_b200.md):
+// Llama-3.1-8B / Qwen2.5-7B shape, each format, alone and in decode-layer chains; profiles/
+// gemv_kernel_family_compare_b200.md):
 //   * N <= 1024 (k/v projections): the tuple's own CUDA-core instance (it splits K across warps; 16-row tiles leave
 //     most SMs with a single partial tile) - signalled by returning -2;
-//   * INT4 with K >= 8192, or with K/128 not a multiple of 8 and N >= 16384: the register-fed tensor-core kernel
-//     (gemv_mma.cuh, 2 steps in flight, 8 warps): x staging and per-row scale copies cost the TMA path more there;
 //   * otherwise the TMA-fed tensor-core kernel with the decode measured fastest (BF16 as is, FP8 e4m3 straight into
 //     e4m3 MMA, INT4 through the integer MMA; 8 consumer warps, 2 steps per iteration, as deep a ring as fits).
+//     (Alone, the register-fed kernel wins a few long-K INT4 shapes by up to 15%; inside the chained decode layer,
+//     which is how the op runs, the TMA kernel is faster for every INT4 layer sequence measured.)
 // Returns -2 when the chosen kernel cannot stage the shape (the caller then runs the tuple's own instance).
 int launch_b200_default(int fmt, const Params& p, cudaStream_t st) {
     if (p.N <= 1024) return -2;
-    if ((fmt == kINT4 || fmt == kINT4A) && (p.K >= 8192 || (p.groups % 8 != 0 && p.N >= 16384))) {
-        const Variant* inst = find_instance(fmt, 1, 2, 8, 2);
-        if (inst) {
-            Variant v = *inst;
-            v.H = 1;
-            const LaunchOpts o{0, 0};
-            const int rc = launch_variant(v, p, o, st);
-            if (rc != -2) return rc;
-        }
-    }
     static const int maths[4][2] = {{5, 0}, {8, 0}, {7, 5}, {7, 5}};   // first choice, then a fallback (0: none)
     for (int k = 0; k < 2; ++k) {
         const int math = maths[fmt][k];
