@@ -167,6 +167,11 @@ class Gemv:
                 n += t.numel() * t.element_size()
         return n
 
+    def op_dict(self, x, y):
+        p = lambda t: None if t is None else t.data_ptr()      # noqa: E731
+        return dict(Wq=p(self.W), scales=p(self.s), zeros=p(self.z), x=p(x), bias=p(self.bias), y=p(y), N=self.N,
+                    K=self.K)
+
     def io_bytes(self):
         return 2 * self.K + 2 * self.N + (2 * self.N if self.bias is not None else 0)
 
@@ -267,6 +272,24 @@ class Layer:
 
     def weight_bytes(self):
         return sum(gm.weight_bytes() for gm in self.gemvs)
+
+    def op_dicts(self):
+        return [gm.op_dict(x, y) for gm, x, y in zip(self.gemvs, self.xs, self.ys)]
+
+    def layer_launcher(self):
+        """A zero-argument function launching this layer's GEMVs as one paia_gemv_layer call (raw ctypes)."""
+        import ctypes
+        import torch
+        from paia_gemv.loader import GemvOp, _KINDS
+        ops = (GemvOp * len(self.gemvs))(*[GemvOp(**d) for d in self.op_dicts()])
+        self.counters = torch.zeros(len(self.gemvs) + 1, dtype=torch.int32, device="cuda")
+        P = ctypes.c_void_p
+        fn, kind, n, c = self.gemvs[0].lib._lib.paia_gemv_layer, _KINDS[self.gemvs[0].kind], len(self.gemvs), \
+            P(self.counters.data_ptr())
+        dev = torch.cuda.current_device()
+        cur = torch._C._cuda_getCurrentRawStream
+        self._ops = ops
+        return lambda: fn(kind, 0, n, ops, c, P(cur(dev)))
 
 
 def capture(fn, warm=1):
@@ -621,37 +644,88 @@ def run_sweep(args):
                 del copies, xs, ys, calls, first
                 torch.cuda.empty_cache()
         for model in ("llama31_8b", "qwen25_7b"):
-            nl = synthetic.N_LAYERS[model]
-            layers = [Layer(lib, kind, model, g, tuned, random_codes=True) for _ in range(nl)]
-            N, K = synthetic.SHAPES[model]["lm_head"]
-            vid, _ = variant_for(lib, kind, N, K, tuned)
-            head = Gemv(lib, kind, N, K, g, "lm_head", variant=vid, random_codes=True)
-            hy = torch.empty(N, device="cuda", dtype=torch.bfloat16)
-            hcall = head.launcher(layers[-1].ys[-1], hy)
+            print(json.dumps(decode_token(lib, kind, model, g, tuned, peak, "per_op")), flush=True)
+    return 0
 
-            def token():
-                for lay in layers:
-                    lay.step()
-                hcall()
 
-            gph = capture(token)
-            for _ in range(3):
-                gph.replay()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = 10
-            e0.record()
-            for _ in range(reps):
-                gph.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
-            tb = sum(l.weight_bytes() for l in layers) + head.weight_bytes()
-            print(json.dumps({"kind": kind, "model": model, "decode_us_per_token": round(us, 2),
-                              "layers": nl, "weight_GB": round(tb / 1e9, 3), "GBps": round(tb / us / 1e3, 1),
-                              "frac_of_peak": round(tb / us / 1e3 / peak, 4)}), flush=True)
-            del layers, head, gph
-            torch.cuda.empty_cache()
+def decode_token(lib, kind, model, g, tuned, peak, mode, reps=10):
+    """µs per token of a model's decode GEMVs (every layer's qkv, o, gate_up, down, chained, then the lm_head; distinct
+    weights per layer), timed as a CUDA graph. mode "per_op": one launch per GEMV with programmatic dependent launch
+    (the reference's per-token sum of per-op launches); "layer": one paia_gemv_layer launch per layer, then the
+    lm_head; "plan": one paia_gemv_plan launch for the whole token."""
+    import torch
+    from paia_gemv import synthetic
+    from paia_gemv.loader import GemvOp
+    nl = synthetic.N_LAYERS[model]
+    layers = [Layer(lib, kind, model, g, tuned, random_codes=True) for _ in range(nl)]
+    N, K = synthetic.SHAPES[model]["lm_head"]
+    vid, _ = variant_for(lib, kind, N, K, tuned)
+    head = Gemv(lib, kind, N, K, g, "lm_head", variant=vid, random_codes=True)
+    hy = torch.empty(N, device="cuda", dtype=torch.bfloat16)
+    hx = layers[-1].ys[-1][:K]
+    plan = None
+    if mode == "per_op":
+        hcall = head.launcher(hx, hy)
+
+        def token():
+            for lay in layers:
+                lay.step()
+            hcall()
+    elif mode == "layer":
+        hcall = head.launcher(hx, hy)
+        calls = [lay.layer_launcher() for lay in layers]
+
+        def token():
+            for c in calls:
+                rc = c()
+                if rc:
+                    raise RuntimeError(f"layer launch failed with code {rc}")
+            hcall()
+    else:
+        ops = [d for lay in layers for d in lay.op_dicts()] + [head.op_dict(hx, hy)]
+        plan = lib.plan_create(kind, ops)
+
+        def token():
+            lib.plan_launch(plan)
+    gph = capture(token)
+    for _ in range(3):
+        gph.replay()
+    torch.cuda.synchronize()
+    err = lib.device_error(True)
+    if err:
+        raise RuntimeError(f"device error {err} in decode_token {kind} {model} {mode}")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    tb = sum(l.weight_bytes() for l in layers) + head.weight_bytes()
+    del gph
+    if plan is not None:
+        lib.plan_destroy(plan)
+    out = {"kind": kind, "model": model, "mode": mode, "decode_us_per_token": round(us, 2), "layers": nl,
+           "weight_GB": round(tb / 1e9, 3), "GBps": round(tb / us / 1e3, 1),
+           "frac_of_peak": round(tb / us / 1e3 / peak, 4)}
+    del layers, head
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_decode(args):
+    """Decode µs/token of both models in each format, per-op launches vs one launch per layer vs one plan per token."""
+    import torch
+    from paia_gemv import load_lib
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    tuned = load_tuned()
+    peak, _ = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    for kind in args.kinds.split(","):
+        for model in ("llama31_8b", "qwen25_7b"):
+            for mode in ("per_op", "layer", "plan"):
+                print(json.dumps(decode_token(lib, kind, model, g, tuned, peak, mode)), flush=True)
     return 0
 
 
@@ -830,6 +904,8 @@ def main():
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
     ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
     ap.add_argument("--launches", type=int, default=4)
+    ap.add_argument("--decode", action="store_true",
+                    help="decode us/token: per-op launches vs one launch per layer vs one plan per token")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -844,6 +920,8 @@ def main():
         return run_one(args)
     if args.families:
         return run_families(args)
+    if args.decode:
+        return run_decode(args)
     if args.tp:
         return run_tp(args, rank, world, local_rank)
     return run_main(args, rank, world, local_rank)

@@ -129,6 +129,39 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
                         const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
                         void* stream);
 
+/* One launch for a sequence of up to 6 GEMVs of one format (a decode layer's projections): a persistent grid, one CTA
+ * per SM, streams the weights of op 0, 1, ... back to back, so op j + 1's weights are already in flight while op j
+ * finishes. Op j's x is read only after every CTA has stored op j - 1's outputs, so x of op j may be the y of any
+ * earlier op; y of op j must not overlap x of op j. Same decode and accuracy as the per-format calls, and the same
+ * bits on every run of the same op list; a separate per-format call may differ in the last bits, because the stage
+ * chunk (and with it the split of a row among warps) is chosen for the whole sequence. math 0 = the format's default decode (bf16 5, fp8 8, int4 / int4_asym 7, falling back to 5), else a TMA math
+ * code of paia_gemv_launch_ex. `counters`: nops + 1 zero-initialised uint32 in device memory, 4-byte aligned,
+ * used by one launch at a time; the kernel leaves them zero. A wait that gives up after ~2 s sets error code 7 in
+ * paia_gemv_device_error(). No reference counterpart (the reference launches one kernel per GEMV,
+ * src/paia_gemv/gemv_quant.cu:61-71). Codes: 0, -2 bad argument / shape the kernel cannot stage, >0 cudaError_t. */
+typedef struct paia_gemv_op {
+    const void* Wq;       /* weights in the format of `kind` */
+    const void* scales;   /* fp8 float row scales, int4 fp16 / int4_asym bf16 group scales; NULL for bf16 */
+    const void* zeros;    /* int4_asym bf16 group zeros; NULL otherwise */
+    const void* x;        /* bf16 [K] */
+    const void* bias;     /* bf16 [N] or NULL */
+    void* y;              /* bf16 [N] */
+    int N, K;
+} paia_gemv_op;
+int paia_gemv_layer(int kind, int math, int nops, const paia_gemv_op* ops, unsigned int* counters, void* stream);
+
+/* A plan: the same persistent launch for a longer sequence (up to 4096 ops, e.g. every GEMV of one decode token:
+ * each layer's projections and the lm_head), its op table and counters in device memory owned by the plan.
+ * paia_gemv_plan_create checks the ops as paia_gemv_layer does, chooses the geometry once, and allocates and fills
+ * the device table (synchronous; not inside a captured stream); paia_gemv_plan_launch is one launch (capturable,
+ * no allocation; launches of one plan must not overlap); paia_gemv_plan_destroy frees it. The plan belongs to the
+ * device that was current at creation. No reference counterpart (its per-token GEMV cost is the sum of one launch
+ * per GEMV over the layers plus the lm_head, paia-bench/bench/analyze_e4.py:177-192). */
+typedef struct paia_gemv_plan paia_gemv_plan;
+int paia_gemv_plan_create(int kind, int math, int nops, const paia_gemv_op* ops, paia_gemv_plan** plan);
+int paia_gemv_plan_launch(const paia_gemv_plan* plan, void* stream);
+int paia_gemv_plan_destroy(paia_gemv_plan* plan);
+
 /* Device-side error word of the current device (0 = none), set by kernels whose bounded waits gave up; clear != 0
  * resets it. Synchronous. */
 int paia_gemv_device_error(int clear);

@@ -11,6 +11,7 @@
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 #include "gemv_launch.cuh"
 #include "paia_gemv.h"
 
@@ -288,6 +289,52 @@ __global__ void tp_wait_kernel(unsigned int* counters, unsigned int per_call) {
 }  // namespace pb2tp
 
 
+namespace {
+// Checks the ops of a layer launch or plan and converts them to kernel descriptors; *maxN = the largest N.
+int fill_ops(int kind, int nops, const paia_gemv_op* ops, pb2::GemvOp* out, int* maxN) {
+    *maxN = 0;
+    for (int j = 0; j < nops; ++j) {
+        const paia_gemv_op& o = ops[j];
+        const int rc = check_args(kind, o.Wq, o.scales, o.zeros, o.x, o.bias, o.y, o.N, o.K);
+        if (rc) return rc;
+        const uintptr_t x0 = (uintptr_t)o.x, x1 = x0 + 2 * (size_t)o.K;
+        const uintptr_t y0 = (uintptr_t)o.y, y1 = y0 + 2 * (size_t)o.N;
+        if (x0 < y1 && y0 < x1) return -2;                   // other CTAs store y while x is still being read
+        GemvOp& g = out[j];
+        g = GemvOp{};
+        g.W = static_cast<const uint8_t*>(o.Wq);
+        g.s = o.scales;
+        g.z = o.zeros;
+        g.x = static_cast<const __nv_bfloat16*>(o.x);
+        g.bias = static_cast<const __nv_bfloat16*>(o.bias);
+        g.y = static_cast<__nv_bfloat16*>(o.y);
+        g.N = o.N;
+        g.K = o.K;
+        g.nchunk = row_bytes(kind, o.K) / 16;
+        g.groups = o.K / 128;
+        *maxN = o.N > *maxN ? o.N : *maxN;
+    }
+    return 0;
+}
+
+// The TMA instance of a layer launch and its geometry: math 0 = the format's default decode (then a fallback when it
+// cannot stage the sequence), one CTA per SM so that every CTA is resident.
+int plan_layer(int kind, int math, Params& p, const Variant** inst_out, Planned* pl) {
+    static const int maths[4][2] = {{5, 0}, {8, 0}, {7, 5}, {7, 5}};
+    const int first = math ? math : maths[kind][0], second = math ? 0 : maths[kind][1];
+    for (int m : {first, second}) {
+        if (m < 5) break;
+        const Variant* inst = find_instance(kind, 0, 2, 8, m);
+        if (!inst) return -2;
+        const LaunchOpts o{0, 1};
+        const int rc = plan_variant(*inst, p, o, pl);
+        if (rc == 0) { *inst_out = inst; return 0; }
+        if (rc != -2) return rc;
+    }
+    return -2;
+}
+}  // namespace
+
 extern "C" {
 
 // ------------------------------------------------------------------ the reference's ABI
@@ -461,6 +508,76 @@ int paia_gemv_tp_wait(unsigned int* counters, unsigned int per_call, void* strea
     pb2tp::tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counters, per_call);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : (int)e;
+}
+
+// ------------------------------------------------------------------ layer launch and plans
+
+
+int paia_gemv_layer(int kind, int math, int nops, const paia_gemv_op* ops, unsigned int* counters, void* stream) {
+    if (kind < 0 || kind > 3 || nops < 1 || nops > kMaxOps || !ops || !counters || !aligned(counters, 4)) return -2;
+    Params p{};
+    p.nops = nops;
+    p.layer_done = counters;
+    const int rc = fill_ops(kind, nops, ops, p.ops, &p.N);
+    if (rc) return rc;
+    const Variant* inst = nullptr;
+    Planned pl;
+    const int prc = plan_layer(kind, math, p, &inst, &pl);
+    if (prc) return prc;
+    return launch_planned(inst->fn, pl, static_cast<cudaStream_t>(stream));
+}
+
+struct paia_gemv_plan {
+    KernelFn fn;
+    Planned pl;
+    void* dev_mem;            // op table, then nops + 1 counters
+};
+
+int paia_gemv_plan_create(int kind, int math, int nops, const paia_gemv_op* ops, paia_gemv_plan** out) {
+    if (!out) return -2;
+    *out = nullptr;
+    if (kind < 0 || kind > 3 || nops < 1 || nops > kMaxPlanOps || !ops) return -2;
+    std::vector<GemvOp> host((size_t)nops);
+    Params p{};
+    p.nops = nops;
+    int rc = fill_ops(kind, nops, ops, host.data(), &p.N);
+    if (rc) return rc;
+    p.host_ops = host.data();
+    const Variant* inst = nullptr;
+    Planned pl;
+    rc = plan_layer(kind, math, p, &inst, &pl);           // also fills every op's stages per row in `host`
+    if (rc) return rc;
+    const size_t table = (size_t)nops * sizeof(GemvOp), ctr = (size_t)(nops + 1) * sizeof(unsigned int);
+    void* mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, table + ctr);
+    if (e == cudaSuccess) e = cudaMemcpy(mem, host.data(), table, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(static_cast<uint8_t*>(mem) + table, 0, ctr);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        if (mem) cudaFree(mem);
+        return (int)e;
+    }
+    paia_gemv_plan* plan = new paia_gemv_plan;
+    plan->fn = inst->fn;
+    plan->pl = pl;
+    plan->pl.p.op_table = static_cast<const GemvOp*>(mem);
+    plan->pl.p.layer_done = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(mem) + table);
+    plan->dev_mem = mem;
+    *out = plan;
+    return 0;
+}
+
+int paia_gemv_plan_launch(const paia_gemv_plan* plan, void* stream) {
+    if (!plan) return -2;
+    return launch_planned(plan->fn, plan->pl, static_cast<cudaStream_t>(stream));
+}
+
+int paia_gemv_plan_destroy(paia_gemv_plan* plan) {
+    if (!plan) return 0;
+    const cudaError_t e = cudaFree(plan->dev_mem);
+    delete plan;
+    if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
+    return 0;
 }
 
 // ------------------------------------------------------------------ B200 additions

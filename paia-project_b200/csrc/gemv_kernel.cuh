@@ -44,6 +44,23 @@ namespace pb2 {
 
 enum : int { kBF16 = 0, kFP8 = 1, kINT4 = 2, kINT4A = 3 };
 
+// Transform applied to x while it is staged (layer mode): none, or SiLU(gate) * up with x = [gate | up], 2K values,
+// each product rounded to bf16 (the activation between a fused gate_up projection and the down projection).
+enum : int { kActNone = 0, kActSiluMul = 1 };
+
+// One GEMV of a fused sequence (TMA kernels' layer mode): operands and shape; nch = stages per 16-row tile.
+struct GemvOp {
+    const uint8_t* W;
+    const void* s;
+    const void* z;
+    const __nv_bfloat16* x;
+    const __nv_bfloat16* bias;
+    __nv_bfloat16* y;
+    int N, K, nchunk, groups, nch, act;
+};
+constexpr int kMaxOps = 6;             // ops carried in the kernel parameters
+constexpr int kMaxPlanOps = 4096;       // ops of a plan (device-memory op table)
+
 struct Params {
     const uint8_t* W;              // [N][rowbytes]
     const void* s;                 // FP8: float[N]; INT4: half[N][G]; INT4A: bf16[N][G]; else unused
@@ -64,6 +81,17 @@ struct Params {
     int tp_world, tp_off;
     __nv_bfloat16* tp_y[8];
     unsigned int* tp_flag[8];
+    // Layer mode (TMA kernels; nops = 0: off, the single GEMV above). One persistent cooperative launch runs ops
+    // 0..nops-1 in order, each op's x being any earlier op's y: the weights of every op stream without a break, and
+    // the consumers of op j wait until every CTA has written op j-1 (layer_done[j-1] == grid size). layer_done holds
+    // nops + 1 zeroed counters; the last CTA to finish zeroes them again for the next launch.
+    // Ops come from `ops` (nops <= kMaxOps) or, for longer sequences (a whole token's GEMVs), from op_table in device
+    // memory; host_ops is the host copy the launch geometry is computed from (host only; ops when null).
+    int nops;
+    unsigned int* layer_done;
+    GemvOp ops[kMaxOps];
+    const GemvOp* op_table;
+    GemvOp* host_ops;
 };
 
 template <int F> struct Elems;     // weights per 16-byte chunk

@@ -57,8 +57,18 @@ inline int choose_ks(int nchunk, int rows_per_cta, int W, int R, int U) {
     return ks < cap ? ks : cap;
 }
 
-// grid_out != nullptr: plan only (no launch) and return the grid size in *grid_out.
-inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaStream_t st, long long* grid_out = nullptr) {
+// A launch with its geometry fixed: the kernel's Params (stage geometry filled in), grid, block and shared memory.
+struct Planned {
+    Params p;
+    size_t smem;
+    long long G;
+    int threads;
+    bool pdl;
+};
+
+// Geometry of a launch of v on the current device: returns 0 and fills `out`, or -2 when the shape cannot run.
+inline int plan_variant(const Variant& v, const Params& p_in, const LaunchOpts& o, Planned* out) {
+    Params p = p_in;
     size_t smem;
     if (v.prep) {
         const int share = o.share > 0 ? o.share : 1;
@@ -88,26 +98,51 @@ inline int launch_variant(const Variant& v, Params p, const LaunchOpts& o, cudaS
         if (ks > v.W || (v.W % ks) != 0 || (ks & (ks - 1)) != 0) return -2;
     }
     p.ks_log2 = ilog2(ks);
+    p.host_ops = nullptr;                                     // host memory: never part of what the kernel sees
+    out->p = p;
+    out->smem = smem;
+    out->G = G;
+    out->threads = threads;
+    out->pdl = v.H != 0;
+    return 0;
+}
 
-    if (grid_out) {
-        *grid_out = G;
-        return 0;
-    }
+// Layer mode (p.nops > 0) launches cooperatively: CTAs wait for every CTA's outputs of the previous op, so all of
+// them must be resident at once. Otherwise programmatic dependent launch when the variant asks for it.
+inline int launch_planned(KernelFn fn, const Planned& pl, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)G);
-    cfg.blockDim = dim3((unsigned)threads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.gridDim = dim3((unsigned)pl.G);
+    cfg.blockDim = dim3((unsigned)pl.threads);
+    cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    if (v.H) {
+    if (pl.p.nops > 0) {
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    } else if (pl.pdl) {
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, v.fn, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, pl.p);
     if (e != cudaSuccess) { (void)cudaGetLastError(); return (int)e; }
     return 0;
+}
+
+// grid_out != nullptr: plan only (no launch) and return the grid size in *grid_out.
+inline int launch_variant(const Variant& v, const Params& p, const LaunchOpts& o, cudaStream_t st,
+                          long long* grid_out = nullptr) {
+    Planned pl;
+    const int rc = plan_variant(v, p, o, &pl);
+    if (rc) return rc;
+    if (grid_out) {
+        *grid_out = pl.G;
+        return 0;
+    }
+    return launch_planned(v.fn, pl, st);
 }
 
 template <int F, int NW, int R>

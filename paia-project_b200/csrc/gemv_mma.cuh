@@ -113,8 +113,39 @@ __host__ __device__ constexpr size_t mma_smem_bytes(int K) {
 // (one dependent memory round per four blocks instead of one per block); blocks at or past K / 8 read as zeros.
 // CACHE 1 keeps the first round's four blocks in `c`, CACHE 2 takes them from `c` instead of loading them again (a
 // second pass over x then costs no memory round when K <= 32 nthr).
+// x as the staging helpers see it: the vector, its length, and the transform applied on load (kActSiluMul: x holds
+// [gate | up], 2K values, and the staged value is bf16(SiLU(gate) * up)).
+struct XSrc {
+    const __nv_bfloat16* x;
+    int K;
+    int act = 0;
+};
+// x is loaded at L2 (ld.global.cg): in a fused sequence of GEMVs it is the output of the previous one, written by
+// other CTAs of the same grid, so the non-coherent read-only path must not serve it.
+__device__ __forceinline__ uint4 ld_x16(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+// bf16(SiLU(g) * u) of two packed bf16 pairs, SiLU(g) = g / (1 + e^-g) in fp32 with the library expf.
+__device__ __forceinline__ uint32_t silu_mul2(uint32_t g, uint32_t u) {
+    const float g0 = __uint_as_float(g << 16), g1 = __uint_as_float(g & 0xFFFF0000u);
+    const float u0 = __uint_as_float(u << 16), u1 = __uint_as_float(u & 0xFFFF0000u);
+    const float a0 = g0 / (1.f + expf(-g0)) * u0, a1 = g1 / (1.f + expf(-g1)) * u1;
+    const __nv_bfloat162 r = __floats2bfloat162_rn(a0, a1);
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+// 16-byte block i of the staged x (i < K / 8).
+__device__ __forceinline__ uint4 x_block(const XSrc& p, const uint4* x4, int nx, int i) {
+    if (p.act == kActSiluMul) {
+        const uint4 g = ld_x16(x4 + i), u = ld_x16(x4 + nx + i);
+        return make_uint4(silu_mul2(g.x, u.x), silu_mul2(g.y, u.y), silu_mul2(g.z, u.z), silu_mul2(g.w, u.w));
+    }
+    return ld_x16(x4 + i);
+}
+
 template <int CACHE = 0, typename Fn>
-__device__ __forceinline__ void x_blocks(const Params& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
+__device__ __forceinline__ void x_blocks(const XSrc& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
     const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
     const int nx = p.K / 8;
     for (int i0 = tid, r = 0; i0 < n; i0 += 4 * nthr, ++r) {
@@ -123,7 +154,7 @@ __device__ __forceinline__ void x_blocks(const Params& p, int tid, int nthr, int
         for (int k = 0; k < 4; ++k) {
             const int i = i0 + k * nthr;
             if (CACHE == 2 && r == 0) v[k] = c[k];
-            else v[k] = i < nx ? __ldg(x4 + i) : make_uint4(0u, 0u, 0u, 0u);
+            else v[k] = i < nx ? x_block(p, x4, nx, i) : make_uint4(0u, 0u, 0u, 0u);
             if (CACHE == 1 && r == 0) c[k] = v[k];
         }
 #pragma unroll
@@ -134,7 +165,7 @@ __device__ __forceinline__ void x_blocks(const Params& p, int tid, int nthr, int
 // As x_blocks, but every thread calls fn(i, v) in every round (i may be >= n; v is then zero), so fn may use
 // warp shuffles; blocks i0 + tid of a round belong to consecutive lanes.
 template <int CACHE = 0, typename Fn>
-__device__ __forceinline__ void x_blocks_all(const Params& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
+__device__ __forceinline__ void x_blocks_all(const XSrc& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
     const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
     const int nx = p.K / 8;
     for (int i0 = 0, r = 0; i0 < n; i0 += 4 * nthr, ++r) {
@@ -143,7 +174,7 @@ __device__ __forceinline__ void x_blocks_all(const Params& p, int tid, int nthr,
         for (int k = 0; k < 4; ++k) {
             const int i = i0 + k * nthr + tid;
             if (CACHE == 2 && r == 0) v[k] = c[k];
-            else v[k] = i < nx ? __ldg(x4 + i) : make_uint4(0u, 0u, 0u, 0u);
+            else v[k] = i < nx ? x_block(p, x4, nx, i) : make_uint4(0u, 0u, 0u, 0u);
             if (CACHE == 1 && r == 0) c[k] = v[k];
         }
 #pragma unroll
@@ -158,7 +189,7 @@ __device__ __forceinline__ void x_blocks_all(const Params& p, int tid, int nthr,
 // Called by `nthr` threads (thread index tid); `sync` is the barrier over exactly those threads; `scratch` holds
 // nthr/32 floats. Ends with x visible to the caller only after the caller's own barrier.
 template <int F, int DEC, int GST = 1, typename Sync>
-__device__ __forceinline__ void stage_x(const Params& p, uint16_t* xs, float* gsum, float* xscale, float* scratch, int tid,
+__device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum, float* xscale, float* scratch, int tid,
                                         int nthr, Sync sync) {
     // INT4 group sums are written GST words apart (the integer path needs 8 words per group)
     static_assert(!(F == kINT4 || F == kINT4A) || DEC != 2 || GST == 8, "integer INT4 staging needs 8 words per group");
@@ -653,7 +684,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_mma_kernel(const Params p) {
 
     grid_dependency_wait();
 
-    stage_x<F, DEC>(p, xs, gsum, xscale, part, tid, NW * 32, []() { __syncthreads(); });
+    stage_x<F, DEC>(XSrc{p.x, p.K}, xs, gsum, xscale, part, tid, NW * 32, []() { __syncthreads(); });
     __syncthreads();
     launch_dependents();
 

@@ -119,6 +119,7 @@ constexpr int kTmaMaxRing = 16;        // ring stages at most
 constexpr int kTmaMaxParts = kTmaMaxRing + 1;   // tile-partial buffers at most
 // mbarriers: full[16], empty[16], tile_done[17], part_free[17], x_ready (67 x 8 bytes, padded to 640)
 constexpr int kTmaBarBytes = 640;
+constexpr int kTmaTailBytes = 160;     // x scale of two ops (2 x 4 floats) + x staging scratch (32 floats)
 
 // Metadata slot of a stage (bytes): FP8 row scales float[16] at 0; bias words (18 halves) at 64; INT4 scales and
 // (INT4A) zeros at 112, 16 rows x tma_meta_row(CS) halves each.
@@ -136,7 +137,7 @@ __host__ __device__ constexpr int tma_part_bufs(int ring, int nch) { return (rin
 // Shared-memory layout (bytes): [0,640) mbarriers; ring x st_bytes; metadata ring x tma_meta_bytes (16-byte
 // multiples); x: Kpad x 2 (INT4 integer path: Kpad x 3) + 64 (FP8 lo plane at Kpad + 64, INT4 planes Kpad + 16
 // apart); INT4 group sums
-// (tma_gsum_words per group); tile partials NB x NC x 16 floats; x scale 16 bytes.
+// (tma_gsum_words per group); tile partials NB x NC x 16 floats; x scales of two ops and staging scratch (160 bytes).
 template <int F, int NC, int DEC>
 __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int kc, int st_bytes) {
     const int kp = mma_kpad<F>(K);
@@ -145,15 +146,29 @@ __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int k
     // x: 2 bytes per element (3 for the INT4 integer path's digit planes)
     constexpr size_t xb = ((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2;
     return kTmaBarBytes + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * xb + 64 +
-           ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * tma_gsum_words(DEC) * 4 : 0) + (size_t)nb * NC * 16 * 4 + 16;
+           ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * tma_gsum_words(DEC) * 4 : 0) + (size_t)nb * NC * 16 * 4 +
+           kTmaTailBytes;
 }
 
 // Host: choose the stage geometry for this shape within `cap` bytes of shared memory and return the dynamic shared
 // memory size (0 when it cannot be staged). A row is split into NCH equal chunks of KC bytes (a multiple of 64, at most
 // 4096 so that a 16-row stage stays <= 64 KB; INT4 at most 2048, i.e. <= 32 groups of metadata per stage). p.ring on
 // entry is the requested ring depth (>= 2), or 0 for as many stages as fit (2..16; KC then sized for >= 3 stages).
+// Layer mode (p.nops > 0): the ops share one stage geometry, chosen for the longest row; p.K and p.nchunk become the
+// largest K and row, each op gets its own NCH (stages per row) and p.nch the smallest of them (the most tiles a ring
+// can span, which sizes the partial buffers).
 template <int F, int NC, int DEC>
 size_t tma_prep(Params& p, size_t cap) {
+    GemvOp* ops = p.host_ops ? p.host_ops : p.ops;
+    if (p.nops > 0) {
+        int K = 0, nchunk = 0;
+        for (int j = 0; j < p.nops; ++j) {
+            K = ops[j].K > K ? ops[j].K : K;
+            nchunk = ops[j].nchunk > nchunk ? ops[j].nchunk : nchunk;
+        }
+        p.K = K;
+        p.nchunk = nchunk;
+    }
     const size_t rowbytes = (size_t)p.nchunk * 16;
     const int want = p.ring;
     if (want == 1 || want > kTmaMaxRing) return 0;
@@ -170,13 +185,38 @@ size_t tma_prep(Params& p, size_t cap) {
     if (kc_max < 64) return 0;
     const long need = (long)((rowbytes + 63) / 64 * 64);
     const long kc0 = need < kc_max ? need : kc_max;
-    const int nch = (int)((rowbytes + kc0 - 1) / kc0);
+    int nch = (int)((rowbytes + kc0 - 1) / kc0);
     long kc = (long)((rowbytes + nch - 1) / nch);
     kc = (kc + 63) / 64 * 64;
+    if (p.nops > 0) {
+        // one chunk size for every op: the largest whose stages are fullest over the whole sequence (weight bytes of
+        // all ops / ring bytes their stages occupy), among chunks down to a quarter of the largest that fits
+        double best = -1.0;
+        const long lo = kc_max / 4 > 64 ? kc_max / 4 : 64;
+        for (long c = kc0; c >= lo; c -= 64) {
+            double used = 0.0, held = 0.0;
+            for (int j = 0; j < p.nops; ++j) {
+                const double rb = (double)ops[j].nchunk * 16;
+                used += rb * ops[j].N;
+                held += (double)((long)(rb + c - 1) / c) * c * ops[j].N;
+            }
+            if (used / held > best + 0.005) { best = used / held; kc = c; }
+        }
+        nch = (int)((rowbytes + kc - 1) / kc);
+    }
     p.kc = (int)kc;
     p.nch = nch;
     p.rs = (int)(kc % 128 == 0 ? kc + 64 : kc);
     p.st_bytes = (16 * p.rs + 127) / 128 * 128;
+    if (p.nops > 0) {
+        int mn = nch;
+        for (int j = 0; j < p.nops; ++j) {
+            GemvOp& o = ops[j];
+            o.nch = (int)(((size_t)o.nchunk * 16 + kc - 1) / kc);
+            mn = o.nch < mn ? o.nch : mn;
+        }
+        p.nch = mn;
+    }
     int ring = want;
     if (ring == 0) {
         const size_t per_stage = (size_t)p.st_bytes + (size_t)(tma_meta_bytes<F>((int)kc / 64) + 15) / 16 * 16;
@@ -184,9 +224,9 @@ size_t tma_prep(Params& p, size_t cap) {
         ring = fit > (size_t)kTmaMaxRing ? kTmaMaxRing : (int)fit;
         if (ring < 2) return 0;
     }
-    size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, nch, p.kc, p.st_bytes);
+    size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, p.nch, p.kc, p.st_bytes);
     while (want == 0 && total > cap && ring > 2)               // deeper rings need more partial buffers
-        total = tma_smem_bytes<F, NC, DEC>(p.K, --ring, nch, p.kc, p.st_bytes);
+        total = tma_smem_bytes<F, NC, DEC>(p.K, --ring, p.nch, p.kc, p.st_bytes);
     p.ring = ring;
     return total <= cap ? total : 0;
 }
@@ -357,37 +397,58 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
     }
 }
 
+// Op j of the launch: the single GEMV of Params (nops == 0) or the layer list.
+__device__ __forceinline__ GemvOp tma_op(const Params& p, int j) {
+    if (p.op_table) return p.op_table[j];
+    if (p.nops > 0) return p.ops[j];
+    GemvOp o;
+    o.W = p.W; o.s = p.s; o.z = p.z; o.x = p.x; o.bias = p.bias; o.y = p.y;
+    o.N = p.N; o.K = p.K; o.nchunk = p.nchunk; o.groups = p.groups; o.nch = p.nch;
+    return o;
+}
+
+// Bounded wait (~2 s) until *c >= target (acquire, gpu scope); on timeout records `code` and returns.
+__device__ __forceinline__ void wait_count(const unsigned int* c, unsigned int target, int code) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        unsigned int v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+        if (v >= target) return;
+        if (global_ns() - t0 > 2000000000ull) {
+            atomicCAS(&g_tma_error, 0, code);
+            return;
+        }
+        __nanosleep(64);
+    }
+}
+
 template <int F, int NC, int U, int DEC = 0>
-__global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params p) {
+__global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid_constant__ Params p) {
     constexpr bool I4 = (F == kINT4 || F == kINT4A);
     extern __shared__ __align__(128) uint8_t smem[];
-    const int KC = p.kc, NCH = p.nch, RS = p.rs;
+    // geometry shared by every op of the launch (p.K: the largest K, p.nch: the smallest NCH)
+    const int KC = p.kc, RS = p.rs;
     const int ST = p.ring;                                    // 2..16 stages (the host checks)
-    const int NB = tma_part_bufs(ST, NCH);
+    const int NB = tma_part_bufs(ST, p.nch);
     const int CS = KC >> 6, MR = tma_meta_row(CS);
     const int MB = (tma_meta_bytes<F>(CS) + 15) & ~15;
-    const int S = (p.nchunk + 3) >> 2;                        // 64-byte steps per row
-    const int SF = p.nchunk >> 2;                             // steps whose four 16-byte chunks are all in the row
-    const size_t rowbytes = (size_t)p.nchunk * 16;
-    const int Kp = mma_kpad<F>(p.K);
+    const int Kpm = mma_kpad<F>(p.K);
+    const int nops = p.nops > 0 ? p.nops : 1;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kTmaMaxRing;
     uint64_t* tdone = empty + kTmaMaxRing;                    // tile t's NC partials are in buffer t mod NB
     uint64_t* pfree = tdone + kTmaMaxParts;                   // the epilogue warp has read buffer t mod NB
-    uint64_t* xready = pfree + kTmaMaxParts;                  // the consumers have staged x
+    uint64_t* xready = pfree + kTmaMaxParts;                  // the consumers have staged x (op 0)
     uint8_t* ring = smem + kTmaBarBytes;
     uint8_t* meta = ring + (size_t)ST * p.st_bytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(meta + (size_t)ST * MB);
-    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)Kp * ((I4 && DEC == 2) ? 3 : 2) + 64);
+    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)Kpm * ((I4 && DEC == 2) ? 3 : 2) + 64);
     constexpr int GW = tma_gsum_words(DEC);
-    float* part = gsum + (I4 ? GW * (Kp / 128) : 0);
-    float* xscale = part + (size_t)NB * NC * 16;
+    float* part = gsum + (I4 ? GW * (Kpm / 128) : 0);
+    float* xscale = part + (size_t)NB * NC * 16;              // [2][4]: the x scale of even and odd ops
+    float* xscr = xscale + 8;                                 // 32 floats of x staging scratch
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rb = (int)((long long)blockIdx.x * p.N / gridDim.x);
-    const int re = (int)((long long)(blockIdx.x + 1) * p.N / gridDim.x);
-    const int T = (re - rb + 15) >> 4;
-    const int nst = T * NCH;                                  // stages this CTA streams
 
     if (tid == 0) {
         // full: the producer's expect_tx arrival, 32 lanes' cp.async arrivals and its closing arrival
@@ -400,79 +461,92 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
 
     if (warp == NC) {
         // ------------------------------------------------------------ producer warp
-        const long long NG = (long long)p.N * p.groups;
+        // Streams every op's stages back to back: op j + 1's weights never wait for op j's x.
         const int pre = (p.pre > 0 && p.pre < ST) ? p.pre : -1;    // -1: never wait
         const uint64_t wpol = l2_evict_first();
-        // INT4 whole-row stages whose scale (zero) runs start and end on 16-byte boundaries: one bulk copy per tile
-        bool meta_bulk = false;
-        if constexpr (I4)
-            meta_bulk = NCH == 1 && (p.groups & 7) == 0 && (((uintptr_t)p.s & 15) == 0) &&
-                        (F == kINT4 || ((uintptr_t)p.z & 15) == 0);
-        int s = 0, t = 0, j = 0;
+        int s = 0, g = 0;                                     // ring slot, stage count over all ops
         uint32_t ph = 0;                                      // parity of the slot's previous release
-        for (int i = 0; i < nst; ++i) {
-            const int r0 = rb + 16 * t;
-            const int nrows = re - r0 < 16 ? re - r0 : 16;
-            const bool last = j == NCH - 1;
-            const int nsteps = last ? S - j * CS : CS;
-            const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
-            const uint32_t mbytes = meta_bulk ? (uint32_t)(2 * nrows * p.groups) : 0u;   // per metadata array
-            if (lane == 0) {
-                // x is read right after the dependency wait: streaming only `pre` stages until it is staged keeps
-                // the x loads from queueing behind a whole ring of this SM's copies
-                if (i == pre) mbar_wait(xready, 0, 5);
-                if (i >= ST) mbar_wait(&empty[s], ph, 1);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before the copies
-                mbar_arrive_expect_tx(&full[s], (uint32_t)nrows * bytes + (F == kINT4A ? 2 : 1) * mbytes);
-                if (meta_bulk) {
-                    uint8_t* mdst = meta + (size_t)s * MB + 112;
-                    const size_t moff = (size_t)r0 * p.groups * 2;
-                    bulk_copy_g2s(mdst, reinterpret_cast<const uint8_t*>(p.s) + moff, mbytes, &full[s]);
-                    if constexpr (F == kINT4A)
-                        bulk_copy_g2s(mdst + 32 * MR, reinterpret_cast<const uint8_t*>(p.z) + moff, mbytes, &full[s]);
-                }
-            }
-            __syncwarp();                                     // the slot is free and its byte count announced
-            if (lane < nrows)
-                bulk_copy_g2s_ef(ring + (size_t)s * p.st_bytes + (size_t)lane * RS,
-                                 p.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s], wpol);
-            uint8_t* ms = meta + (size_t)s * MB;
-            if constexpr (I4) {
-                uint16_t* msc = reinterpret_cast<uint16_t*>(ms + 112);
-                const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s);
-                const uint16_t* za = reinterpret_cast<const uint16_t*>(p.z);
-                if (NCH == 1) {
-                    // whole rows per stage: the tile's scales (zeros) are one contiguous run of nrows x G halves
-                    const long long e0 = (long long)r0 * p.groups;
-                    const int n = nrows * p.groups;
-                    if (!meta_bulk) {
-                        const int nw = u16_words(sa, e0, n);
-                        for (int k = lane; k < nw; k += 32) u16_word_copy(msc, sa, NG, e0, k);
+        for (int jo = 0; jo < nops; ++jo) {
+            const GemvOp op = tma_op(p, jo);
+            const int NCH = op.nch;
+            const int S = (op.nchunk + 3) >> 2;
+            const size_t rowbytes = (size_t)op.nchunk * 16;
+            const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
+            const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
+            const int nst = ((re - rb + 15) >> 4) * NCH;
+            const long long NG = (long long)op.N * op.groups;
+            // INT4 whole-row stages whose scale (zero) runs start and end on 16-byte boundaries: one bulk copy per
+            // tile
+            bool meta_bulk = false;
+            if constexpr (I4)
+                meta_bulk = NCH == 1 && (op.groups & 7) == 0 && (((uintptr_t)op.s & 15) == 0) &&
+                            (F == kINT4 || ((uintptr_t)op.z & 15) == 0);
+            int t = 0, j = 0;
+            for (int i = 0; i < nst; ++i, ++g) {
+                const int r0 = rb + 16 * t;
+                const int nrows = re - r0 < 16 ? re - r0 : 16;
+                const bool last = j == NCH - 1;
+                const int nsteps = last ? S - j * CS : CS;
+                const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
+                const uint32_t mbytes = meta_bulk ? (uint32_t)(2 * nrows * op.groups) : 0u;   // per metadata array
+                if (lane == 0) {
+                    // x is read right after the dependency wait: streaming only `pre` stages until it is staged
+                    // keeps the x loads from queueing behind a whole ring of this SM's copies
+                    if (g == pre) mbar_wait(xready, 0, 5);
+                    if (g >= ST) mbar_wait(&empty[s], ph, 1);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before copies
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)nrows * bytes + (F == kINT4A ? 2 : 1) * mbytes);
+                    if (meta_bulk) {
+                        uint8_t* mdst = meta + (size_t)s * MB + 112;
+                        const size_t moff = (size_t)r0 * op.groups * 2;
+                        bulk_copy_g2s(mdst, reinterpret_cast<const uint8_t*>(op.s) + moff, mbytes, &full[s]);
                         if constexpr (F == kINT4A)
-                            for (int k = lane; k < nw; k += 32) u16_word_copy(msc + 16 * MR, za, NG, e0, k);
-                    }
-                } else {
-                    // rows x words of this stage's scale (and zero) runs, spread over the lanes; every row copies
-                    // the (nsteps + 2) / 2 words that hold its run for either element parity
-                    const int wpr = (nsteps + 2) >> 1;
-                    int rr = lane / wpr, k = lane - rr * wpr;
-                    const int drr = 32 / wpr, dk = 32 - drr * wpr;
-                    while (rr < nrows) {
-                        const long long e0 = (long long)(r0 + rr) * p.groups + (long long)j * CS;
-                        if (k < u16_words(sa, e0, nsteps)) u16_word_copy(msc + rr * MR, sa, NG, e0, k);
-                        if constexpr (F == kINT4A)
-                            if (k < u16_words(za, e0, nsteps)) u16_word_copy(msc + (16 + rr) * MR, za, NG, e0, k);
-                        rr += drr;
-                        k += dk;
-                        if (k >= wpr) { k -= wpr; ++rr; }
+                            bulk_copy_g2s(mdst + 32 * MR, reinterpret_cast<const uint8_t*>(op.z) + moff, mbytes,
+                                          &full[s]);
                     }
                 }
+                __syncwarp();                                 // the slot is free and its byte count announced
+                if (lane < nrows)
+                    bulk_copy_g2s_ef(ring + (size_t)s * p.st_bytes + (size_t)lane * RS,
+                                     op.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s], wpol);
+                uint8_t* ms = meta + (size_t)s * MB;
+                if constexpr (I4) {
+                    uint16_t* msc = reinterpret_cast<uint16_t*>(ms + 112);
+                    const uint16_t* sa = reinterpret_cast<const uint16_t*>(op.s);
+                    const uint16_t* za = reinterpret_cast<const uint16_t*>(op.z);
+                    if (NCH == 1) {
+                        // whole rows per stage: the tile's scales (zeros) are one contiguous run of nrows x G halves
+                        const long long e0 = (long long)r0 * op.groups;
+                        const int n = nrows * op.groups;
+                        if (!meta_bulk) {
+                            const int nw = u16_words(sa, e0, n);
+                            for (int k = lane; k < nw; k += 32) u16_word_copy(msc, sa, NG, e0, k);
+                            if constexpr (F == kINT4A)
+                                for (int k = lane; k < nw; k += 32) u16_word_copy(msc + 16 * MR, za, NG, e0, k);
+                        }
+                    } else {
+                        // rows x words of this stage's scale (and zero) runs, spread over the lanes; every row
+                        // copies the (nsteps + 2) / 2 words that hold its run for either element parity
+                        const int wpr = (nsteps + 2) >> 1;
+                        int rr = lane / wpr, k = lane - rr * wpr;
+                        const int drr = 32 / wpr, dk = 32 - drr * wpr;
+                        while (rr < nrows) {
+                            const long long e0 = (long long)(r0 + rr) * op.groups + (long long)j * CS;
+                            if (k < u16_words(sa, e0, nsteps)) u16_word_copy(msc + rr * MR, sa, NG, e0, k);
+                            if constexpr (F == kINT4A)
+                                if (k < u16_words(za, e0, nsteps)) u16_word_copy(msc + (16 + rr) * MR, za, NG, e0, k);
+                            rr += drr;
+                            k += dk;
+                            if (k >= wpr) { k -= wpr; ++rr; }
+                        }
+                    }
+                }
+                cp_async_arrive(&full[s]);
+                __syncwarp();                                 // plain-load halves stored before the closing arrival
+                if (lane == 0) mbar_arrive(&full[s]);
+                if (++s == ST) { s = 0; if (g >= ST) ph ^= 1u; }    // waits from round 1 on: parity 0, 1, 0, ...
+                if (++j == NCH) { j = 0; ++t; }
             }
-            cp_async_arrive(&full[s]);
-            __syncwarp();                                     // plain-load halves stored before the closing arrival
-            if (lane == 0) mbar_arrive(&full[s]);
-            if (++s == ST) { s = 0; if (i >= ST) ph ^= 1u; }    // waits from round 1 on: parity 0, 1, 0, ...
-            if (++j == NCH) { j = 0; ++t; }
         }
         return;
     }
@@ -481,41 +555,58 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
         // ------------------------------------------------------------ epilogue warp
         // Lane r < 16 owns row r of each tile: its row scale and bias are loaded before the wait for the tile's
         // partials (so their latency hides behind the tile's compute); then the NC partials are added in warp order
-        // (deterministic), scaled, and stored; the buffer is handed back to the consumers.
+        // (deterministic), scaled, and stored; the buffer is handed back to the consumers. In layer mode, once all
+        // of an op's tiles are stored the CTA counts itself in on the op's counter.
         grid_dependency_wait();                               // y is written only after the preceding grid is done
         int b = 0;
         uint32_t bph = 0;
-        for (int t = 0; t < T; ++t) {
-            const int row = rb + 16 * t + lane;
-            const bool mine = lane < 16 && row < re;
-            float rs = 1.f, rbias = 0.f;
-            if (mine) {
-                if constexpr (F == kFP8) rs = ld_f32(reinterpret_cast<const float*>(p.s) + row);
-                if (p.bias) rbias = __uint_as_float((uint32_t)ld_u16(p.bias + row) << 16);
-            }
-            mbar_wait(&tdone[b], bph, 3);
-            if (mine) {
-                const float* buf = part + (size_t)b * NC * 16;
-                float total = 0.f;
+        for (int jo = 0; jo < nops; ++jo) {
+            const GemvOp op = tma_op(p, jo);
+            const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
+            const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
+            const int T = (re - rb + 15) >> 4;
+            const float* xsc = xscale + 4 * (jo & 1);
+            for (int t = 0; t < T; ++t) {
+                const int row = rb + 16 * t + lane;
+                const bool mine = lane < 16 && row < re;
+                float rs = 1.f, rbias = 0.f;
+                if (mine) {
+                    if constexpr (F == kFP8) rs = ld_f32(reinterpret_cast<const float*>(op.s) + row);
+                    if (op.bias) rbias = __uint_as_float((uint32_t)ld_u16(op.bias + row) << 16);
+                }
+                mbar_wait(&tdone[b], bph, 3);
+                if (mine) {
+                    const float* buf = part + (size_t)b * NC * 16;
+                    float total = 0.f;
 #pragma unroll
-                for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
-                float out = total;
-                if constexpr (F == kFP8)                      // row scale, then 2^e (a normal power of two)
-                    out = out * rs * __uint_as_float((uint32_t)(__float_as_int(xscale[0]) + 127) << 23);
-                if constexpr (I4 && DEC == 1)                 // x was staged as x * 2^-e
-                    out = out * __uint_as_float((uint32_t)(__float_as_int(xscale[0]) + 127) << 23);
-                if constexpr (I4 && DEC == 2)                 // x was staged as integers x * 2^s
-                    out = out * xscale[1];
-                const __nv_bfloat16 v = __float2bfloat16_rn(out + rbias);
-                if (p.tp_world == 0) {
-                    p.y[row] = v;
-                } else {
-                    for (int r = 0; r < p.tp_world; ++r) p.tp_y[r][p.tp_off + row] = v;   // peer stores
+                    for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
+                    float out = total;
+                    if constexpr (F == kFP8)                  // row scale, then 2^e (a normal power of two)
+                        out = out * rs * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
+                    if constexpr (I4 && DEC == 1)             // x was staged as x * 2^-e
+                        out = out * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
+                    if constexpr (I4 && DEC == 2)             // x was staged as integers x * 2^s
+                        out = out * xsc[1];
+                    const __nv_bfloat16 v = __float2bfloat16_rn(out + rbias);
+                    if (p.tp_world == 0) {
+                        op.y[row] = v;
+                    } else {
+                        for (int r = 0; r < p.tp_world; ++r) p.tp_y[r][p.tp_off + row] = v;   // peer stores
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pfree[b]);
+                if (++b == NB) { b = 0; bph ^= 1u; }
+            }
+            if (p.nops > 0) {
+                // this CTA's rows of op jo are in memory: release them, then count the CTA in
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence();
+                    atomicAdd(&p.layer_done[jo], 1u);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&pfree[b]);
-            if (++b == NB) { b = 0; bph ^= 1u; }
         }
         if (p.tp_world > 0) {
             // this CTA's outputs are on every rank: make them visible system-wide, then count the CTA in everywhere
@@ -526,18 +617,21 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
                 for (int r = 0; r < p.tp_world; ++r) atomicAdd_system(p.tp_flag[r], 1u);
             }
         }
+        if (p.nops > 0) consumer_barrier(2, (NC + 1) * 32);    // this CTA's consumers are past their last wait
+        if (p.nops > 0 && lane == 0) {
+            // the last CTA through every op zeroes the counters for the next launch (every CTA's consumers have
+            // passed all of their waits by then)
+            const unsigned int fin = atomicAdd(&p.layer_done[nops], 1u);
+            if (fin == gridDim.x - 1) {
+                __threadfence();
+                for (int jo = 0; jo <= nops; ++jo) atomicExch(&p.layer_done[jo], 0u);
+                __threadfence();
+            }
+        }
         return;
     }
 
     // ---------------------------------------------------------------- consumer warps
-    grid_dependency_wait();
-    stage_x<F, DEC, tma_gsum_words(DEC)>(p, xs, gsum, xscale, part, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
-    consumer_barrier(1, NC * 32);
-    if (tid == 0) {
-        launch_dependents();
-        mbar_arrive(xready);
-    }
-
     const int g = lane >> 2, c = lane & 3;
     // accumulator chains scaled by 1 (cvt decode, BF16) or 256 (FP8 ALU decode holds value / 256)
     constexpr float f0 = (F == kFP8 && DEC == 1) ? 256.f : 1.f;
@@ -545,90 +639,122 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const Params
     TmaAcc<U> A;
     A.zero();
     float acc0 = 0.f, acc1 = 0.f;
-    const uint16_t* sa = reinterpret_cast<const uint16_t*>(p.s);
-    const uint16_t* za = reinterpret_cast<const uint16_t*>(p.z);
-    int s = 0, t = 0, j = 0, b = 0;
+    int s = 0, b = 0, tg = 0;                                 // ring slot, partial buffer, tiles over all ops
     uint32_t ph = 0, bph = 0;
-    for (int i = 0; i < nst; ++i) {
-        const int r0 = rb + 16 * t;
-        const bool last = j == NCH - 1;
-        mbar_wait(&full[s], ph, 2);
-        const int nsteps = last ? S - j * CS : CS;
-        const int sa0 = warp * nsteps / NC, sb0 = (warp + 1) * nsteps / NC;
-        const uint8_t* st = ring + (size_t)s * p.st_bytes;
-        const uint8_t* ms = meta + (size_t)s * MB;
-        const uint8_t* r0p = st + (size_t)g * RS + 16 * c;
-        const uint8_t* r1p = r0p + (size_t)8 * RS;
-        // INT4: this lane's scale (and zero) runs of rows g and g + 8, element parity folded in
-        const uint16_t* msc = reinterpret_cast<const uint16_t*>(ms + 112);
-        const uint16_t *sc0 = msc, *sc1 = msc, *zr0 = msc, *zr1 = msc;
-        if constexpr (I4) {
-            if (NCH == 1) {                                   // the tile's run: row rr at rr x G (+ run parity)
-                const long long e0 = (long long)r0 * p.groups;
-                sc0 = msc + u16_parity(sa + e0) + g * p.groups;
-                sc1 = sc0 + 8 * p.groups;
-                if constexpr (F == kINT4A) {
-                    zr0 = msc + 16 * MR + u16_parity(za + e0) + g * p.groups;
-                    zr1 = zr0 + 8 * p.groups;
-                }
-            } else {                                          // per-row runs: row rr at rr x MR (+ row parity)
-                const long long e0 = (long long)(r0 + g) * p.groups + (long long)j * CS;
-                const long long e1 = e0 + 8LL * p.groups;
-                sc0 = msc + g * MR + u16_parity(sa + e0);
-                sc1 = msc + (g + 8) * MR + u16_parity(sa + e1);
-                if constexpr (F == kINT4A) {
-                    zr0 = msc + (16 + g) * MR + u16_parity(za + e0);
-                    zr1 = msc + (24 + g) * MR + u16_parity(za + e1);
-                }
-            }
+    for (int jo = 0; jo < nops; ++jo) {
+        const GemvOp op = tma_op(p, jo);
+        if (jo == 0) {
+            grid_dependency_wait();
+        } else {
+            // every consumer warp is done with the previous op's x; then every CTA must have stored op jo - 1
+            consumer_barrier(1, NC * 32);
+            if (lane == 0) wait_count(&p.layer_done[jo - 1], gridDim.x, 7);
+            __syncwarp();
         }
-        const int gb = j * CS;                                // global step of stage-local step 0
-        const int sfull = SF - gb < sb0 ? SF - gb : sb0;      // steps below sfull are whole
-        int sl = sa0;
-#pragma unroll 2
-        for (; sl + U <= sfull; sl += U)
-            tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp + 16);
-        for (; sl < sfull; ++sl)
-            tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp + 16);
-        for (; sl < sb0; ++sl)                                // the ragged last step of the row
-            tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c, p.nchunk, Kp + 16);
-
-        if (last) {
-            // tile end: this warp's partial sums of rows g, g + 8 -> buffer b for the epilogue warp
-            float s0, s1;
+        const int NCH = op.nch;
+        const int S = (op.nchunk + 3) >> 2;                   // 64-byte steps per row
+        const int SF = op.nchunk >> 2;                        // steps whose four 16-byte chunks are all in the row
+        const int Kp = mma_kpad<F>(op.K);
+        const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
+        const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
+        const int nst = ((re - rb + 15) >> 4) * NCH;
+        if (nst > 0) {                                        // CTA-uniform: a CTA without rows of the op skips x
+            stage_x<F, DEC, tma_gsum_words(DEC)>(XSrc{op.x, op.K}, xs, gsum, xscale + 4 * (jo & 1), xscr, tid,
+                                                 NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+            consumer_barrier(1, NC * 32);
+        }
+        if (jo == 0 && tid == 0) {
+            launch_dependents();
+            mbar_arrive(xready);
+        }
+        const uint16_t* sa = reinterpret_cast<const uint16_t*>(op.s);
+        const uint16_t* za = reinterpret_cast<const uint16_t*>(op.z);
+        int t = 0, j = 0;
+        for (int i = 0; i < nst; ++i) {
+            const int r0 = rb + 16 * t;
+            const bool last = j == NCH - 1;
+            mbar_wait(&full[s], ph, 2);
+            const int nsteps = last ? S - j * CS : CS;
+            const int sa0 = warp * nsteps / NC, sb0 = (warp + 1) * nsteps / NC;
+            const uint8_t* st = ring + (size_t)s * p.st_bytes;
+            const uint8_t* ms = meta + (size_t)s * MB;
+            const uint8_t* r0p = st + (size_t)g * RS + 16 * c;
+            const uint8_t* r1p = r0p + (size_t)8 * RS;
+            const uint16_t* msc = reinterpret_cast<const uint16_t*>(ms + 112);
+            const uint16_t *sc0 = msc, *sc1 = msc, *zr0 = msc, *zr1 = msc;
             if constexpr (I4) {
-                s0 = acc0; s1 = acc1;
-                if constexpr (DEC == 2) {                         // digits 0-1 (lane c = 0) + digit 2 (c = 1)
-                    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-                    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-                }
-                acc0 = acc1 = 0.f;
-            } else {
-                s0 = 0.f; s1 = 0.f;
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if constexpr (F == kFP8 && DEC == 3) {        // columns 0 (x hi) + 1 (x lo)
-                        s0 += (A.a[u][0][0] + A.a[u][0][1]) + (A.a[u][1][0] + A.a[u][1][1]);
-                        s1 += (A.a[u][0][2] + A.a[u][0][3]) + (A.a[u][1][2] + A.a[u][1][3]);
-                    } else {
-                        s0 += A.a[u][0][0] * f0 + A.a[u][1][0] * f1;
-                        s1 += A.a[u][0][2] * f0 + A.a[u][1][2] * f1;
+                if (NCH == 1) {                               // the tile's run: row rr at rr x G (+ run parity)
+                    const long long e0 = (long long)r0 * op.groups;
+                    sc0 = msc + u16_parity(sa + e0) + g * op.groups;
+                    sc1 = sc0 + 8 * op.groups;
+                    if constexpr (F == kINT4A) {
+                        zr0 = msc + 16 * MR + u16_parity(za + e0) + g * op.groups;
+                        zr1 = zr0 + 8 * op.groups;
+                    }
+                } else {                                      // per-row runs: row rr at rr x MR (+ row parity)
+                    const long long e0 = (long long)(r0 + g) * op.groups + (long long)j * CS;
+                    const long long e1 = e0 + 8LL * op.groups;
+                    sc0 = msc + g * MR + u16_parity(sa + e0);
+                    sc1 = msc + (g + 8) * MR + u16_parity(sa + e1);
+                    if constexpr (F == kINT4A) {
+                        zr0 = msc + (16 + g) * MR + u16_parity(za + e0);
+                        zr1 = msc + (24 + g) * MR + u16_parity(za + e1);
                     }
                 }
-                A.zero();
             }
-            if (t >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile t - NB
-            float* buf = part + (size_t)b * NC * 16;
-            if (c == 0) { buf[warp * 16 + g] = s0; buf[warp * 16 + g + 8] = s1; }
+            const int gb = j * CS;                            // global step of stage-local step 0
+            const int sfull = SF - gb < sb0 ? SF - gb : sb0;  // steps below sfull are whole
+            int sl = sa0;
+#pragma unroll 2
+            for (; sl + U <= sfull; sl += U)
+                tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                            op.nchunk, Kp + 16);
+            for (; sl < sfull; ++sl)
+                tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                            op.nchunk, Kp + 16);
+            for (; sl < sb0; ++sl)                            // the ragged last step of the row
+                tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                           op.nchunk, Kp + 16);
+
+            if (last) {
+                // tile end: this warp's partial sums of rows g, g + 8 -> buffer b for the epilogue warp
+                float s0, s1;
+                if constexpr (I4) {
+                    s0 = acc0; s1 = acc1;
+                    if constexpr (DEC == 2) {                     // digits 0-1 (lane c = 0) + digit 2 (c = 1)
+                        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+                        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+                    }
+                    acc0 = acc1 = 0.f;
+                } else {
+                    s0 = 0.f; s1 = 0.f;
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        if constexpr (F == kFP8 && DEC == 3) {    // columns 0 (x hi) + 1 (x lo)
+                            s0 += (A.a[u][0][0] + A.a[u][0][1]) + (A.a[u][1][0] + A.a[u][1][1]);
+                            s1 += (A.a[u][0][2] + A.a[u][0][3]) + (A.a[u][1][2] + A.a[u][1][3]);
+                        } else {
+                            s0 += A.a[u][0][0] * f0 + A.a[u][1][0] * f1;
+                            s1 += A.a[u][0][2] * f0 + A.a[u][1][2] * f1;
+                        }
+                    }
+                    A.zero();
+                }
+                if (tg >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile tg - NB
+                ++tg;
+                float* buf = part + (size_t)b * NC * 16;
+                if (c == 0) { buf[warp * 16 + g] = s0; buf[warp * 16 + g + 8] = s1; }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tdone[b]);         // release: this warp's partials of the tile
+                if (++b == NB) { b = 0; bph ^= 1u; }
+            }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tdone[b]);             // release: this warp's partials of tile t
-            if (++b == NB) { b = 0; bph ^= 1u; }
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == ST) { s = 0; ph ^= 1u; }
+            if (++j == NCH) { j = 0; ++t; }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == ST) { s = 0; ph ^= 1u; }
-        if (++j == NCH) { j = 0; ++t; }
     }
+    if (p.nops > 0) consumer_barrier(2, (NC + 1) * 32);        // no consumer waits on a counter any more
 }
 
 }  // namespace pb2

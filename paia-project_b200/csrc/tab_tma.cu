@@ -58,7 +58,9 @@ const Variant* tma_instances(int fmt, int math, int* n) {
 }
 #undef PB2_N
 
-// Error word of the bounded mbarrier waits (1 producer gave up on a free stage, 2 consumer gave up on a full stage).
+// Error word of the bounded waits (1 producer gave up on a free stage, 2 consumer on a full stage, 3 epilogue on a
+// tile's partials, 4 consumer on a free partial buffer, 5 producer on the staged x, 7 consumer on the previous op of
+// a layer launch).
 int tma_device_error(int clear) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_tma_error, sizeof(int)) != cudaSuccess) { (void)cudaGetLastError(); return -1; }

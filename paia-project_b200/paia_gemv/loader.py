@@ -7,8 +7,8 @@ tables (`variants`, `variants_fp8`, `variants_int4`: lists of {"id", "R", "U", "
 behaviour (a nonzero return code raises RuntimeError; -1 bad variant, -2 bad shape or alignment, >0 cudaError_t).
 
 Added for the B200 build: `int4_asym` (asymmetric INT4 g128, bf16 scale and zero), an optional fused bias on every
-format (`*_bias`), `variant_info_ex` (the B200 launch configuration a variant maps to), `device_error()`, and the
-tensor-parallel helpers used by paia_gemv.tp. There is no CPU fallback: without the library every op raises.
+format (`*_bias`), `variant_info_ex` (the B200 launch configuration a variant maps to), `device_error()`, `layer` and `plan_*` (one
+persistent launch for a sequence of GEMVs), and the tensor-parallel helpers used by paia_gemv.tp. There is no CPU fallback: without the library every op raises.
 """
 import ctypes
 import os
@@ -41,6 +41,16 @@ _EX_FIELDS = ("R", "U", "W", "S", "H", "KS", "pdl", "vec_bytes", "math")
 
 class VariantEx(ctypes.Structure):
     _fields_ = [(f, ctypes.c_int) for f in _EX_FIELDS]
+
+
+class GemvOp(ctypes.Structure):
+    """paia_gemv_op: one GEMV of a layer launch (raw device pointers; unused ones None)."""
+    _fields_ = [("Wq", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("zeros", ctypes.c_void_p),
+                ("x", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("N", ctypes.c_int), ("K", ctypes.c_int)]
+
+
+MAX_LAYER_OPS = 6
 
 
 class GemvLib:
@@ -83,6 +93,14 @@ class GemvLib:
         lib.paia_gemv_tp_wait.restype = I
         lib.paia_gemv_tp_wait.argtypes = [P, ctypes.c_uint, P]
         # --- B200 additions
+        lib.paia_gemv_layer.restype = I
+        lib.paia_gemv_layer.argtypes = [I, I, I, ctypes.POINTER(GemvOp), P, P]
+        lib.paia_gemv_plan_create.restype = I
+        lib.paia_gemv_plan_create.argtypes = [I, I, I, ctypes.POINTER(GemvOp), ctypes.POINTER(P)]
+        lib.paia_gemv_plan_launch.restype = I
+        lib.paia_gemv_plan_launch.argtypes = [P, P]
+        lib.paia_gemv_plan_destroy.restype = I
+        lib.paia_gemv_plan_destroy.argtypes = [P]
         lib.paia_gemv_int4_asym.restype = I
         lib.paia_gemv_int4_asym.argtypes = [P, P, P, P, P, I, I, I, P]
         lib.paia_gemv_bf16_bias.restype = I
@@ -245,6 +263,30 @@ class GemvLib:
     def tp_wait(self, counters_ptr, per_call, stream=None):
         self._check(self._lib.paia_gemv_tp_wait(counters_ptr, per_call & 0xFFFFFFFF, self._st(stream)),
                     "paia_gemv_tp_wait")
+
+    def layer(self, kind, ops, counters_ptr, math=0, stream=None):
+        """One launch for a sequence of GEMVs of one format. `ops`: a list of dicts (or GemvOp) with Wq, scales,
+        zeros, x, bias, y (raw device pointers or None) and N, K; `counters_ptr`: len(ops) + 1 zeroed uint32 on the
+        device (left zero by the kernel)."""
+        if not 1 <= len(ops) <= MAX_LAYER_OPS:
+            raise ValueError(f"a layer launch takes 1..{MAX_LAYER_OPS} ops, got {len(ops)}")
+        arr = (GemvOp * len(ops))(*[o if isinstance(o, GemvOp) else GemvOp(**o) for o in ops])
+        self._check(self._lib.paia_gemv_layer(_KINDS[kind], math, len(ops), arr, counters_ptr, self._st(stream)),
+                    "paia_gemv_layer")
+
+    def plan_create(self, kind, ops, math=0):
+        """A plan for a sequence of up to 4096 GEMVs of one format (ops as for `layer`); returns its handle."""
+        arr = (GemvOp * len(ops))(*[o if isinstance(o, GemvOp) else GemvOp(**o) for o in ops])
+        h = ctypes.c_void_p()
+        self._check(self._lib.paia_gemv_plan_create(_KINDS[kind], math, len(ops), arr, ctypes.byref(h)),
+                    "paia_gemv_plan_create")
+        return h.value
+
+    def plan_launch(self, plan, stream=None):
+        self._check(self._lib.paia_gemv_plan_launch(plan, self._st(stream)), "paia_gemv_plan_launch")
+
+    def plan_destroy(self, plan):
+        self._check(self._lib.paia_gemv_plan_destroy(plan), "paia_gemv_plan_destroy")
 
     def device_error(self, clear=True):
         """The device-side error word (0 = none) written by kernels whose bounded waits gave up."""

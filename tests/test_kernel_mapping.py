@@ -297,11 +297,15 @@ def tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec=0):
     nb = tma_part_bufs(max(ring, 2), nch)
     i4 = fmt.startswith("int4")
     return (640 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * (3 if i4 and dec == 2 else 2) + 64
-            + (kp // 128 * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * 4 + 16)
+            + (kp // 128 * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * 4 + 160)
 
 
-def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0):
-    """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged."""
+def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
+    """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged.
+    Layer mode (`ops`: a list of (N, K)): K is the largest K, one chunk size for all ops, nch the smallest op NCH, and
+    a seventh element, the list of per-op NCH."""
+    if ops:
+        K = max(k for _, k in ops)
     rowbytes = ROWBYTES[fmt](K)
     if ring == 1 or ring > 16:
         return None
@@ -321,6 +325,16 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0):
     kc0 = min(need, kc_max)
     nch = (rowbytes + kc0 - 1) // kc0
     kc = ((rowbytes + nch - 1) // nch + 63) // 64 * 64
+    op_nch = None
+    if ops:
+        best = -1.0
+        for c in range(kc0, max(kc_max // 4, 64) - 1, -64):
+            used = sum(ROWBYTES[fmt](k) * n for n, k in ops)
+            held = sum((ROWBYTES[fmt](k) + c - 1) // c * c * n for n, k in ops)
+            if used / held > best + 0.005:
+                best, kc = used / held, c
+        op_nch = [(ROWBYTES[fmt](k) + kc - 1) // kc for _, k in ops]
+        nch = min(op_nch)
     rs = kc + 64 if kc % 128 == 0 else kc
     st_bytes = (16 * rs + 127) // 128 * 128
     auto_ring = ring == 0
@@ -332,7 +346,9 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0):
     while auto_ring and total > cap and ring > 2:
         ring -= 1
         total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec)
-    return (kc, nch, rs, st_bytes, ring, total) if total <= cap else None
+    if total > cap:
+        return None
+    return (kc, nch, rs, st_bytes, ring, total) + ((op_nch,) if ops else ())
 
 
 def meta_copy_u16(mod, T, e0, n, slot, lanes=32):
@@ -365,6 +381,15 @@ def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
     geo = tma_prep(fmt, NC, K, ring, cap)
     assert geo is not None, (fmt, K, NC, ring, share)
     KC, NCH, RS, ST_BYTES, ST, smem = geo
+    G = grid(N, sms, per_sm)
+    nsts = replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G)
+    for nst in nsts:
+        replay_ring(nst, ST, NC, [i // NCH for i in range(nst)], tma_part_bufs(ST, NCH))
+
+
+def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G):
+    """Stage-level checks of one GEMV streamed with geometry (KC, NCH, RS, ST_BYTES) by G CTAs; returns the number of
+    stages of every CTA."""
     assert smem <= cap and KC % 64 == 0 and RS % 16 == 0 and ST_BYTES % 128 == 0 and 2 <= ST <= 16
     assert 16 * RS <= ST_BYTES
     CS = KC // 64
@@ -377,14 +402,15 @@ def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
     Kp = (K + SK - 1) // SK * SK
     groups = K // 128
     assert NCH * KC >= rowbytes and (NCH - 1) * KC < rowbytes
-    G = grid(N, sms, per_sm)
     copied = np.zeros((N, nchunk), dtype=np.int32)
     consumed = np.zeros((N, nchunk), dtype=np.int32)
     stores = np.zeros(N, dtype=np.int32)
+    nsts = []
     for blk in range(G):
         rb, re = blk * N // G, (blk + 1) * N // G
         T = (re - rb + 15) >> 4
         nst = T * NCH
+        nsts.append(nst)
         # --- producer: copies and metadata
         for i in range(nst):
             t, j = divmod(i, NCH)
@@ -444,38 +470,70 @@ def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
                 for g in range(16):
                     if r0 + g < re:
                         stores[r0 + g] += 1
-        # --- mbarrier protocol: the producer may fill stage i once stage i - ring is released by all NC warps; a
-        # stage is readable once filled (copies and metadata complete on its full barrier). Consumers run at most
-        # ring - 1 stages ahead of the slowest warp, so the tile-partial buffers in use stay below NB.
-        NB = tma_part_bufs(ST, NCH)
-        assert (ST - 1 + NCH - 1) // NCH + 1 < NB
-        released = [0] * nst
-        issued, consumed_upto, steps = 0, 0, 0
-        while consumed_upto < nst:
-            steps += 1
-            assert steps < 4 * nst + 16, "mbarrier protocol stalled"
-            progressed = False
-            if issued < nst and (issued < ST or released[issued - ST] == NC):
-                issued += 1
-                progressed = True
-            if consumed_upto < issued:
-                released[consumed_upto] = NC
-                consumed_upto += 1
-                progressed = True
-            assert progressed, "deadlock"
-        # producer/consumer mbarrier parities follow the rounds of the ring: wait k of slot s has parity k & 1
-        ph, s = 0, 0
-        for i in range(nst):
-            if i >= ST:
-                assert ph == ((i // ST) - 1) & 1
-            s += 1
-            if s == ST:
-                s = 0
-                if i >= ST:
-                    ph ^= 1
     assert np.all(copied == 1), f"{fmt} N={N} K={K}: copies min {copied.min()} max {copied.max()}"
     assert np.all(consumed == 1), f"{fmt} N={N} K={K}: consumed min {consumed.min()} max {consumed.max()}"
     assert np.all(stores == 1)
+    return nsts
+
+
+def replay_ring(nst, ST, NC, tile_of, NB):
+    """The full/empty mbarrier protocol of one CTA's stream of nst stages (tile_of[i]: the tile, numbered over the whole
+    stream, that stage i belongs to): the producer may fill stage i once stage i - ST is released by all NC warps; a
+    stage is readable once filled. A warp may run up to ST - 1 stages ahead of the slowest one, so the tiles in flight
+    between them must fit the NB tile-partial buffers (one more for the epilogue's read)."""
+    for i in range(nst):
+        assert tile_of[i] - tile_of[max(0, i - (ST - 1))] + 2 <= NB, (i, ST, NB)
+    released = [0] * nst
+    issued, consumed_upto, steps = 0, 0, 0
+    while consumed_upto < nst:
+        steps += 1
+        assert steps < 4 * nst + 16, "mbarrier protocol stalled"
+        progressed = False
+        if issued < nst and (issued < ST or released[issued - ST] == NC):
+            issued += 1
+            progressed = True
+        if consumed_upto < issued:
+            released[consumed_upto] = NC
+            consumed_upto += 1
+            progressed = True
+        assert progressed, "deadlock"
+    # producer/consumer mbarrier parities follow the rounds of the ring: wait k of slot s has parity k & 1
+    ph, s = 0, 0
+    for i in range(nst):
+        if i >= ST:
+            assert ph == ((i // ST) - 1) & 1
+        s += 1
+        if s == ST:
+            s = 0
+            if i >= ST:
+                ph ^= 1
+
+
+def replay_layer(fmt, ops, NC, U, sms=148, dec=0):
+    """Replay of a layer launch (one CTA per SM): one stage geometry for every op, each op's stages checked as a GEMV of
+    its own, and the ring protocol over the concatenated stream of all ops' stages (slots, parities and tile-partial
+    buffers continue across op boundaries). Also the x region: every op's staged x fits the one sized for the
+    largest K."""
+    geo = tma_prep(fmt, NC, 0, 0, SMEM_CAP, dec, ops=ops)
+    assert geo is not None, (fmt, ops)
+    KC, NCH_MIN, RS, ST_BYTES, ST, smem, op_nch = geo
+    G = min(sms, max(n for n, _ in ops))
+    Kmax = max(k for _, k in ops)
+    SK = MMA_STEP_K[fmt]
+    per_cta = [[] for _ in range(G)]
+    for (N, K), nch in zip(ops, op_nch):
+        assert (K + SK - 1) // SK * SK <= (Kmax + SK - 1) // SK * SK
+        nsts = replay_tma_op(fmt, N, K, NC, U, KC, nch, RS, ST_BYTES, ST, smem, SMEM_CAP, G)
+        for blk in range(G):
+            per_cta[blk].append((nsts[blk], nch))
+    NB = tma_part_bufs(ST, NCH_MIN)
+    for blk in range(G):
+        tile_of, base = [], 0
+        for nst, nch in per_cta[blk]:
+            tile_of += [base + i // nch for i in range(nst)]
+            base += nst // nch
+        replay_ring(len(tile_of), ST, NC, tile_of, NB)
+    return geo
 
 
 TMA_SHAPES = dict(SHAPES)
@@ -494,6 +552,33 @@ def test_tma_mapping_exactly_once(fmt):
             assert K > 16384 or ring == 16, (fmt, K, ring, share)   # only long rows or deep rings may not fit
             continue
         replay_tma(fmt, N, K, NC, ring, U, sms=rnd.choice((148, 7, 1)), per_sm=rnd.choice((1, 2)), share=share)
+
+
+LAYERS = {
+    # Llama-3.1-8B decode layer (qkv, o, gate_up, down) and Qwen2.5-7B, plus a chain with ragged and tiny N
+    "llama": [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)],
+    "qwen": [(4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944)],
+    "ragged": [(1536, 1024), (1024, 1536), (14336, 1024), (100, 14336), (40, 256), (3000, 128)],
+}
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int4", "int4_asym"])
+@pytest.mark.parametrize("name", list(LAYERS))
+def test_layer_mapping(fmt, name):
+    ops = LAYERS[name]
+    if name == "ragged":
+        replay_layer(fmt, ops, 8, 2, sms=rnd_sms(fmt))
+    kc, nch, rs, st_bytes, ring, smem, op_nch = tma_prep(fmt, 8, 0, 0, SMEM_CAP, 0, ops=ops)
+    # real layers: the stages are >= 97% full over the layer's weight bytes and the ring still holds >= 3 stages
+    if name != "ragged":
+        used = sum(ROWBYTES[fmt](k) * n for n, k in ops)
+        held = sum(c * kc * n for (n, _), c in zip(ops, op_nch))
+        assert used / held >= 0.97, (fmt, name, kc, used / held)
+        assert ring >= 3 and smem <= SMEM_CAP
+
+
+def rnd_sms(fmt):
+    return {"bf16": 148, "fp8": 7, "int4": 148, "int4_asym": 3}[fmt]
 
 
 def test_tma_prep_geometry():
