@@ -147,6 +147,8 @@ typedef struct paia_gemv_op {
     const void* bias;     /* bf16 [N] or NULL */
     void* y;              /* bf16 [N] */
     int N, K;
+    int act;              /* 0: x as given; 1: x holds [gate | up] (2K bf16) and the op reads bf16(SiLU(gate) * up),
+                             SiLU(v) = v / (1 + e^-v) in fp32 (the activation between gate_up and down, fused) */
 } paia_gemv_op;
 int paia_gemv_layer(int kind, int math, int nops, const paia_gemv_op* ops, unsigned int* counters, void* stream);
 

@@ -247,6 +247,16 @@ def dequant_int4_to_bf16(packed, scales16):
     return out
 
 
+def silu_mul(gu_bits):
+    """bf16(SiLU(gate) * up) of x = [gate | up] (bf16 bits, 2K values), SiLU(v) = v / (1 + e^-v) carried in fp64 and
+    rounded once: the activation a fused gate_up projection feeds the down projection."""
+    v = bf16_to_f32(_c(gu_bits, np.uint16)).astype(np.float64)
+    K = v.shape[0] // 2
+    g, u = v[:K], v[K:]
+    with np.errstate(over="ignore"):                   # e^-g overflows to inf for g << 0: SiLU -> -0
+        return f64_to_bf16(g / (1.0 + np.exp(-g)) * u)
+
+
 # ------------------------------------------------------------------ comparison metrics
 
 def rel_l2(y_bits, ref_bits):

@@ -297,7 +297,8 @@ int fill_ops(int kind, int nops, const paia_gemv_op* ops, pb2::GemvOp* out, int*
         const paia_gemv_op& o = ops[j];
         const int rc = check_args(kind, o.Wq, o.scales, o.zeros, o.x, o.bias, o.y, o.N, o.K);
         if (rc) return rc;
-        const uintptr_t x0 = (uintptr_t)o.x, x1 = x0 + 2 * (size_t)o.K;
+        if (o.act != kActNone && o.act != kActSiluMul) return -2;
+        const uintptr_t x0 = (uintptr_t)o.x, x1 = x0 + 2 * (size_t)o.K * (o.act == kActSiluMul ? 2 : 1);
         const uintptr_t y0 = (uintptr_t)o.y, y1 = y0 + 2 * (size_t)o.N;
         if (x0 < y1 && y0 < x1) return -2;                   // other CTAs store y while x is still being read
         GemvOp& g = out[j];
@@ -312,6 +313,7 @@ int fill_ops(int kind, int nops, const paia_gemv_op* ops, pb2::GemvOp* out, int*
         g.K = o.K;
         g.nchunk = row_bytes(kind, o.K) / 16;
         g.groups = o.K / 128;
+        g.act = o.act;
         *maxN = o.N > *maxN ? o.N : *maxN;
     }
     return 0;

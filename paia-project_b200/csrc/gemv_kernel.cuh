@@ -48,7 +48,8 @@ enum : int { kBF16 = 0, kFP8 = 1, kINT4 = 2, kINT4A = 3 };
 // each product rounded to bf16 (the activation between a fused gate_up projection and the down projection).
 enum : int { kActNone = 0, kActSiluMul = 1 };
 
-// One GEMV of a fused sequence (TMA kernels' layer mode): operands and shape; nch = stages per 16-row tile.
+// One GEMV of a fused sequence (TMA kernels' layer mode): operands and shape, and its stage geometry: nch stages per
+// 16-row tile, kc row bytes per stage, rs shared-memory row stride.
 struct GemvOp {
     const uint8_t* W;
     const void* s;
@@ -56,7 +57,7 @@ struct GemvOp {
     const __nv_bfloat16* x;
     const __nv_bfloat16* bias;
     __nv_bfloat16* y;
-    int N, K, nchunk, groups, nch, act;
+    int N, K, nchunk, groups, nch, act, kc, rs;
 };
 constexpr int kMaxOps = 6;             // ops carried in the kernel parameters
 constexpr int kMaxPlanOps = 4096;       // ops of a plan (device-memory op table)
@@ -73,6 +74,8 @@ struct Params {
     int ks_log2;                   // log2(KS): warps that share a row
     int groups;                    // K / 128 (INT4 formats)
     int kc, nch, rs, st_bytes;     // TMA kernels: bytes per row per stage, stages per tile, smem row stride, stage size
+    int cs_slot;                   // TMA kernels: 64-byte steps a stage slot holds per row
+    int mr;                        // TMA kernels: halves per row of a stage's metadata slot
     int ring;                      // TMA kernels: stages in the shared-memory ring
     int pre;                       // TMA kernels: stages streamed before x is staged (0 = the whole ring)
     // Row-sharded tensor parallelism (TMA kernels; tp_world = 0: off). This rank computes rows [0, N) of its shard and

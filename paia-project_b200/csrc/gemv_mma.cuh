@@ -115,10 +115,17 @@ __host__ __device__ constexpr size_t mma_smem_bytes(int K) {
 // second pass over x then costs no memory round when K <= 32 nthr).
 // x as the staging helpers see it: the vector, its length, and the transform applied on load (kActSiluMul: x holds
 // [gate | up], 2K values, and the staged value is bf16(SiLU(gate) * up)).
+// kx: the staged length (zero-filled past K; 0 = mma_kpad(K)).
 struct XSrc {
     const __nv_bfloat16* x;
     int K;
     int act = 0;
+    int kx = 0;
+};
+// Which 16-byte blocks of x a staging pass visits: count(n) blocks, the q-th being block idx(q); XAll visits all n.
+struct XAll {
+    __device__ __forceinline__ int count(int n) const { return n; }
+    __device__ __forceinline__ int idx(int q) const { return q; }
 };
 // x is loaded at L2 (ld.global.cg): in a fused sequence of GEMVs it is the output of the previous one, written by
 // other CTAs of the same grid, so the non-coherent read-only path must not serve it.
@@ -135,52 +142,74 @@ __device__ __forceinline__ uint32_t silu_mul2(uint32_t g, uint32_t u) {
     const __nv_bfloat162 r = __floats2bfloat162_rn(a0, a1);
     return *reinterpret_cast<const uint32_t*>(&r);
 }
-// 16-byte block i of the staged x (i < K / 8).
-__device__ __forceinline__ uint4 x_block(const XSrc& p, const uint4* x4, int nx, int i) {
-    if (p.act == kActSiluMul) {
+// 16-byte block i of the staged x (i < K / 8); ACT: the SiLU(gate) * up transform (a compile-time choice, so the
+// loads of a round issue back to back).
+template <bool ACT>
+__device__ __forceinline__ uint4 x_block(const uint4* x4, int nx, int i) {
+    if constexpr (ACT) {
         const uint4 g = ld_x16(x4 + i), u = ld_x16(x4 + nx + i);
         return make_uint4(silu_mul2(g.x, u.x), silu_mul2(g.y, u.y), silu_mul2(g.z, u.z), silu_mul2(g.w, u.w));
     }
     return ld_x16(x4 + i);
 }
 
-template <int CACHE = 0, typename Fn>
-__device__ __forceinline__ void x_blocks(const XSrc& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
+// R blocks per thread per round (R loads in flight); CACHE 1 keeps the first round's blocks in c[0 .. R), CACHE 2 takes
+// them from there. The map is taken by value: a stateful map (a cursor over its runs) restarts on every pass, and
+// sees q in increasing order within a thread.
+template <bool ACT, int CACHE, int R, typename Fn, typename Map>
+__device__ __forceinline__ void x_blocks_t(const XSrc& p, int tid, int nthr, int n0, Fn& fn, uint4* c, Map map) {
     const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
-    const int nx = p.K / 8;
-    for (int i0 = tid, r = 0; i0 < n; i0 += 4 * nthr, ++r) {
-        uint4 v[4];
+    const int nx = p.K / 8, n = map.count(n0);
+    for (int i0 = tid, r = 0; i0 < n; i0 += R * nthr, ++r) {
+        uint4 v[R];
+        int ii[R];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int i = i0 + k * nthr;
+        for (int k = 0; k < R; ++k) {
+            const int q = i0 + k * nthr;
+            ii[k] = q < n ? map.idx(q) : nx;
             if (CACHE == 2 && r == 0) v[k] = c[k];
-            else v[k] = i < nx ? x_block(p, x4, nx, i) : make_uint4(0u, 0u, 0u, 0u);
+            else v[k] = ii[k] < nx ? x_block<ACT>(x4, nx, ii[k]) : make_uint4(0u, 0u, 0u, 0u);
             if (CACHE == 1 && r == 0) c[k] = v[k];
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (i0 + k * nthr < n) fn(i0 + k * nthr, v[k]);
+        for (int k = 0; k < R; ++k)
+            if (i0 + k * nthr < n) fn(ii[k], v[k]);
     }
 }
-// As x_blocks, but every thread calls fn(i, v) in every round (i may be >= n; v is then zero), so fn may use
-// warp shuffles; blocks i0 + tid of a round belong to consecutive lanes.
-template <int CACHE = 0, typename Fn>
-__device__ __forceinline__ void x_blocks_all(const XSrc& p, int tid, int nthr, int n, Fn fn, uint4* c = nullptr) {
+template <int CACHE = 0, int R = 4, typename Fn, typename Map = XAll>
+__device__ __forceinline__ void x_blocks(const XSrc& p, int tid, int nthr, int n0, Fn fn, uint4* c = nullptr,
+                                         Map map = Map()) {
+    if (p.act == kActSiluMul) x_blocks_t<true, CACHE, R>(p, tid, nthr, n0, fn, c, map);
+    else x_blocks_t<false, CACHE, R>(p, tid, nthr, n0, fn, c, map);
+}
+// As x_blocks, but every thread calls fn(i, v) in every round (i may be >= the staged length; v is then zero), so fn
+// may use warp shuffles; blocks q0 + tid of a round belong to consecutive lanes (with a Map, 16 consecutive q of a
+// 16-aligned run map to one 128-group: runs are whole groups).
+template <bool ACT, int CACHE, int R, typename Fn, typename Map>
+__device__ __forceinline__ void x_blocks_all_t(const XSrc& p, int tid, int nthr, int n0, Fn& fn, uint4* c, Map map) {
     const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
-    const int nx = p.K / 8;
-    for (int i0 = 0, r = 0; i0 < n; i0 += 4 * nthr, ++r) {
-        uint4 v[4];
+    const int nx = p.K / 8, n = map.count(n0);
+    for (int i0 = 0, r = 0; i0 < n; i0 += R * nthr, ++r) {
+        uint4 v[R];
+        int ii[R];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int i = i0 + k * nthr + tid;
+        for (int k = 0; k < R; ++k) {
+            const int q = i0 + k * nthr + tid;
+            ii[k] = q < n ? map.idx(q) : (1 << 30);
             if (CACHE == 2 && r == 0) v[k] = c[k];
-            else v[k] = i < nx ? x_block(p, x4, nx, i) : make_uint4(0u, 0u, 0u, 0u);
+            else v[k] = ii[k] < nx ? x_block<ACT>(x4, nx, ii[k]) : make_uint4(0u, 0u, 0u, 0u);
             if (CACHE == 1 && r == 0) c[k] = v[k];
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (i0 + k * nthr < n) fn(i0 + k * nthr + tid, v[k]);
+        for (int k = 0; k < R; ++k)
+            if (i0 + k * nthr < n) fn(ii[k], v[k]);
     }
+}
+template <int CACHE = 0, int R = 4, typename Fn, typename Map = XAll>
+__device__ __forceinline__ void x_blocks_all(const XSrc& p, int tid, int nthr, int n0, Fn fn, uint4* c = nullptr,
+                                             Map map = Map()) {
+    if (p.act == kActSiluMul) x_blocks_all_t<true, CACHE, R>(p, tid, nthr, n0, fn, c, map);
+    else x_blocks_all_t<false, CACHE, R>(p, tid, nthr, n0, fn, c, map);
 }
 
 // Stage x for the tensor-core kernels (padded with zeros to Kpad): BF16 as is; FP8 as f16 scaled by 2^-e (e from the
@@ -188,14 +217,15 @@ __device__ __forceinline__ void x_blocks_all(const XSrc& p, int tid, int nthr, i
 // expects; INT4 with each 8-block permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7) plus the sum of every 128-group.
 // Called by `nthr` threads (thread index tid); `sync` is the barrier over exactly those threads; `scratch` holds
 // nthr/32 floats. Ends with x visible to the caller only after the caller's own barrier.
-template <int F, int DEC, int GST = 1, typename Sync>
+// With a Map, only the mapped blocks are staged (and the max is taken over them). XR: blocks per thread per round.
+template <int F, int DEC, int GST = 1, int XR = 4, typename Sync, typename Map = XAll>
 __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum, float* xscale, float* scratch, int tid,
-                                        int nthr, Sync sync) {
+                                        int nthr, Sync sync, const Map& map = Map()) {
     // INT4 group sums are written GST words apart (the integer path needs 8 words per group)
     static_assert(!(F == kINT4 || F == kINT4A) || DEC != 2 || GST == 8, "integer INT4 staging needs 8 words per group");
-    const int Kp = mma_kpad<F>(p.K);
+    const int Kp = p.kx ? p.kx : mma_kpad<F>(p.K);
     if constexpr (F == kBF16) {
-        x_blocks(p, tid, nthr, Kp / 8, [&](int i, uint4 v) { reinterpret_cast<uint4*>(xs)[i] = v; });   // K % 8 == 0
+        x_blocks<0, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) { reinterpret_cast<uint4*>(xs)[i] = v; }, nullptr, map);   // K % 8 == 0
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     } else if constexpr (F == kFP8 && DEC == 3) {
         // x * 2^-e (max|x| * 2^-e in [128, 256)) split into two e4m3 terms hi + lo, bytes in natural order: hi at xs,
@@ -203,11 +233,11 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         // exactly for |v| >= 2^-2 (bf16 carries 8 significant bits); smaller values keep an absolute error below
         // 2^-10, i.e. < 2^-17 of max|x|.
         float m = 0.f;
-        uint4 xc[4] = {};
-        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+        uint4 xc[XR] = {};
+        x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }, xc);
+        }, xc, map);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -228,7 +258,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         const float inv = xscale[1];
         uint8_t* xh = reinterpret_cast<uint8_t*>(xs);
         uint8_t* xl = xh + Kp + 64;          // +64: hi and lo reads of one quarter-warp fall in different banks
-        x_blocks<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
+        x_blocks<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             uint2 h = make_uint2(0u, 0u), l = make_uint2(0u, 0u);
             if (8 * i < p.K) {
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
@@ -248,15 +278,15 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
             }
             reinterpret_cast<uint2*>(xh)[i] = h;
             reinterpret_cast<uint2*>(xl)[i] = l;
-        }, xc);
+        }, xc, map);
     } else if constexpr (F == kFP8) {
         // max |x| over the CTA, then x * 2^-e in f16 (exact while max|x| * 2^-e < 2^15 and values stay normal)
         float m = 0.f;
-        uint4 xc[4] = {};
-        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+        uint4 xc[XR] = {};
+        x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }, xc);
+        }, xc, map);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -275,7 +305,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         }
         sync();
         const float inv = xscale[1];
-        x_blocks<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
+        x_blocks<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             uint4 o = make_uint4(0u, 0u, 0u, 0u);
             if (8 * i < p.K) {
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
@@ -294,7 +324,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
                 o = make_uint4(oo[0], oo[1], oo[2], oo[3]);
             }
             reinterpret_cast<uint4*>(xs)[i] = o;
-        }, xc);
+        }, xc, map);
     } else if constexpr (DEC == 2) {
         // INT4 for the integer MMA: v = x * 2^s rounded to an integer below 2^20 in magnitude (exact for every element
         // within 2^12 of max|x|, bf16 carrying 8 significant bits; smaller ones keep an error below 2^-21 max|x|),
@@ -304,15 +334,15 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
         float m = 0.f;
         bool bad = false;
-        uint4 xc[4] = {};
-        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+        uint4 xc[XR] = {};
+        x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 bad |= ((vv[j] & 0x7F800000u) == 0x7F800000u) || ((vv[j] & 0x7F80u) == 0x7F80u);
                 m = fmaxf(m, fmaxf(fabsf(bf_lo(vv[j])), fabsf(bf_hi(vv[j]))));
             }
-        }, xc);
+        }, xc, map);
         if (__any_sync(0xffffffffu, bad)) m = __int_as_float(0x7F800000);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -341,7 +371,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         const float up2 = __uint_as_float((uint32_t)(127 + (sh > 0 ? sh - sh / 2 : sh)) << 23);
         uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
         int* gi = reinterpret_cast<int*>(gsum);
-        x_blocks_all<2>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
+        x_blocks_all<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             // blocks past K / 8 arrive as zeros and stage as zero digits
             float sd[3] = {0.f, 0.f, 0.f};
             if (i < Kp / 8) {
@@ -377,18 +407,18 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
                 for (int d = 0; d < 3; ++d) gi[8 * gg + d] = (int)sd[d];
                 gsum[8 * gg + 4] = sd[0] + 128.f * sd[1] + 16384.f * sd[2];
             }
-        }, xc);
+        }, xc, map);
     } else if constexpr (DEC == 1) {
         // INT4 for the f16 nibble decode: x * 2^-e in f16 (max|x| * 2^-e in [2^13, 2^14)), 8-element blocks stored as
         // pairs (x0,x4),(x2,x6),(x1,x5),(x3,x7) (even k feed the "1024 + n" MMA, odd k the "1024 + 16 n" MMA); per
         // 128-group g: gsum[GST g] = 1032 S_even + 72 S_odd (the decode and symmetric offsets), gsum[GST g + 1] =
         // S_even + S_odd, over the f16 values the MMA sees.
         float m = 0.f;
-        uint4 xc[4] = {};
-        x_blocks<1>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
+        uint4 xc[XR] = {};
+        x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }, xc);
+        }, xc, map);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -408,7 +438,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         sync();
         const float inv = xscale[1];
         const int nb = p.K / 8;                                  // K % 128 == 0 -> nb % 16 == 0
-        x_blocks_all<2>(p, tid, nthr, nb, [&](int i, uint4 v) {
+        x_blocks_all<2, XR>(p, tid, nthr, nb, [&](int i, uint4 v) {
             float se = 0.f, so = 0.f;
             if (i < nb) {
                 const __half2 h01 = __floats2half2_rn(bf_lo(v.x) * inv, bf_hi(v.x) * inv);
@@ -433,11 +463,11 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
                 gsum[GST * (i >> 4)] = 1032.f * se + 72.f * so;
                 gsum[GST * (i >> 4) + 1] = se + so;
             }
-        }, xc);
+        }, xc, map);
     } else {
         // 8-element blocks permuted to pairs (x0,x4),(x1,x5),(x2,x6),(x3,x7); sum of each 128-group (16 blocks)
         const int nb = p.K / 8;                                  // K % 128 == 0 -> nb % 16 == 0
-        x_blocks_all(p, tid, nthr, nb, [&](int i, uint4 v) {
+        x_blocks_all<0, XR>(p, tid, nthr, nb, [&](int i, uint4 v) {
             float sum = 0.f;
             if (i < nb) {
                 const uint32_t pr0 = (v.x & 0xFFFFu) | (v.z << 16);            // (x0, x4)
@@ -451,7 +481,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);   // 16-lane groups
             if (i < nb && (i & 15) == 0) gsum[GST * (i >> 4)] = sum;
-        });
+        }, nullptr, map);
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     }
 }

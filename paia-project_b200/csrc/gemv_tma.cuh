@@ -1,25 +1,27 @@
 // TMA-fed tensor-core GEMV for B200 (sm_100a): the streaming design of the decode GEMV family.
 //
 // Measured on B200: loading MMA fragments straight from HBM (each warp instruction touching 16 rows x 64 B) stops at
-// ~4.4-5.4 TB/s, while bulk copies of contiguous pieces of >= ~2 KB stream at ~6.0-6.3 TB/s with ~170-190 KB in flight
-// per SM. So a producer warp moves the weights with cp.async.bulk (1-D TMA, completion counted on an mbarrier) into
-// a ring of shared-memory stages, and consumer warps read the MMA fragments from shared memory.
+// ~4.4-5.4 TB/s, while bulk copies stream at up to ~6.6 TB/s. A CTA's copy throughput is bounded by the number of
+// bulk copies (about 15 million per second per SM), not only by the bytes in flight: at ~190 KB in flight per SM,
+// 4 KB copies reach HBM speed and 0.7 KB copies a quarter of it. So a producer warp moves the weights in as few,
+// large cp.async.bulk copies as possible (1-D TMA, completion counted on an mbarrier) into a ring of shared-memory
+// stages, and consumer warps read the MMA fragments from shared memory.
 //
-//   CTA       one persistent CTA per SM (or two when the ring is small); rows [c N/G, (c+1) N/G), cut into 16-row
-//             tiles; a tile is streamed as NCH stages of 16 rows x KC bytes (KC a multiple of 64, pieces >= ~2 KB).
-//   producer  warp NC. Lane 0 waits for the slot, then lane r issues row r's bulk copy (rows beyond the CTA's range are not
-//             copied; their MMA rows compute garbage that is never stored) into a padded layout (row stride KC or
-//             KC + 64, so that the two rows a fragment load phase touches sit in different bank halves). The
-//             producer starts at launch, before the programmatic-dependency wait: weights never depend on the
-//             preceding kernel. All 32 lanes then copy the stage's metadata (INT4 scales and zeros of its rows and
-//             groups; FP8 row scales and the bias at a tile's last stage) with 4-byte cp.async, whose completion is
-//             also counted on the stage's `full` mbarrier, so no register ever waits on a load: under a saturated
-//             memory system a plain load takes as long as the whole ring's copies. 2-byte arrays are copied as the
-//             aligned words that hold them (the element parity is recomputed by the readers); a word that would
-//             reach past either end of its array is read with plain loads instead.
+//   CTA       one persistent CTA per SM; rows [c N/G, (c+1) N/G), cut into 16-row tiles; a tile is streamed as NCH
+//             stages of 16 rows x KC bytes (a whole row when it fits the slot, else equal chunks, a multiple of 64).
+//   producer  warp NC. Lane 0 waits for the slot; then a whole-row stage of short rows (< 3 KB) is two bulk copies
+//             (tile rows 0-7 and 8-15, contiguous in global memory) and any other stage one copy per row (rows
+//             beyond the CTA's range are not copied; their MMA rows compute garbage that is never stored). The two
+//             8-row blocks sit 8 RS + 64 bytes apart and MMA rows are mapped to tile rows so that the two rows a
+//             fragment load phase touches lie in different blocks (different bank halves). The producer starts at
+//             launch, before the programmatic-dependency wait: weights never depend on the preceding kernel. All 32
+//             lanes then copy the stage's metadata (INT4 scales and zeros of its rows and groups) with one bulk copy
+//             per array when the run is 16-byte aligned, else as the 16-byte blocks that hold it (cp.async), whose
+//             completion is also counted on the stage's `full` mbarrier, so no register ever waits on a load: under
+//             a saturated memory system a plain load takes as long as the whole ring's copies.
 //   consumers warps 0..NC-1 wait for the dependency, stage x (as gemv_mma.cuh), then for every stage take an equal
-//             share of its 64-byte steps, load A fragments from the stage (rows g and g+8, bytes 16c of each step),
-//             B fragments from x, and run the dequantisation and mma.sync of the format. The step loop is
+//             share of its 64-byte steps, load A fragments from the stage (MMA rows g and g+8, bytes 16c of each
+//             step), B fragments from x, and run the dequantisation and mma.sync of the format. The step loop is
 //             branch-free (U steps per iteration; the remainder and the ragged last step of a row run one at a time)
 //             and keeps two accumulator chains per step. At the last stage of a tile each warp leaves its 16 partial
 //             sums in a shared-memory buffer and arrives on the buffer's `tile_done` mbarrier; no consumer waits
@@ -27,8 +29,11 @@
 //   epilogue  warp NC+1 adds each tile's NC partials in warp order (deterministic), applies the row scale, the x
 //             scale and the bias (loaded from global memory while the tile is computed), writes the 16 outputs and
 //             frees the buffer (`part_free`), so the tile-end work never stalls the consumers.
-//   waits     every mbarrier wait gives up after ~2 s (%globaltimer), records an error code that
-//             paia_gemv_device_error() reports, and carries on without waiting, so a fault can never hang the GPU.
+//   layer     one launch may stream a sequence of GEMVs (layer mode: Params::nops); the ring, the partial buffers
+//             and their phases run on across op boundaries, and the consumers of op j wait for every CTA's outputs
+//             of op j - 1 (a per-op completion counter) before they stage x of op j.
+//   waits     every wait gives up after ~2 s (%globaltimer), records an error code that paia_gemv_device_error()
+//             reports, and carries on without waiting, so a fault can never hang the GPU.
 #pragma once
 #include "gemv_mma.cuh"
 
@@ -96,23 +101,20 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* m) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" :: "r"(smem_addr(m)) : "memory");
 }
 
-// Word k of the copy of elements [e0, e0 + n) of a 2-byte array a[0, T) into dst (4-byte aligned): the aligned words
-// that hold the range land in dst[2k], dst[2k + 1], so element e sits at dst[u16_parity(a + e0) + e - e0]. A word that
-// reaches outside a[0, T) is read with plain loads of its in-range halves.
-__device__ __forceinline__ int u16_parity(const void* p) { return (int)(((uintptr_t)p >> 1) & 1u); }
-__device__ __forceinline__ int u16_words(const uint16_t* a, long long e0, int n) {
-    const uintptr_t b = (uintptr_t)(a + e0);
-    return (int)(((b + 2 * (uintptr_t)n - 1) >> 2) - (b >> 2) + 1);
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void u16_word_copy(uint16_t* dst, const uint16_t* a, long long T, long long e0, int k) {
-    const uintptr_t w = (((uintptr_t)(a + e0)) & ~(uintptr_t)3) + 4 * (uintptr_t)k;
-    const uintptr_t lo = (uintptr_t)a, hi = (uintptr_t)(a + T);
-    if (w >= lo && w + 4 <= hi) {
-        cp_async4(dst + 2 * k, (const void*)w);
-    } else {
-        if (w >= lo && w + 2 <= hi) dst[2 * k] = ld_u16((const void*)w);
-        if (w + 2 >= lo && w + 4 <= hi) dst[2 * k + 1] = ld_u16((const void*)(w + 2));
-    }
+// Block k of the copy of elements [e0, e0 + n) of a 2-byte array a (any 2-byte alignment) into dst (16-byte aligned):
+// the 16-byte aligned blocks that hold the range land in dst[8k .. 8k + 7], so element e sits at
+// dst[u16_off16(a + e0) + e - e0]. The first and last block may reach a few bytes past the array's ends; an aligned
+// 16-byte block that holds a byte of the array lies in the same memory page, so those bytes are readable (and unused).
+__device__ __forceinline__ int u16_off16(const void* p) { return (int)(((uintptr_t)p >> 1) & 7u); }
+__device__ __forceinline__ int u16_blocks16(const uint16_t* a, long long e0, int n) {
+    const uintptr_t b = (uintptr_t)(a + e0);
+    return (int)(((b + 2 * (uintptr_t)n - 1) >> 4) - (b >> 4) + 1);
+}
+__device__ __forceinline__ void u16_block_copy(uint16_t* dst, const uint16_t* a, long long e0, int k) {
+    cp_async16(dst + 8 * k, (const void*)((((uintptr_t)(a + e0)) & ~(uintptr_t)15) + 16 * (uintptr_t)k));
 }
 
 constexpr int kTmaMaxRing = 16;        // ring stages at most
@@ -121,12 +123,15 @@ constexpr int kTmaMaxParts = kTmaMaxRing + 1;   // tile-partial buffers at most
 constexpr int kTmaBarBytes = 640;
 constexpr int kTmaTailBytes = 160;     // x scale of two ops (2 x 4 floats) + x staging scratch (32 floats)
 
-// Metadata slot of a stage (bytes): FP8 row scales float[16] at 0; bias words (18 halves) at 64; INT4 scales and
-// (INT4A) zeros at 112, 16 rows x tma_meta_row(CS) halves each.
-__host__ __device__ constexpr int tma_meta_row(int cs) { return (cs + 3) & ~1; }     // >= CS + 2 halves, even
+// Metadata slot of a stage (bytes): INT4 scales and (INT4A) zeros at 112, 16 rows x tma_meta_row(CS) halves each
+// (CS: 64-byte steps per row the slot holds; a row's run is copied as the 16-byte blocks that hold it, which span
+// at most CS + 14 halves, and a whole-row tile's run of 16 x CS halves as blocks spanning at most 16 CS + 14).
+// Halves per metadata row, a multiple of 8 (16-byte rows): >= CS + 14 when some row is chunked (a chunk's run copied as
+// 16-byte blocks), else >= CS + 1 (whole-row tiles: 16 G halves plus at most 14 of block slack in 16 rows).
+__host__ __device__ constexpr int tma_meta_row(int cs, bool chunked) { return chunked ? (cs + 21) & ~7 : (cs + 8) & ~7; }
 template <int F>
-__host__ __device__ constexpr int tma_meta_bytes(int cs) {
-    return 112 + ((F == kINT4 || F == kINT4A) ? 16 * tma_meta_row(cs) * 2 * (F == kINT4A ? 2 : 1) : 0);
+__host__ __device__ constexpr int tma_meta_bytes(int mr) {
+    return 112 + ((F == kINT4 || F == kINT4A) ? 16 * mr * 2 * (F == kINT4A ? 2 : 1) : 0);
 }
 // INT4 per-group sums in shared memory: 8 words per group for the integer path (digit sums and sum x), else 2.
 __host__ __device__ constexpr int tma_gsum_words(int dec) { return dec == 2 ? 8 : 2; }
@@ -134,14 +139,21 @@ __host__ __device__ constexpr int tma_gsum_words(int dec) { return dec == 2 ? 8 
 // tiles; one more lets the epilogue warp lag a tile before a consumer waits for a free buffer.
 __host__ __device__ constexpr int tma_part_bufs(int ring, int nch) { return (ring - 1 + nch - 1) / nch + 2; }
 
+// Staged x length: K rounded up to whole 64-byte weight steps (32 BF16, 64 FP8, 128 INT4 weights), so that every
+// x read of a row's ragged last step lands on staged zeros.
+template <int F>
+__host__ __device__ constexpr int tma_kx(int K) {
+    return F == kBF16 ? (K + 31) / 32 * 32 : (F == kFP8 ? (K + 63) / 64 * 64 : (K + 127) / 128 * 128);
+}
+
 // Shared-memory layout (bytes): [0,640) mbarriers; ring x st_bytes; metadata ring x tma_meta_bytes (16-byte
-// multiples); x: Kpad x 2 (INT4 integer path: Kpad x 3) + 64 (FP8 lo plane at Kpad + 64, INT4 planes Kpad + 16
-// apart); INT4 group sums
-// (tma_gsum_words per group); tile partials NB x NC x 16 floats; x scales of two ops and staging scratch (160 bytes).
+// multiples); x: Kx x 2 (INT4 integer path: Kx x 3) + 64 (FP8 lo plane at Kx + 64, INT4 planes Kx + 16 apart);
+// INT4 group sums (tma_gsum_words per group); tile partials NB x NC x 16 floats; per consumer warp its x scale
+// (4 floats) and a staging scratch word (kTmaTailBytes).
 template <int F, int NC, int DEC>
-__host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int kc, int st_bytes) {
-    const int kp = mma_kpad<F>(K);
-    const size_t mb = (size_t)(tma_meta_bytes<F>(kc / 64) + 15) / 16 * 16;
+__host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int mr, int st_bytes) {
+    const int kp = tma_kx<F>(K);
+    const size_t mb = (size_t)(tma_meta_bytes<F>(mr) + 15) / 16 * 16;
     const int nb = tma_part_bufs(ring < 2 ? 2 : ring, nch);
     // x: 2 bytes per element (3 for the INT4 integer path's digit planes)
     constexpr size_t xb = ((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2;
@@ -150,13 +162,56 @@ __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int k
            kTmaTailBytes;
 }
 
+// Stage layouts (bytes from the stage base). Chunked and long rows: row r at r x RS, RS = KC (+ 64 when KC is a
+// multiple of 128), so the two rows of a fragment load phase (MMA rows g, g + 1) sit in different bank halves; MMA
+// row m reads tile row m; every row is one bulk copy of its chunk. Short whole rows (a multiple of 64 bytes, below
+// kTmaBlockRow; RS = row bytes): rows 0-7 and rows 8-15 of a tile are two blocks 8 RS + 64 bytes apart, each one bulk
+// copy (contiguous rows in global memory and in the block), and MMA row m reads tile row tma_tile_row(m), so that the
+// two rows of an access phase lie in different blocks (64 bytes apart modulo 128).
+// Rows at least kTmaBlockRow long stream at full speed one copy per row; shorter rows go 8 per copy (measured on
+// B200: 2 KB copies cap a CTA near 30 GB/s, 4 KB copies do not limit it).
+constexpr int kTmaBlockRow = 3072;
+__host__ __device__ constexpr bool tma_blocked(int nch, int kc, int rs) {
+    return nch == 1 && rs == kc && kc < kTmaBlockRow;
+}
+__host__ __device__ constexpr int tma_row_off(int r, int rs, bool blocked) {
+    return blocked ? (r >> 3) * (8 * rs + 64) + (r & 7) * rs : r * rs;
+}
+__host__ __device__ constexpr int tma_tile_row(int m, bool blocked) {
+    return blocked ? (((m & 1) << 3) | ((m >> 1) & 3) | (m & 8 ? 4 : 0)) : m;
+}
+__host__ __device__ constexpr int tma_stage_bytes(int rs, bool blocked) {
+    return (16 * rs + (blocked ? 64 : 0) + 127) / 128 * 128;
+}
+
+// Host: the stage geometry of a row of `nchunk` 16-byte chunks in a slot of `kcs` bytes per row (a multiple of 64):
+// the whole row when it fits (nch 1, kc = row bytes), else nch equal chunks of kc bytes (a multiple of 64), and the
+// row stride of the layout above.
+inline void tma_op_geometry(int nchunk, int kcs, int* nch, int* kc, int* rs) {
+    const long rb = (long)nchunk * 16;
+    long c = rb;
+    int n = 1;
+    if (rb > kcs) {
+        n = (int)((rb + kcs - 1) / kcs);
+        c = ((rb + n - 1) / n + 63) / 64 * 64;
+    }
+    *nch = n;
+    *kc = (int)c;
+    if (n == 1 && rb % 64 == 0 && rb < kTmaBlockRow) {
+        *rs = (int)rb;                                         // blocked layout
+    } else {
+        const long c64 = (c + 63) / 64 * 64;
+        *rs = (int)(c64 % 128 == 0 ? c64 + 64 : c64);
+    }
+}
+
 // Host: choose the stage geometry for this shape within `cap` bytes of shared memory and return the dynamic shared
-// memory size (0 when it cannot be staged). A row is split into NCH equal chunks of KC bytes (a multiple of 64, at most
-// 4096 so that a 16-row stage stays <= 64 KB; INT4 at most 2048, i.e. <= 32 groups of metadata per stage). p.ring on
-// entry is the requested ring depth (>= 2), or 0 for as many stages as fit (2..16; KC then sized for >= 3 stages).
-// Layer mode (p.nops > 0): the ops share one stage geometry, chosen for the longest row; p.K and p.nchunk become the
-// largest K and row, each op gets its own NCH (stages per row) and p.nch the smallest of them (the most tiles a ring
-// can span, which sizes the partial buffers).
+// memory size (0 when it cannot be staged). The slot holds 16 rows x KCS bytes (KCS a multiple of 64, at most 4096 so
+// that a stage stays <= 64 KB). p.ring on entry is the requested ring depth (>= 2), or 0 for as many stages as fit
+// (2..16; KCS then sized for >= 3 stages). Single GEMV: KCS = the row split into the fewest equal chunks that fit.
+// Layer mode (p.nops > 0): one slot size for every op (the largest that fits next to x of the largest K), each op
+// staged in its own geometry within it; p.K and p.nchunk become the largest K and row, p.nch the smallest op NCH
+// (the most tiles a ring can span, which sizes the partial buffers).
 template <int F, int NC, int DEC>
 size_t tma_prep(Params& p, size_t cap) {
     GemvOp* ops = p.host_ops ? p.host_ops : p.ops;
@@ -173,60 +228,61 @@ size_t tma_prep(Params& p, size_t cap) {
     const int want = p.ring;
     if (want == 1 || want > kTmaMaxRing) return 0;
     // everything but the ring and its metadata (partial buffers sized for a 4-stage ring; checked again below)
-    const size_t fixed = tma_smem_bytes<F, NC, DEC>(p.K, 0, 1, 64, 0) + (size_t)3 * (NC * 64 + 4);
+    const size_t fixed = tma_smem_bytes<F, NC, DEC>(p.K, 0, 1, 0, 0) + (size_t)3 * (NC * 64 + 4);
     if (fixed >= cap) return 0;
-    // a stage needs at most 16 (KC + 64) + 128 ring bytes and 112 + 2 x 2 x 16 (KC/64 + 3) + 15 metadata bytes
+    // a stage needs at most 16 KCS + 192 ring bytes and 112 + 2 x 2 x 16 (KCS/64 + 3) + 15 metadata bytes
     const size_t per_stage_cap = (cap - fixed) / (want >= 2 ? want : 3);
     if (per_stage_cap < 1536 + 17 * 64) return 0;
     long kc_max = (long)(per_stage_cap - 1536) / 17;
     if (kc_max > 65536 / 16) kc_max = 65536 / 16;
-    if (F == kINT4 || F == kINT4A) kc_max = kc_max > 2048 ? 2048 : kc_max;
     kc_max = kc_max / 64 * 64;
     if (kc_max < 64) return 0;
     const long need = (long)((rowbytes + 63) / 64 * 64);
     const long kc0 = need < kc_max ? need : kc_max;
-    int nch = (int)((rowbytes + kc0 - 1) / kc0);
-    long kc = (long)((rowbytes + nch - 1) / nch);
-    kc = (kc + 63) / 64 * 64;
-    if (p.nops > 0) {
-        // one chunk size for every op: the largest whose stages are fullest over the whole sequence (weight bytes of
-        // all ops / ring bytes their stages occupy), among chunks down to a quarter of the largest that fits
-        double best = -1.0;
-        const long lo = kc_max / 4 > 64 ? kc_max / 4 : 64;
-        for (long c = kc0; c >= lo; c -= 64) {
-            double used = 0.0, held = 0.0;
-            for (int j = 0; j < p.nops; ++j) {
-                const double rb = (double)ops[j].nchunk * 16;
-                used += rb * ops[j].N;
-                held += (double)((long)(rb + c - 1) / c) * c * ops[j].N;
-            }
-            if (used / held > best + 0.005) { best = used / held; kc = c; }
-        }
-        nch = (int)((rowbytes + kc - 1) / kc);
+    long kcs = kc0;
+    if (p.nops == 0) {                                         // fewest equal chunks
+        const long n = (long)((rowbytes + kc0 - 1) / kc0);
+        kcs = (long)(((rowbytes + n - 1) / n + 63) / 64 * 64);
     }
-    p.kc = (int)kc;
-    p.nch = nch;
-    p.rs = (int)(kc % 128 == 0 ? kc + 64 : kc);
-    p.st_bytes = (16 * p.rs + 127) / 128 * 128;
-    if (p.nops > 0) {
-        int mn = nch;
+    p.cs_slot = (int)(kcs / 64);
+    int rs_max = 0;
+    if (p.nops == 0) {
+        tma_op_geometry(p.nchunk, (int)kcs, &p.nch, &p.kc, &p.rs);
+        rs_max = p.rs;
+    } else {
+        int mn = 1 << 30;
         for (int j = 0; j < p.nops; ++j) {
             GemvOp& o = ops[j];
-            o.nch = (int)(((size_t)o.nchunk * 16 + kc - 1) / kc);
+            tma_op_geometry(o.nchunk, (int)kcs, &o.nch, &o.kc, &o.rs);
             mn = o.nch < mn ? o.nch : mn;
+            rs_max = o.rs > rs_max ? o.rs : rs_max;
         }
         p.nch = mn;
+        p.kc = (int)kcs;
+        p.rs = rs_max;
+    }
+    bool chunked = p.nops == 0 ? p.nch > 1 : false;
+    for (int j = 0; j < p.nops; ++j) chunked = chunked || ops[j].nch > 1;
+    p.mr = tma_meta_row(p.cs_slot, chunked);
+    p.st_bytes = 0;
+    if (p.nops == 0) {
+        p.st_bytes = tma_stage_bytes(p.rs, tma_blocked(p.nch, p.kc, p.rs));
+    } else {
+        for (int j = 0; j < p.nops; ++j) {
+            const int sb = tma_stage_bytes(ops[j].rs, tma_blocked(ops[j].nch, ops[j].kc, ops[j].rs));
+            p.st_bytes = sb > p.st_bytes ? sb : p.st_bytes;
+        }
     }
     int ring = want;
     if (ring == 0) {
-        const size_t per_stage = (size_t)p.st_bytes + (size_t)(tma_meta_bytes<F>((int)kc / 64) + 15) / 16 * 16;
+        const size_t per_stage = (size_t)p.st_bytes + (size_t)(tma_meta_bytes<F>(p.mr) + 15) / 16 * 16;
         const size_t fit = (cap - fixed) / per_stage;
         ring = fit > (size_t)kTmaMaxRing ? kTmaMaxRing : (int)fit;
         if (ring < 2) return 0;
     }
-    size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, p.nch, p.kc, p.st_bytes);
+    size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, p.nch, p.mr, p.st_bytes);
     while (want == 0 && total > cap && ring > 2)               // deeper rings need more partial buffers
-        total = tma_smem_bytes<F, NC, DEC>(p.K, --ring, p.nch, p.kc, p.st_bytes);
+        total = tma_smem_bytes<F, NC, DEC>(p.K, --ring, p.nch, p.mr, p.st_bytes);
     p.ring = ring;
     return total <= cap ? total : 0;
 }
@@ -403,7 +459,8 @@ __device__ __forceinline__ GemvOp tma_op(const Params& p, int j) {
     if (p.nops > 0) return p.ops[j];
     GemvOp o;
     o.W = p.W; o.s = p.s; o.z = p.z; o.x = p.x; o.bias = p.bias; o.y = p.y;
-    o.N = p.N; o.K = p.K; o.nchunk = p.nchunk; o.groups = p.groups; o.nch = p.nch;
+    o.N = p.N; o.K = p.K; o.nchunk = p.nchunk; o.groups = p.groups; o.nch = p.nch; o.act = 0;
+    o.kc = p.kc; o.rs = p.rs;
     return o;
 }
 
@@ -426,13 +483,12 @@ template <int F, int NC, int U, int DEC = 0>
 __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid_constant__ Params p) {
     constexpr bool I4 = (F == kINT4 || F == kINT4A);
     extern __shared__ __align__(128) uint8_t smem[];
-    // geometry shared by every op of the launch (p.K: the largest K, p.nch: the smallest NCH)
-    const int KC = p.kc, RS = p.rs;
+    // geometry shared by every op of the launch (p.K: the largest K, p.nch: the smallest NCH, p.cs_slot: the slot)
     const int ST = p.ring;                                    // 2..16 stages (the host checks)
     const int NB = tma_part_bufs(ST, p.nch);
-    const int CS = KC >> 6, MR = tma_meta_row(CS);
-    const int MB = (tma_meta_bytes<F>(CS) + 15) & ~15;
-    const int Kpm = mma_kpad<F>(p.K);
+    const int MR = p.mr;
+    const int MB = (tma_meta_bytes<F>(MR) + 15) & ~15;
+    const int Kpm = tma_kx<F>(p.K);
     const int nops = p.nops > 0 ? p.nops : 1;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kTmaMaxRing;
@@ -468,7 +524,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         uint32_t ph = 0;                                      // parity of the slot's previous release
         for (int jo = 0; jo < nops; ++jo) {
             const GemvOp op = tma_op(p, jo);
-            const int NCH = op.nch;
+            const int NCH = op.nch, KC = op.kc, RS = op.rs, CS = KC >> 6;
+            const bool dense = tma_blocked(NCH, KC, RS);     // short whole rows: one copy per 8-row block
             const int S = (op.nchunk + 3) >> 2;
             const size_t rowbytes = (size_t)op.nchunk * 16;
             const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
@@ -506,9 +563,17 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     }
                 }
                 __syncwarp();                                 // the slot is free and its byte count announced
-                if (lane < nrows)
-                    bulk_copy_g2s_ef(ring + (size_t)s * p.st_bytes + (size_t)lane * RS,
+                uint8_t* sdst = ring + (size_t)s * p.st_bytes;
+                if (dense) {                                  // rows 8b .. 8b + 7 of the tile: one copy per block
+                    if (lane < 2 && nrows > 8 * lane) {
+                        const int nb = nrows - 8 * lane < 8 ? nrows - 8 * lane : 8;
+                        bulk_copy_g2s_ef(sdst + (size_t)lane * (8 * RS + 64), op.W + (size_t)(r0 + 8 * lane) * rowbytes,
+                                         (uint32_t)(nb * rowbytes), &full[s], wpol);
+                    }
+                } else if (lane < nrows) {
+                    bulk_copy_g2s_ef(sdst + (size_t)lane * RS,
                                      op.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s], wpol);
+                }
                 uint8_t* ms = meta + (size_t)s * MB;
                 if constexpr (I4) {
                     uint16_t* msc = reinterpret_cast<uint16_t*>(ms + 112);
@@ -519,25 +584,25 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                         const long long e0 = (long long)r0 * op.groups;
                         const int n = nrows * op.groups;
                         if (!meta_bulk) {
-                            const int nw = u16_words(sa, e0, n);
-                            for (int k = lane; k < nw; k += 32) u16_word_copy(msc, sa, NG, e0, k);
-                            if constexpr (F == kINT4A)
-                                for (int k = lane; k < nw; k += 32) u16_word_copy(msc + 16 * MR, za, NG, e0, k);
+                            const int nb = u16_blocks16(sa, e0, n);
+                            for (int k = lane; k < nb; k += 32) u16_block_copy(msc, sa, e0, k);
+                            if constexpr (F == kINT4A) {
+                                const int nz = u16_blocks16(za, e0, n);
+                                for (int k = lane; k < nz; k += 32) u16_block_copy(msc + 16 * MR, za, e0, k);
+                            }
                         }
                     } else {
-                        // rows x words of this stage's scale (and zero) runs, spread over the lanes; every row
-                        // copies the (nsteps + 2) / 2 words that hold its run for either element parity
-                        const int wpr = (nsteps + 2) >> 1;
-                        int rr = lane / wpr, k = lane - rr * wpr;
-                        const int drr = 32 / wpr, dk = 32 - drr * wpr;
-                        while (rr < nrows) {
-                            const long long e0 = (long long)(r0 + rr) * op.groups + (long long)j * CS;
-                            if (k < u16_words(sa, e0, nsteps)) u16_word_copy(msc + rr * MR, sa, NG, e0, k);
-                            if constexpr (F == kINT4A)
-                                if (k < u16_words(za, e0, nsteps)) u16_word_copy(msc + (16 + rr) * MR, za, NG, e0, k);
-                            rr += drr;
-                            k += dk;
-                            if (k >= wpr) { k -= wpr; ++rr; }
+                        // rows x 16-byte blocks of this stage's scale (and zero) runs, spread over the lanes (a run of
+                        // nsteps halves spans at most (nsteps + 21) / 8 blocks)
+                        const int bpr = (nsteps + 21) >> 3;
+                        for (int it = lane; it < 16 * bpr; it += 32) {
+                            const int rr = it / bpr, k = it - rr * bpr;
+                            if (rr < nrows) {
+                                const long long e0 = (long long)(r0 + rr) * op.groups + (long long)j * CS;
+                                if (k < u16_blocks16(sa, e0, nsteps)) u16_block_copy(msc + rr * MR, sa, e0, k);
+                                if constexpr (F == kINT4A)
+                                    if (k < u16_blocks16(za, e0, nsteps)) u16_block_copy(msc + (16 + rr) * MR, za, e0, k);
+                            }
                         }
                     }
                 }
@@ -580,6 +645,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     float total = 0.f;
 #pragma unroll
                     for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
+                    // row scale first, then the x scale (products that only the row scale keeps finite stay finite)
                     float out = total;
                     if constexpr (F == kFP8)                  // row scale, then 2^e (a normal power of two)
                         out = out * rs * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
@@ -651,16 +717,18 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             if (lane == 0) wait_count(&p.layer_done[jo - 1], gridDim.x, 7);
             __syncwarp();
         }
-        const int NCH = op.nch;
+        const int NCH = op.nch, RS = op.rs, CS = op.kc >> 6;
+        const bool blk = tma_blocked(NCH, op.kc, RS);
+        const int m0 = tma_tile_row(g, blk), m1 = tma_tile_row(g + 8, blk);   // tile rows of MMA rows g, g + 8
         const int S = (op.nchunk + 3) >> 2;                   // 64-byte steps per row
         const int SF = op.nchunk >> 2;                        // steps whose four 16-byte chunks are all in the row
-        const int Kp = mma_kpad<F>(op.K);
+        const int Kp = tma_kx<F>(op.K);
         const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
         const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
         const int nst = ((re - rb + 15) >> 4) * NCH;
         if (nst > 0) {                                        // CTA-uniform: a CTA without rows of the op skips x
-            stage_x<F, DEC, tma_gsum_words(DEC)>(XSrc{op.x, op.K}, xs, gsum, xscale + 4 * (jo & 1), xscr, tid,
-                                                 NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+            stage_x<F, DEC, tma_gsum_words(DEC)>(XSrc{op.x, op.K, op.act, Kp}, xs, gsum, xscale + 4 * (jo & 1), xscr,
+                                                 tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
             consumer_barrier(1, NC * 32);
         }
         if (jo == 0 && tid == 0) {
@@ -678,27 +746,27 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             const int sa0 = warp * nsteps / NC, sb0 = (warp + 1) * nsteps / NC;
             const uint8_t* st = ring + (size_t)s * p.st_bytes;
             const uint8_t* ms = meta + (size_t)s * MB;
-            const uint8_t* r0p = st + (size_t)g * RS + 16 * c;
-            const uint8_t* r1p = r0p + (size_t)8 * RS;
+            const uint8_t* r0p = st + tma_row_off(m0, RS, blk) + 16 * c;
+            const uint8_t* r1p = st + tma_row_off(m1, RS, blk) + 16 * c;
             const uint16_t* msc = reinterpret_cast<const uint16_t*>(ms + 112);
             const uint16_t *sc0 = msc, *sc1 = msc, *zr0 = msc, *zr1 = msc;
             if constexpr (I4) {
                 if (NCH == 1) {                               // the tile's run: row rr at rr x G (+ run parity)
                     const long long e0 = (long long)r0 * op.groups;
-                    sc0 = msc + u16_parity(sa + e0) + g * op.groups;
-                    sc1 = sc0 + 8 * op.groups;
+                    sc0 = msc + u16_off16(sa + e0) + m0 * op.groups;
+                    sc1 = msc + u16_off16(sa + e0) + m1 * op.groups;
                     if constexpr (F == kINT4A) {
-                        zr0 = msc + 16 * MR + u16_parity(za + e0) + g * op.groups;
-                        zr1 = zr0 + 8 * op.groups;
+                        zr0 = msc + 16 * MR + u16_off16(za + e0) + m0 * op.groups;
+                        zr1 = msc + 16 * MR + u16_off16(za + e0) + m1 * op.groups;
                     }
                 } else {                                      // per-row runs: row rr at rr x MR (+ row parity)
-                    const long long e0 = (long long)(r0 + g) * op.groups + (long long)j * CS;
-                    const long long e1 = e0 + 8LL * op.groups;
-                    sc0 = msc + g * MR + u16_parity(sa + e0);
-                    sc1 = msc + (g + 8) * MR + u16_parity(sa + e1);
+                    const long long e0 = (long long)(r0 + m0) * op.groups + (long long)j * CS;
+                    const long long e1 = (long long)(r0 + m1) * op.groups + (long long)j * CS;
+                    sc0 = msc + m0 * MR + u16_off16(sa + e0);
+                    sc1 = msc + m1 * MR + u16_off16(sa + e1);
                     if constexpr (F == kINT4A) {
-                        zr0 = msc + (16 + g) * MR + u16_parity(za + e0);
-                        zr1 = msc + (24 + g) * MR + u16_parity(za + e1);
+                        zr0 = msc + (16 + m0) * MR + u16_off16(za + e0);
+                        zr1 = msc + (16 + m1) * MR + u16_off16(za + e1);
                     }
                 }
             }
@@ -743,7 +811,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 if (tg >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile tg - NB
                 ++tg;
                 float* buf = part + (size_t)b * NC * 16;
-                if (c == 0) { buf[warp * 16 + g] = s0; buf[warp * 16 + g + 8] = s1; }
+                if (c == 0) { buf[warp * 16 + m0] = s0; buf[warp * 16 + m1] = s1; }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tdone[b]);         // release: this warp's partials of the tile
                 if (++b == NB) { b = 0; bph ^= 1u; }

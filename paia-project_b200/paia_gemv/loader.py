@@ -44,10 +44,12 @@ class VariantEx(ctypes.Structure):
 
 
 class GemvOp(ctypes.Structure):
-    """paia_gemv_op: one GEMV of a layer launch (raw device pointers; unused ones None)."""
+    """paia_gemv_op: one GEMV of a layer launch (raw device pointers; unused ones None). act = ACT_SILU_MUL: x holds
+    [gate | up] (2K values) and the op reads bf16(SiLU(gate) * up)."""
     _fields_ = [("Wq", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("zeros", ctypes.c_void_p),
                 ("x", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p),
-                ("N", ctypes.c_int), ("K", ctypes.c_int)]
+                ("N", ctypes.c_int), ("K", ctypes.c_int), ("act", ctypes.c_int)]
+    ACT_NONE, ACT_SILU_MUL = 0, 1
 
 
 MAX_LAYER_OPS = 6

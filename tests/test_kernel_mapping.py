@@ -278,12 +278,12 @@ def share_cap(share):
     return min(SMEM_CAP, SM_SMEM // share - (1024 if share > 1 else 0))
 
 
-def tma_meta_row(cs):
-    return (cs + 3) & ~1
+def tma_meta_row(cs, chunked):
+    return (cs + 21) & ~7 if chunked else (cs + 8) & ~7
 
 
-def tma_meta_bytes(fmt, cs):
-    i4 = 16 * tma_meta_row(cs) * 2 * (2 if fmt == "int4_asym" else 1) if fmt.startswith("int4") else 0
+def tma_meta_bytes(fmt, mr):
+    i4 = 16 * mr * 2 * (2 if fmt == "int4_asym" else 1) if fmt.startswith("int4") else 0
     return (112 + i4 + 15) // 16 * 16
 
 
@@ -291,117 +291,172 @@ def tma_part_bufs(ring, nch):
     return (ring - 1 + nch - 1) // nch + 2
 
 
-def tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec=0):
+def tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec=0):
     SK = MMA_STEP_K[fmt]
     kp = (K + SK - 1) // SK * SK
     nb = tma_part_bufs(max(ring, 2), nch)
     i4 = fmt.startswith("int4")
-    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, kc // 64)) + kp * (3 if i4 and dec == 2 else 2) + 64
+    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, mr)) + kp * (3 if i4 and dec == 2 else 2) + 64
             + (kp // 128 * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * 4 + 160)
+
+
+BLOCK_ROW = 3072                                               # kTmaBlockRow
+
+
+def tma_blocked(nch, kc, rs):
+    return nch == 1 and rs == kc and kc < BLOCK_ROW
+
+
+def tma_row_off(r, rs, blocked):
+    """Byte offset of tile row r in a stage: padded rows r x rs, or two 8-row blocks 8 rs + 64 apart."""
+    return (r >> 3) * (8 * rs + 64) + (r & 7) * rs if blocked else r * rs
+
+
+def tma_tile_row(m, blocked):
+    """Tile row that MMA row m (0..15) reads."""
+    return (((m & 1) << 3) | ((m >> 1) & 3) | (4 if m & 8 else 0)) if blocked else m
+
+
+def tma_stage_bytes(rs, blocked):
+    return (16 * rs + (64 if blocked else 0) + 127) // 128 * 128
+
+
+def tma_op_geometry(nchunk, kcs):
+    """Mirror of tma_op_geometry: (nch, kc, rs) of a row of nchunk 16-byte chunks in a slot of kcs bytes per row."""
+    rb = nchunk * 16
+    c, n = rb, 1
+    if rb > kcs:
+        n = (rb + kcs - 1) // kcs
+        c = ((rb + n - 1) // n + 63) // 64 * 64
+    if n == 1 and rb % 64 == 0 and rb < BLOCK_ROW:
+        return n, c, rb
+    c64 = (c + 63) // 64 * 64
+    return n, c, c64 + 64 if c64 % 128 == 0 else c64
 
 
 def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
     """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged.
-    Layer mode (`ops`: a list of (N, K)): K is the largest K, one chunk size for all ops, nch the smallest op NCH, and
-    a seventh element, the list of per-op NCH."""
+    Layer mode (`ops`: a list of (N, K)): K is the largest K, one slot size (kc = the slot's bytes per row) for all
+    ops, nch the smallest op NCH, rs the largest op row stride, and a seventh element, the list of per-op
+    (nch, kc, rs)."""
     if ops:
         K = max(k for _, k in ops)
-    rowbytes = ROWBYTES[fmt](K)
+    rowbytes = max(ROWBYTES[fmt](k) for _, k in ops) if ops else ROWBYTES[fmt](K)
     if ring == 1 or ring > 16:
         return None
-    fixed = tma_smem_bytes(fmt, NC, K, 0, 1, 64, 0, dec) + 3 * (NC * 64 + 4)
+    fixed = tma_smem_bytes(fmt, NC, K, 0, 1, 0, 0, dec) + 3 * (NC * 64 + 4)
     if fixed >= cap:
         return None
     per_stage_cap = (cap - fixed) // (ring if ring >= 2 else 3)
     if per_stage_cap < 1536 + 17 * 64:
         return None
-    kc_max = min((per_stage_cap - 1536) // 17, 65536 // 16)
-    if fmt.startswith("int4"):
-        kc_max = min(kc_max, 2048)
-    kc_max = kc_max // 64 * 64
+    kc_max = min((per_stage_cap - 1536) // 17, 65536 // 16) // 64 * 64
     if kc_max < 64:
         return None
-    need = (rowbytes + 63) // 64 * 64
-    kc0 = min(need, kc_max)
-    nch = (rowbytes + kc0 - 1) // kc0
-    kc = ((rowbytes + nch - 1) // nch + 63) // 64 * 64
-    op_nch = None
+    kc0 = min((rowbytes + 63) // 64 * 64, kc_max)
     if ops:
-        best = -1.0
-        for c in range(kc0, max(kc_max // 4, 64) - 1, -64):
-            used = sum(ROWBYTES[fmt](k) * n for n, k in ops)
-            held = sum((ROWBYTES[fmt](k) + c - 1) // c * c * n for n, k in ops)
-            if used / held > best + 0.005:
-                best, kc = used / held, c
-        op_nch = [(ROWBYTES[fmt](k) + kc - 1) // kc for _, k in ops]
-        nch = min(op_nch)
-    rs = kc + 64 if kc % 128 == 0 else kc
-    st_bytes = (16 * rs + 127) // 128 * 128
+        kcs = kc0
+        geos = [tma_op_geometry(ROWBYTES[fmt](k) // 16, kcs) for _, k in ops]
+        nch = min(g[0] for g in geos)
+        rs = max(g[2] for g in geos)
+        kc = kcs
+        st_bytes = max(tma_stage_bytes(g[2], tma_blocked(*g)) for g in geos)
+    else:
+        n = (rowbytes + kc0 - 1) // kc0
+        kcs = ((rowbytes + n - 1) // n + 63) // 64 * 64
+        nch, kc, rs = tma_op_geometry(rowbytes // 16, kcs)
+        st_bytes = tma_stage_bytes(rs, tma_blocked(nch, kc, rs))
+    chunked = any(g[0] > 1 for g in geos) if ops else nch > 1
+    mr = tma_meta_row(kcs // 64, chunked)
     auto_ring = ring == 0
     if ring == 0:
-        ring = min(16, (cap - fixed) // (st_bytes + tma_meta_bytes(fmt, kc // 64)))
+        ring = min(16, (cap - fixed) // (st_bytes + tma_meta_bytes(fmt, mr)))
         if ring < 2:
             return None
-    total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec)
+    total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec)
     while auto_ring and total > cap and ring > 2:
         ring -= 1
-        total = tma_smem_bytes(fmt, NC, K, ring, nch, kc, st_bytes, dec)
+        total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec)
     if total > cap:
         return None
-    return (kc, nch, rs, st_bytes, ring, total) + ((op_nch,) if ops else ())
+    if ops:
+        return (kc, nch, rs, st_bytes, ring, total, geos)
+    return (kc, nch, rs, st_bytes, ring, total)
+
+
+def check_banks(rs, blocked):
+    """Every shared-memory access phase of the consumers' 16-byte fragment loads (8 lanes: MMA rows 2m', 2m'+1 of the
+    first or second load, bytes 16c of one 64-byte step) touches each of the 32 banks once."""
+    for second in (0, 8):
+        for mp in range(4):
+            for step_off in (0, 64, 128, 192, 64 * 37):
+                banks = []
+                for m in (2 * mp + second, 2 * mp + 1 + second):
+                    r = tma_tile_row(m, blocked)
+                    for c in range(4):
+                        a = tma_row_off(r, rs, blocked) + step_off + 16 * c
+                        banks += [(a // 4 + w) % 32 for w in range(4)]
+                assert sorted(banks) == list(range(32)), (rs, second, mp, step_off)
 
 
 def meta_copy_u16(mod, T, e0, n, slot, lanes=32):
-    """Mirror of u16_words / u16_word_copy for a 2-byte array at byte address `mod` (mod 4) with T elements: every word
-    copied with cp.async lies inside the array, partial words are read half by half inside it, the copy fits its
-    shared-memory slot of `slot` halves, and every element of [e0, e0 + n) lands at parity + (e - e0)."""
+    """Mirror of u16_blocks16 / u16_block_copy for a 2-byte array at byte address `mod` (mod 16) with T elements: every
+    16-byte block copied holds at least one byte of the array (so it lies in a page the array occupies), the copy fits
+    its shared-memory slot of `slot` halves, and every element of [e0, e0 + n) lands at off16 + (e - e0)."""
     b = mod + 2 * e0
-    nw = ((b + 2 * n - 1) >> 2) - (b >> 2) + 1
-    assert 1 <= nw and (lanes is None or nw <= lanes) and 2 * nw <= slot
+    nb = ((b + 2 * n - 1) >> 4) - (b >> 4) + 1
+    assert 1 <= nb and (lanes is None or nb <= lanes) and 8 * nb <= slot, (mod, e0, n, nb, slot)
     lo, hi = mod, mod + 2 * T
     got = {}
-    for k in range(nw):
-        w = (b & ~3) + 4 * k
-        halves = [w, w + 2] if (w >= lo and w + 4 <= hi) else [h for h in (w, w + 2) if h >= lo and h + 2 <= hi]
-        for h in halves:
-            assert lo <= h and h + 2 <= hi
-            got[2 * k + (h - w) // 2] = (h - mod) // 2                # smem half index -> element
-    par = (b >> 1) & 1
+    for k in range(nb):
+        blk = (b & ~15) + 16 * k
+        assert blk < hi and blk + 16 > lo                          # the block overlaps the array
+        for h in range(blk, blk + 16, 2):
+            if lo <= h < hi:
+                got[8 * k + (h - blk) // 2] = (h - mod) // 2           # smem half index -> element
+    off = (b >> 1) & 7
     for e in range(e0, e0 + n):
-        assert got.get(par + e - e0) == e, (mod, T, e0, n, e)
+        assert got.get(off + e - e0) == e, (mod, T, e0, n, e)
 
 
 def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
-    """Replay of gemv_tma_kernel: per CTA the producer streams T x NCH stages through a ring of ST stages (one bulk copy
-    per valid row, KC bytes except the ragged last chunk) while the consumers split each stage's 64-byte steps into NC
-    equal ranges of <= U-step iterations. Checks copies in bounds of W and of the stage, every (row, chunk) copied and
-    consumed exactly once, metadata indices (INT4 scales per row and group, FP8 row scales, bias) in range, every
-    output stored once, and that the full/empty mbarrier protocol (metadata one stage behind) always makes progress."""
+    """Replay of gemv_tma_kernel: per CTA the producer streams T x NCH stages through a ring of ST stages (two block
+    copies per whole-row stage, else one copy per valid row, KC bytes except the ragged last chunk) while the
+    consumers split each stage's 64-byte steps into NC equal ranges of <= U-step iterations. Checks copies in bounds
+    of W and of the stage, every (row, chunk) copied and consumed exactly once, metadata indices (INT4 scales per row
+    and group, bias) in range, every output stored once, conflict-free fragment loads, and that the full/empty
+    mbarrier protocol always makes progress."""
     cap = share_cap(share)
     geo = tma_prep(fmt, NC, K, ring, cap)
     assert geo is not None, (fmt, K, NC, ring, share)
     KC, NCH, RS, ST_BYTES, ST, smem = geo
     G = grid(N, sms, per_sm)
-    nsts = replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G)
+    nsts = replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G, (KC + 63) // 64)
     for nst in nsts:
         replay_ring(nst, ST, NC, [i // NCH for i in range(nst)], tma_part_bufs(ST, NCH))
 
 
-def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G):
-    """Stage-level checks of one GEMV streamed with geometry (KC, NCH, RS, ST_BYTES) by G CTAs; returns the number of
-    stages of every CTA."""
-    assert smem <= cap and KC % 64 == 0 and RS % 16 == 0 and ST_BYTES % 128 == 0 and 2 <= ST <= 16
-    assert 16 * RS <= ST_BYTES
+def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G, CS_SLOT, CHUNKED=False):
+    """Stage-level checks of one GEMV streamed with geometry (KC, NCH, RS) in stage slots of ST_BYTES (metadata slots
+    for CS_SLOT steps per row) by G CTAs; returns the number of stages of every CTA."""
+    assert smem <= cap and RS % 64 == 0 and ST_BYTES % 128 == 0 and 2 <= ST <= 16
+    blocked = tma_blocked(NCH, KC, RS)
+    assert tma_row_off(15, RS, blocked) + RS <= ST_BYTES
+    check_banks(RS, blocked)
     CS = KC // 64
-    if fmt.startswith("int4"):
-        assert CS <= 32                                       # 2 x 16 metadata words per producer lane pair
     SK = MMA_STEP_K[fmt]
     rowbytes = ROWBYTES[fmt](K)
     nchunk = rowbytes // 16
     S = (nchunk + 3) // 4
     Kp = (K + SK - 1) // SK * SK
     groups = K // 128
-    assert NCH * KC >= rowbytes and (NCH - 1) * KC < rowbytes
+    dense = blocked
+    assert NCH * KC >= rowbytes and (NCH - 1) * KC < rowbytes and KC <= RS
+    if NCH > 1:
+        assert KC % 64 == 0 and CS <= CS_SLOT
+    else:
+        assert KC == rowbytes and (rowbytes + 63) // 64 <= max(CS_SLOT, 1) + 1
+    MR = tma_meta_row(CS_SLOT, NCH > 1 or CHUNKED)
     copied = np.zeros((N, nchunk), dtype=np.int32)
     consumed = np.zeros((N, nchunk), dtype=np.int32)
     stores = np.zeros(N, dtype=np.int32)
@@ -418,20 +473,32 @@ def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G):
             nrows = min(re - r0, 16)
             assert 1 <= nrows <= 16
             nsteps = S - j * CS if j == NCH - 1 else CS
-            assert 1 <= nsteps <= CS
+            assert 1 <= nsteps and (NCH == 1 or nsteps <= CS)
             nbytes = rowbytes - j * KC if j == NCH - 1 else KC
             assert 16 <= nbytes <= KC and nbytes % 16 == 0 and j * KC % 16 == 0
             assert nrows * nbytes < 2 ** 20                       # mbarrier transaction count range
-            for rr in range(nrows):
-                src = (r0 + rr) * rowbytes + j * KC
-                assert 0 <= src and src + nbytes <= N * rowbytes and src % 16 == 0
-                assert rr * RS + nbytes <= ST_BYTES
-                copied[r0 + rr, j * KC // 16: j * KC // 16 + nbytes // 16] += 1
+            if dense:
+                for b in range(2):
+                    nb = min(8, nrows - 8 * b)
+                    if nb <= 0:
+                        continue
+                    src = (r0 + 8 * b) * rowbytes
+                    dst = b * (8 * RS + 64)
+                    assert src % 16 == 0 and dst % 16 == 0 and (nb * rowbytes) % 16 == 0
+                    assert src + nb * rowbytes <= N * rowbytes and dst + nb * rowbytes <= ST_BYTES
+                    for rr in range(8 * b, 8 * b + nb):
+                        assert tma_row_off(rr, RS, True) == dst + (rr - 8 * b) * rowbytes
+                        copied[r0 + rr, :] += 1
+            else:
+                for rr in range(nrows):
+                    src = (r0 + rr) * rowbytes + j * KC
+                    assert 0 <= src and src + nbytes <= N * rowbytes and src % 16 == 0
+                    assert rr * RS % 16 == 0 and rr * RS + nbytes <= ST_BYTES
+                    copied[r0 + rr, j * KC // 16: j * KC // 16 + nbytes // 16] += 1
             if fmt.startswith("int4"):
-                MR = tma_meta_row(CS)
                 if NCH == 1:                                       # the tile's contiguous run, words over 32 lanes
-                    assert S <= CS and 16 * groups + 2 <= 16 * MR
-                    for mod in (0, 2):
+                    assert S <= CS_SLOT + 1 and 16 * groups + 2 <= 16 * MR
+                    for mod in range(0, 16, 2):
                         meta_copy_u16(mod, N * groups, r0 * groups, nrows * groups, 16 * MR, lanes=None)
                     if groups % 8 == 0:                            # the bulk-copy form of the same run
                         assert (2 * r0 * groups) % 16 == 0 and (2 * nrows * groups) % 16 == 0
@@ -439,13 +506,9 @@ def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G):
                 else:
                     for rr in range(nrows):
                         e0 = (r0 + rr) * groups + j * CS
-                        for mod in (0, 2):                         # array base address 0 or 2 modulo 4
-                            meta_copy_u16(mod, N * groups, e0, nsteps, MR)
-            if j == 0:
-                for lane in range(min(nrows, 32)):
-                    assert 0 <= r0 + lane < N                      # FP8 row scales (4-byte cp.async)
-                for mod in (0, 2):
-                    meta_copy_u16(mod, N, r0, nrows, 18)           # bias words
+                        for mod in range(0, 16, 2):                # array base address modulo 16
+                            meta_copy_u16(mod, N * groups, e0, nsteps, MR, lanes=None)
+                        assert 16 * ((nsteps + 21) >> 3) >= 16 * 1 and (nsteps + 21) >> 3 >= (nsteps + 14) // 8
         # --- consumers: steps of each stage, loads inside the stage, x inside Kp
         for i in range(nst):
             t, j = divmod(i, NCH)
@@ -453,10 +516,13 @@ def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G):
             nsteps = S - j * CS if j == NCH - 1 else CS
             covered = np.zeros(nsteps, dtype=np.int32)
             rend = min(r0 + 16, re)
-            assert (8 + 7) * RS + 64 * (nsteps - 1) + 16 * 3 + 16 <= ST_BYTES   # rows g, g+8, last step, lane c=3
+            for m in range(16):                                    # every MMA row's last 16-byte load in its slot
+                r = tma_tile_row(m, blocked)
+                assert 64 * (nsteps - 1) + 16 * 3 + 16 <= RS
+            assert sorted(tma_tile_row(m, blocked) for m in range(16)) == list(range(16))
             assert ((j * CS + nsteps) * SK) <= Kp                               # x reads inside the padded x
             if fmt.startswith("int4"):
-                assert j * CS + nsteps <= Kp // 128 and nsteps <= CS            # gsum and metadata indices
+                assert j * CS + nsteps <= Kp // 128                            # gsum and metadata indices
             for warp in range(NC):
                 sa, sb = warp * nsteps // NC, (warp + 1) * nsteps // NC
                 its = list(range(sa, sb, U))
@@ -516,14 +582,15 @@ def replay_layer(fmt, ops, NC, U, sms=148, dec=0):
     largest K."""
     geo = tma_prep(fmt, NC, 0, 0, SMEM_CAP, dec, ops=ops)
     assert geo is not None, (fmt, ops)
-    KC, NCH_MIN, RS, ST_BYTES, ST, smem, op_nch = geo
+    KCS, NCH_MIN, RS_MAX, ST_BYTES, ST, smem, geos = geo
     G = min(sms, max(n for n, _ in ops))
     Kmax = max(k for _, k in ops)
     SK = MMA_STEP_K[fmt]
     per_cta = [[] for _ in range(G)]
-    for (N, K), nch in zip(ops, op_nch):
-        assert (K + SK - 1) // SK * SK <= (Kmax + SK - 1) // SK * SK
-        nsts = replay_tma_op(fmt, N, K, NC, U, KC, nch, RS, ST_BYTES, ST, smem, SMEM_CAP, G)
+    for (N, K), (nch, kc, rs) in zip(ops, geos):
+        assert (K + SK - 1) // SK * SK <= (Kmax + SK - 1) // SK * SK and kc <= KCS and rs <= RS_MAX
+        nsts = replay_tma_op(fmt, N, K, NC, U, kc, nch, rs, ST_BYTES, ST, smem, SMEM_CAP, G, KCS // 64,
+                             any(g[0] > 1 for g in geos))
         for blk in range(G):
             per_cta[blk].append((nsts[blk], nch))
     NB = tma_part_bufs(ST, NCH_MIN)
@@ -568,12 +635,10 @@ def test_layer_mapping(fmt, name):
     ops = LAYERS[name]
     if name == "ragged":
         replay_layer(fmt, ops, 8, 2, sms=rnd_sms(fmt))
-    kc, nch, rs, st_bytes, ring, smem, op_nch = tma_prep(fmt, 8, 0, 0, SMEM_CAP, 0, ops=ops)
-    # real layers: the stages are >= 97% full over the layer's weight bytes and the ring still holds >= 3 stages
+    kcs, nch, rs, st_bytes, ring, smem, geos = tma_prep(fmt, 8, 0, 0, SMEM_CAP, 0, ops=ops)
+    # real layers: every op's stage pieces are >= 1.5 KB per row (few, large copies) and the ring holds >= 3 stages
     if name != "ragged":
-        used = sum(ROWBYTES[fmt](k) * n for n, k in ops)
-        held = sum(c * kc * n for (n, _), c in zip(ops, op_nch))
-        assert used / held >= 0.97, (fmt, name, kc, used / held)
+        assert all(kc >= 1536 for _, kc, _ in geos), (fmt, name, geos)
         assert ring >= 3 and smem <= SMEM_CAP
 
 

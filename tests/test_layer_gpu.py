@@ -7,6 +7,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from gpu_cases import KINDS, bits, check, make
 
 pytestmark = pytest.mark.gpu
@@ -227,3 +228,43 @@ def test_plan_argument_errors(L):
     assert f(0, 0, 1, one, None) == -2
     assert L._lib.paia_gemv_plan_launch(None, None) == -2
     assert L._lib.paia_gemv_plan_destroy(None) == 0
+
+
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("mode", ["layer", "plan"])
+def test_fused_silu_mul_between_gate_up_and_down(L, kind, mode):
+    """gate_up (2I rows) then down (K = I) reading bf16(SiLU(gate) * up) of gate_up's output, fused into the down
+    op's x staging (act = 1): down's output matches the oracle on the activation computed from the stored gate_up
+    output."""
+    from paia_gemv.loader import GemvOp
+    I, H = 1536, 1024
+    gu = make(kind, 2 * I, H, seed=300)
+    dn = make(kind, H, I, seed=301)
+    y_gu = torch.full((2 * I,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    y_dn = torch.full((H,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    ops = [op_dict(gu, gu.x, y_gu), dict(op_dict(dn, y_gu, y_dn), act=GemvOp.ACT_SILU_MUL)]
+    if mode == "layer":
+        c = counters(2)
+        L.layer(kind, ops, c.data_ptr())
+    else:
+        plan = L.plan_create(kind, ops)
+        L.plan_launch(plan)
+    torch.cuda.synchronize()
+    if mode == "plan":
+        L.plan_destroy(plan)
+    assert L.device_error(1) == 0
+    check(gu, bits(y_gu), gu.oracle()[0], f"{mode} {kind} gate_up")
+    act = O.silu_mul(bits(y_gu))
+    check(dn, bits(y_dn), dn.oracle(x_bits=act)[0], f"{mode} {kind} down(silu*mul)")
+
+
+def test_act_argument_checks(L):
+    o = make("fp8", 256, 512, seed=1)
+    c = counters(1)
+    from paia_gemv.loader import GemvOp
+    bad = (GemvOp * 1)(GemvOp(**dict(op_dict(o, o.x, o.y), act=2)))
+    assert L._lib.paia_gemv_layer(1, 0, 1, bad, c.data_ptr(), None) == -2
+    # with act = 1 x spans 2K values: a y right after the first K values overlaps it
+    xx = torch.zeros(2 * 512 + 256, dtype=torch.bfloat16, device="cuda")
+    ov = (GemvOp * 1)(GemvOp(**dict(op_dict(o, xx, xx[512:]), act=1)))
+    assert L._lib.paia_gemv_layer(1, 0, 1, ov, c.data_ptr(), None) == -2
