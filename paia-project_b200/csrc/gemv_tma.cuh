@@ -205,13 +205,44 @@ inline void tma_op_geometry(int nchunk, int kcs, int* nch, int* kc, int* rs) {
     }
 }
 
-// Host: choose the stage geometry for this shape within `cap` bytes of shared memory and return the dynamic shared
-// memory size (0 when it cannot be staged). The slot holds 16 rows x KCS bytes (KCS a multiple of 64, at most 4096 so
-// that a stage stays <= 64 KB). p.ring on entry is the requested ring depth (>= 2), or 0 for as many stages as fit
-// (2..16; KCS then sized for >= 3 stages). Single GEMV: KCS = the row split into the fewest equal chunks that fit.
-// Layer mode (p.nops > 0): one slot size for every op (the largest that fits next to x of the largest K), each op
-// staged in its own geometry within it; p.K and p.nchunk become the largest K and row, p.nch the smallest op NCH
-// (the most tiles a ring can span, which sizes the partial buffers).
+// Host: the stage geometry of every op of p (the single GEMV, or the layer list `ops`) for a slot of kcs bytes per row
+// (single GEMV: the row split into the fewest equal chunks that fit); sets p.cs_slot, p.mr, p.st_bytes and p.nch (the
+// smallest op NCH).
+template <int F>
+inline void tma_apply_slot(Params& p, GemvOp* ops, long kcs) {
+    if (p.nops == 0) {
+        const long rb = (long)p.nchunk * 16;
+        const long n = (rb + kcs - 1) / kcs;
+        kcs = ((rb + n - 1) / n + 63) / 64 * 64;
+        tma_op_geometry(p.nchunk, (int)kcs, &p.nch, &p.kc, &p.rs);
+        p.st_bytes = tma_stage_bytes(p.rs, tma_blocked(p.nch, p.kc, p.rs));
+        p.mr = tma_meta_row((int)(kcs / 64), p.nch > 1);
+    } else {
+        int mn = 1 << 30, rs_max = 0, sb_max = 0;
+        bool chunked = false;
+        for (int j = 0; j < p.nops; ++j) {
+            GemvOp& o = ops[j];
+            tma_op_geometry(o.nchunk, (int)kcs, &o.nch, &o.kc, &o.rs);
+            mn = o.nch < mn ? o.nch : mn;
+            rs_max = o.rs > rs_max ? o.rs : rs_max;
+            const int sb = tma_stage_bytes(o.rs, tma_blocked(o.nch, o.kc, o.rs));
+            sb_max = sb > sb_max ? sb : sb_max;
+            chunked = chunked || o.nch > 1;
+        }
+        p.nch = mn;
+        p.kc = (int)kcs;
+        p.rs = rs_max;
+        p.st_bytes = sb_max;
+        p.mr = tma_meta_row((int)(kcs / 64), chunked);
+    }
+    p.cs_slot = (int)(kcs / 64);
+}
+
+// Host: choose the stage geometry within `cap` bytes of shared memory and return the dynamic shared memory size (0 when
+// the shape cannot be staged). The slot is the largest (a multiple of 64 bytes per row, at most 4096 so that a stage
+// stays <= 64 KB) for which the exact layout fits p.ring stages, or, with p.ring 0 (auto), 3 stages (2 if no slot
+// fits 3); the ring then holds as many stages as fit (2..16). Layer mode (p.nops > 0): one slot for every op (next
+// to x of the largest K), each op staged in its own geometry within it; p.K and p.nchunk become the largest K and row.
 template <int F, int NC, int DEC>
 size_t tma_prep(Params& p, size_t cap) {
     GemvOp* ops = p.host_ops ? p.host_ops : p.ops;
@@ -224,66 +255,29 @@ size_t tma_prep(Params& p, size_t cap) {
         p.K = K;
         p.nchunk = nchunk;
     }
-    const size_t rowbytes = (size_t)p.nchunk * 16;
+    const long need = ((long)p.nchunk * 16 + 63) / 64 * 64;
     const int want = p.ring;
     if (want == 1 || want > kTmaMaxRing) return 0;
-    // everything but the ring and its metadata (partial buffers sized for a 4-stage ring; checked again below)
-    const size_t fixed = tma_smem_bytes<F, NC, DEC>(p.K, 0, 1, 0, 0) + (size_t)3 * (NC * 64 + 4);
-    if (fixed >= cap) return 0;
-    // a stage needs at most 16 KCS + 192 ring bytes and 112 + 2 x 2 x 16 (KCS/64 + 3) + 15 metadata bytes
-    const size_t per_stage_cap = (cap - fixed) / (want >= 2 ? want : 3);
-    if (per_stage_cap < 1536 + 17 * 64) return 0;
-    long kc_max = (long)(per_stage_cap - 1536) / 17;
-    if (kc_max > 65536 / 16) kc_max = 65536 / 16;
-    kc_max = kc_max / 64 * 64;
-    if (kc_max < 64) return 0;
-    const long need = (long)((rowbytes + 63) / 64 * 64);
-    const long kc0 = need < kc_max ? need : kc_max;
-    long kcs = kc0;
-    if (p.nops == 0) {                                         // fewest equal chunks
-        const long n = (long)((rowbytes + kc0 - 1) / kc0);
-        kcs = (long)(((rowbytes + n - 1) / n + 63) / 64 * 64);
-    }
-    p.cs_slot = (int)(kcs / 64);
-    int rs_max = 0;
-    if (p.nops == 0) {
-        tma_op_geometry(p.nchunk, (int)kcs, &p.nch, &p.kc, &p.rs);
-        rs_max = p.rs;
-    } else {
-        int mn = 1 << 30;
-        for (int j = 0; j < p.nops; ++j) {
-            GemvOp& o = ops[j];
-            tma_op_geometry(o.nchunk, (int)kcs, &o.nch, &o.kc, &o.rs);
-            mn = o.nch < mn ? o.nch : mn;
-            rs_max = o.rs > rs_max ? o.rs : rs_max;
+    const long top = need < 4096 ? need : 4096;
+    bool found = false;
+    for (int rmin = want >= 2 ? want : 3; !found && rmin >= 2; --rmin) {
+        for (long kcs = top; kcs >= 64; kcs -= 64) {
+            tma_apply_slot<F>(p, ops, kcs);
+            if (tma_smem_bytes<F, NC, DEC>(p.K, rmin, p.nch, p.mr, p.st_bytes) <= cap) {
+                found = true;
+                break;
+            }
         }
-        p.nch = mn;
-        p.kc = (int)kcs;
-        p.rs = rs_max;
+        if (want >= 2) break;                                 // an explicit ring depth is not lowered
     }
-    bool chunked = p.nops == 0 ? p.nch > 1 : false;
-    for (int j = 0; j < p.nops; ++j) chunked = chunked || ops[j].nch > 1;
-    p.mr = tma_meta_row(p.cs_slot, chunked);
-    p.st_bytes = 0;
-    if (p.nops == 0) {
-        p.st_bytes = tma_stage_bytes(p.rs, tma_blocked(p.nch, p.kc, p.rs));
-    } else {
-        for (int j = 0; j < p.nops; ++j) {
-            const int sb = tma_stage_bytes(ops[j].rs, tma_blocked(ops[j].nch, ops[j].kc, ops[j].rs));
-            p.st_bytes = sb > p.st_bytes ? sb : p.st_bytes;
-        }
-    }
+    if (!found) return 0;
     int ring = want;
     if (ring == 0) {
-        const size_t per_stage = (size_t)p.st_bytes + (size_t)(tma_meta_bytes<F>(p.mr) + 15) / 16 * 16;
-        const size_t fit = (cap - fixed) / per_stage;
-        ring = fit > (size_t)kTmaMaxRing ? kTmaMaxRing : (int)fit;
-        if (ring < 2) return 0;
+        ring = 2;
+        while (ring < kTmaMaxRing && tma_smem_bytes<F, NC, DEC>(p.K, ring + 1, p.nch, p.mr, p.st_bytes) <= cap) ++ring;
     }
-    size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, p.nch, p.mr, p.st_bytes);
-    while (want == 0 && total > cap && ring > 2)               // deeper rings need more partial buffers
-        total = tma_smem_bytes<F, NC, DEC>(p.K, --ring, p.nch, p.mr, p.st_bytes);
     p.ring = ring;
+    const size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, p.nch, p.mr, p.st_bytes);
     return total <= cap ? total : 0;
 }
 
@@ -475,7 +469,7 @@ __device__ __forceinline__ void wait_count(const unsigned int* c, unsigned int t
             atomicCAS(&g_tma_error, 0, code);
             return;
         }
-        __nanosleep(64);
+        __nanosleep(32);
     }
 }
 
@@ -712,10 +706,11 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         if (jo == 0) {
             grid_dependency_wait();
         } else {
-            // every consumer warp is done with the previous op's x; then every CTA must have stored op jo - 1
+            // every consumer warp is done with the previous op's x; then every CTA must have stored op jo - 1 (one
+            // thread per CTA polls the counter; the barrier passes its acquire on to the others)
             consumer_barrier(1, NC * 32);
-            if (lane == 0) wait_count(&p.layer_done[jo - 1], gridDim.x, 7);
-            __syncwarp();
+            if (tid == 0) wait_count(&p.layer_done[jo - 1], gridDim.x, 7);
+            consumer_barrier(1, NC * 32);
         }
         const int NCH = op.nch, RS = op.rs, CS = op.kc >> 6;
         const bool blk = tma_blocked(NCH, op.kc, RS);

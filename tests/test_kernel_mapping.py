@@ -334,6 +334,19 @@ def tma_op_geometry(nchunk, kcs):
     return n, c, c64 + 64 if c64 % 128 == 0 else c64
 
 
+def tma_apply_slot(fmt, K, rowbytes, kcs, ops):
+    """Mirror of tma_apply_slot: (kc, nch, rs, st_bytes, mr, geos) for a slot of kcs bytes per row."""
+    if not ops:
+        n = (rowbytes + kcs - 1) // kcs
+        kb = ((rowbytes + n - 1) // n + 63) // 64 * 64
+        nch, kc, rs = tma_op_geometry(rowbytes // 16, kb)
+        return kc, nch, rs, tma_stage_bytes(rs, tma_blocked(nch, kc, rs)), tma_meta_row(kb // 64, nch > 1), None
+    geos = [tma_op_geometry(ROWBYTES[fmt](k) // 16, kcs) for _, k in ops]
+    st = max(tma_stage_bytes(g[2], tma_blocked(*g)) for g in geos)
+    mr = tma_meta_row(kcs // 64, any(g[0] > 1 for g in geos))
+    return kcs, min(g[0] for g in geos), max(g[2] for g in geos), st, mr, geos
+
+
 def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
     """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged.
     Layer mode (`ops`: a list of (N, K)): K is the largest K, one slot size (kc = the slot's bytes per row) for all
@@ -344,44 +357,27 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
     rowbytes = max(ROWBYTES[fmt](k) for _, k in ops) if ops else ROWBYTES[fmt](K)
     if ring == 1 or ring > 16:
         return None
-    fixed = tma_smem_bytes(fmt, NC, K, 0, 1, 0, 0, dec) + 3 * (NC * 64 + 4)
-    if fixed >= cap:
+    top = min((rowbytes + 63) // 64 * 64, 4096)
+    geo = None
+    for rmin in ([ring] if ring >= 2 else [3, 2]):
+        for kcs in range(top, 63, -64):
+            kc, nch, rs, st, mr, geos = tma_apply_slot(fmt, K, rowbytes, kcs, ops)
+            if tma_smem_bytes(fmt, NC, K, rmin, nch, mr, st, dec) <= cap:
+                geo = (kc, nch, rs, st, mr, geos)
+                break
+        if geo:
+            break
+    if geo is None:
         return None
-    per_stage_cap = (cap - fixed) // (ring if ring >= 2 else 3)
-    if per_stage_cap < 1536 + 17 * 64:
-        return None
-    kc_max = min((per_stage_cap - 1536) // 17, 65536 // 16) // 64 * 64
-    if kc_max < 64:
-        return None
-    kc0 = min((rowbytes + 63) // 64 * 64, kc_max)
-    if ops:
-        kcs = kc0
-        geos = [tma_op_geometry(ROWBYTES[fmt](k) // 16, kcs) for _, k in ops]
-        nch = min(g[0] for g in geos)
-        rs = max(g[2] for g in geos)
-        kc = kcs
-        st_bytes = max(tma_stage_bytes(g[2], tma_blocked(*g)) for g in geos)
-    else:
-        n = (rowbytes + kc0 - 1) // kc0
-        kcs = ((rowbytes + n - 1) // n + 63) // 64 * 64
-        nch, kc, rs = tma_op_geometry(rowbytes // 16, kcs)
-        st_bytes = tma_stage_bytes(rs, tma_blocked(nch, kc, rs))
-    chunked = any(g[0] > 1 for g in geos) if ops else nch > 1
-    mr = tma_meta_row(kcs // 64, chunked)
-    auto_ring = ring == 0
+    kc, nch, rs, st, mr, geos = geo
     if ring == 0:
-        ring = min(16, (cap - fixed) // (st_bytes + tma_meta_bytes(fmt, mr)))
-        if ring < 2:
-            return None
-    total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec)
-    while auto_ring and total > cap and ring > 2:
-        ring -= 1
-        total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec)
+        ring = 2
+        while ring < 16 and tma_smem_bytes(fmt, NC, K, ring + 1, nch, mr, st, dec) <= cap:
+            ring += 1
+    total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st, dec)
     if total > cap:
         return None
-    if ops:
-        return (kc, nch, rs, st_bytes, ring, total, geos)
-    return (kc, nch, rs, st_bytes, ring, total)
+    return (kc, nch, rs, st, ring, total) + ((geos,) if ops else ())
 
 
 def check_banks(rs, blocked):
