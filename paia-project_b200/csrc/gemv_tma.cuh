@@ -768,7 +768,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             const int gb = j * CS;                            // global step of stage-local step 0
             const int sfull = SF - gb < sb0 ? SF - gb : sb0;  // steps below sfull are whole
             int sl = sa0;
-#pragma unroll 2
+#pragma unroll 1                                      // a compact loop: instruction fetch stalls dominate INT4
             for (; sl + U <= sfull; sl += U)
                 tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
                                             op.nchunk, Kp + 16);
