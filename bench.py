@@ -713,6 +713,49 @@ def decode_token(lib, kind, model, g, tuned, peak, mode, reps=10):
     return out
 
 
+def run_copy_sweep(args):
+    """Copy size against copy count: the TMA kernel on the gate_up shape at explicit ring depths (paia_gemv_launch_ex
+    ring option). The stage slot is sized for the ring, so deeper rings mean smaller bulk copies at about the same
+    bytes in flight per SM; graph mode over L2-rotated copies."""
+    import ctypes
+    import torch
+    from paia_gemv import load_lib, timing
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    l2 = timing.l2_bytes()
+    P = ctypes.c_void_p
+    cur = torch._C._cuda_getCurrentRawStream
+    f = lib._lib.paia_gemv_launch_ex
+    kid = {"bf16": 0, "fp8": 1, "int4": 2, "int4_asym": 3}
+    math_of = {"bf16": 5, "fp8": 8, "int4": 7, "int4_asym": 7}
+    N, K = 28672, 4096
+    for kind in args.kinds.split(","):
+        first = Gemv(lib, kind, N, K, g, "gate_up", variant=0, random_codes=True)
+        n = timing.plan_rotation(first.weight_bytes(), l2)
+        gms = [first] + [Gemv(lib, kind, N, K, g, "gate_up", variant=0, random_codes=True) for _ in range(n - 1)]
+        xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in gms]
+        ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in gms]
+        for ring in (0, 3, 4, 6, 8, 12, 16):
+            def mk(gm, x, y, ring=ring):
+                a = (kid[kind], ring, 2, 8, math_of[kind], 1, 0, 0, P(gm.W.data_ptr()),
+                     P(gm.s.data_ptr() if gm.s is not None else 0), P(gm.z.data_ptr() if gm.z is not None else 0),
+                     P(x.data_ptr()), None, P(y.data_ptr()), N, K)
+                return lambda: f(*a, P(cur(torch.cuda.current_device())))
+            calls = [mk(gm, x, y) for gm, x, y in zip(gms, xs, ys)]
+            rc = calls[0]()
+            torch.cuda.synchronize()
+            if rc:
+                print(json.dumps({"kind": kind, "ring": ring, "rc": rc}), flush=True)
+                continue
+            us = timing.median(timing.time_graph(calls, samples=9))
+            print(json.dumps({"kind": kind, "N": N, "K": K, "ring": ring, "us": round(us, 2),
+                              "GBps": round(first.weight_bytes() / us / 1e3, 1)}), flush=True)
+        del gms, xs, ys, first
+        torch.cuda.empty_cache()
+    return 0
+
+
 def run_decode(args):
     """Decode µs/token of both models in each format, per-op launches vs one launch per layer vs one plan per token."""
     import torch
@@ -904,6 +947,8 @@ def main():
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
     ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
     ap.add_argument("--launches", type=int, default=4)
+    ap.add_argument("--copy-sweep", action="store_true",
+                    help="TMA kernel on gate_up at explicit ring depths (copy size vs copy count)")
     ap.add_argument("--decode", action="store_true",
                     help="decode us/token: per-op launches vs one launch per layer vs one plan per token")
     args = ap.parse_args()
@@ -922,6 +967,8 @@ def main():
         return run_families(args)
     if args.decode:
         return run_decode(args)
+    if args.copy_sweep:
+        return run_copy_sweep(args)
     if args.tp:
         return run_tp(args, rank, world, local_rank)
     return run_main(args, rank, world, local_rank)

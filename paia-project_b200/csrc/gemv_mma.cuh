@@ -326,9 +326,9 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
             reinterpret_cast<uint4*>(xs)[i] = o;
         }, xc, map);
     } else if constexpr (DEC == 2) {
-        // INT4 for the integer MMA: v = x * 2^s rounded to an integer below 2^20 in magnitude (exact for every element
+        // INT4 for the integer MMA: v = x * 2^s rounded to an integer of magnitude <= 2^20 (exact for every element
         // within 2^12 of max|x|, bf16 carrying 8 significant bits; smaller ones keep an error below 2^-21 max|x|),
-        // split into three balanced base-128 digits d0 + 128 d1 + 128^2 d2, each an int8 plane of Kpad bytes at
+        // split into three signed base-128 digits d0 + 128 d1 + 128^2 d2, each an int8 plane of Kpad bytes at
         // xs + d (Kpad + 16) with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
         // Per 128-group g: the digit sums S_d (int) at gsum[8g + d] and sum(v) (float) at gsum[8g + 4].
         // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
@@ -373,29 +373,30 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         int* gi = reinterpret_cast<int*>(gsum);
         x_blocks_all<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             // blocks past K / 8 arrive as zeros and stage as zero digits
-            float sd[3] = {0.f, 0.f, 0.f};
+            int sd[3] = {0, 0, 0};
             if (i < Kp / 8) {
-                uint32_t dw[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+                int dg[3][8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const float xf = (j & 1) ? bf_hi(vv[j >> 1]) : bf_lo(vv[j >> 1]);
-                    // digits in float arithmetic: every step is exact (integers below 2^24)
-                    const float q0 = rintf((xf * up) * up2);
-                    const float q1 = rintf(q0 * 0.0078125f);
-                    const float q2 = rintf(q1 * 0.0078125f);
-                    const float d0 = fmaf(q1, -128.f, q0), d1 = fmaf(q2, -128.f, q1);
-                    sd[0] += d0; sd[1] += d1; sd[2] += q2;
-                    const int slot = (j & 1) ? 4 + (j >> 1) : (j >> 1);   // evens first, then odds
-                    const int sft = 8 * (slot & 3);
-                    dw[0][slot >> 2] |= (uint32_t)(__float2int_rn(d0) & 0xFF) << sft;
-                    dw[1][slot >> 2] |= (uint32_t)(__float2int_rn(d1) & 0xFF) << sft;
-                    dw[2][slot >> 2] |= (uint32_t)(__float2int_rn(q2) & 0xFF) << sft;
+                    // v = x 2^sh exactly (an integer, |v| <= 2^20); t = v + 64 (1 + 128 + 128^2) >= 0 splits into
+                    // base-128 digits u0 + 128 u1 + 128^2 u2, and d = u - 64 gives v = d0 + 128 d1 + 128^2 d2 with
+                    // d0, d1 in [-64, 63] and d2 in [-64, 64]: integer work and one conversion per element
+                    const int t = __float2int_rn((xf * up) * up2) + 1056832;
+                    dg[0][j] = (t & 127) - 64;
+                    dg[1][j] = ((t >> 7) & 127) - 64;
+                    dg[2][j] = (t >> 14) - 64;
                 }
 #pragma unroll
-                for (int d = 0; d < 3; ++d)
+                for (int d = 0; d < 3; ++d) {
+                    sd[d] = ((dg[d][0] + dg[d][1]) + (dg[d][2] + dg[d][3])) + ((dg[d][4] + dg[d][5]) + (dg[d][6] + dg[d][7]));
+                    // evens first (x0, x2, x4, x6), then odds: the low nibbles of a byte pair hold the even k
+                    const uint32_t e = __byte_perm(__byte_perm(dg[d][0], dg[d][2], 0x0040), __byte_perm(dg[d][4], dg[d][6], 0x0040), 0x5410);
+                    const uint32_t o = __byte_perm(__byte_perm(dg[d][1], dg[d][3], 0x0040), __byte_perm(dg[d][5], dg[d][7], 0x0040), 0x5410);
                     *reinterpret_cast<uint2*>(planes + (size_t)d * (Kp + 16) + 8 * (size_t)i) =
-                        make_uint2(dw[d][0], dw[d][1]);   // planes Kpad + 16 apart: no bank conflicts between them
+                        make_uint2(e, o);   // planes Kpad + 16 apart: no bank conflicts between them
+                }
             }
 #pragma unroll
             for (int d = 0; d < 3; ++d)
@@ -404,8 +405,8 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
             if (i < Kp / 8 && (i & 15) == 0) {
                 const int gg = i >> 4;
 #pragma unroll
-                for (int d = 0; d < 3; ++d) gi[8 * gg + d] = (int)sd[d];
-                gsum[8 * gg + 4] = sd[0] + 128.f * sd[1] + 16384.f * sd[2];
+                for (int d = 0; d < 3; ++d) gi[8 * gg + d] = sd[d];
+                gsum[8 * gg + 4] = (float)sd[0] + 128.f * (float)sd[1] + 16384.f * (float)sd[2];
             }
         }, xc, map);
     } else if constexpr (DEC == 1) {
