@@ -756,6 +756,60 @@ def run_copy_sweep(args):
     return 0
 
 
+def run_batched(args):
+    """M > 1 activation rows (paia_gemv_batched) on the Llama-3.1-8B shapes: us per call and weight GB/s for M = 1, 2,
+    4, 8, 16, graph mode over L2-rotated weight copies, against M separate batch-1 calls of the default path."""
+    import ctypes
+    import torch
+    from paia_gemv import load_lib, synthetic, timing
+    from paia_gemv.loader import _KINDS
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    peak, _ = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    l2 = timing.l2_bytes()
+    P = ctypes.c_void_p
+    cur = torch._C._cuda_getCurrentRawStream
+    fb = lib._lib.paia_gemv_batched
+    for kind in args.kinds.split(","):
+        for name in ("qkv_fused", "o_proj", "gate_up_fused", "down_proj"):
+            N, K = synthetic.SHAPES["llama31_8b"][name]
+            vid, _ = variant_for(lib, kind, N, K, None)
+            first = Gemv(lib, kind, N, K, g, name, variant=vid, random_codes=True)
+            n = timing.plan_rotation(first.weight_bytes(), l2)
+            gms = [first] + [Gemv(lib, kind, N, K, g, name, variant=vid, random_codes=True) for _ in range(n - 1)]
+            wb = first.weight_bytes()
+            for M in (1, 2, 4, 8, 16):
+                X = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+                Y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+                def mk(gm):
+                    a = (_KINDS[kind], P(gm.W.data_ptr()), P(gm.s.data_ptr() if gm.s is not None else 0),
+                         P(gm.z.data_ptr() if gm.z is not None else 0), P(X.data_ptr()), None, P(Y.data_ptr()),
+                         M, N, K)
+                    return lambda: fb(*a, P(cur(torch.cuda.current_device())))
+                calls = [mk(gm) for gm in gms]
+                rc = calls[0]()
+                torch.cuda.synchronize()
+                if rc:
+                    print(json.dumps({"kind": kind, "layer": name, "M": M, "rc": rc}), flush=True)
+                    continue
+                us = timing.median(timing.time_graph(calls, samples=9))
+                singles = []
+                for gm in gms:
+                    for m in range(M):
+                        singles.append(gm.launcher(X[m], Y[m]))
+                us1 = timing.median(timing.time_graph(singles, samples=9)) * M   # M batch-1 calls
+                print(json.dumps({"kind": kind, "model": "llama31_8b", "layer": name, "N": N, "K": K, "M": M,
+                                  "us": round(us, 2), "GBps": round(wb / us / 1e3, 1),
+                                  "frac_of_peak": round(wb / us / 1e3 / peak, 4),
+                                  "us_M_single_calls": round(us1, 2), "speedup": round(us1 / us, 2)}), flush=True)
+                del X, Y, calls, singles
+            del gms, first
+            torch.cuda.empty_cache()
+    return 0
+
+
 def run_decode(args):
     """Decode µs/token of both models in each format, per-op launches vs one launch per layer vs one plan per token."""
     import torch
@@ -947,6 +1001,7 @@ def main():
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
     ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
     ap.add_argument("--launches", type=int, default=4)
+    ap.add_argument("--batched", action="store_true", help="M > 1 activation rows (paia_gemv_batched)")
     ap.add_argument("--copy-sweep", action="store_true",
                     help="TMA kernel on gate_up at explicit ring depths (copy size vs copy count)")
     ap.add_argument("--decode", action="store_true",
@@ -969,6 +1024,8 @@ def main():
         return run_decode(args)
     if args.copy_sweep:
         return run_copy_sweep(args)
+    if args.batched:
+        return run_batched(args)
     if args.tp:
         return run_tp(args, rank, world, local_rank)
     return run_main(args, rank, world, local_rank)

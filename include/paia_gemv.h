@@ -129,6 +129,16 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
                         const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
                         void* stream);
 
+/* Batched x (M >= 1 activation rows; the reference kernels are M = 1 only, src/README.md:118):
+ * Y[M, N] = X[M, K] . dequant(W)^T (+ bias on every row), x and y bf16 row-major (row m at x + m K, y + m N), same
+ * weight formats, pointer rules and codes as the per-format calls (kind 0 bf16, 1 fp8, 2 int4, 3 int4_asym; scales /
+ * zeros as there, NULL where unused). Up to 8 x rows ride in the columns of each tensor-core MMA, so a launch streams
+ * the weights once for all of its rows; rows are grouped 8 (fewer when x of the group does not fit in shared memory
+ * next to the weight ring) per launch. Decode per format: bf16 as is, fp8 e4m3 -> f16 with x scaled per row, int4 as
+ * bf16 128 + n. */
+int paia_gemv_batched(int kind, const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                      void* y, int M, int N, int K, void* stream);
+
 /* One launch for a sequence of up to 6 GEMVs of one format (a decode layer's projections): a persistent grid, one CTA
  * per SM, streams the weights of op 0, 1, ... back to back, so op j + 1's weights are already in flight while op j
  * finishes. Op j's x is read only after every CTA has stored op j - 1's outputs, so x of op j may be the y of any

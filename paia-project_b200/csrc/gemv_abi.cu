@@ -512,6 +512,63 @@ int paia_gemv_tp_wait(unsigned int* counters, unsigned int per_call, void* strea
     return e == cudaSuccess ? 0 : (int)e;
 }
 
+// ------------------------------------------------------------------ batched x (M > 1)
+
+int paia_gemv_batched(int kind, const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                      void* y, int M, int N, int K, void* stream) {
+    if (kind < 0 || kind > 3 || M < 1) return -2;
+    const int rc = check_args(kind, Wq, scales, zeros, x, bias, y, N, K);
+    if (rc) return rc;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const Variant* inst = find_instance(kind, 0, 2, 8, 9);
+    if (!inst) return -2;
+    int n = 0;
+    const Variant* tab = table_of(kind, &n);
+    int dflt = -1;                                             // the format's default tuple: rows no group can take
+    for (int v = 0; v < n; ++v)
+        if (is_default_tuple(kind, tab[v])) { dflt = v; break; }
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    auto* yb = static_cast<__nv_bfloat16*>(y);
+    // groups of up to 8 x rows per launch, as many as fit next to the ring; each launch streams the weights once
+    for (int m0 = 0; m0 < M;) {
+        int mg = M - m0 < 8 ? M - m0 : 8;
+        Planned pl;
+        int prc = -2;
+        for (; mg >= 1; --mg) {
+            Params p{};
+            p.W = static_cast<const uint8_t*>(Wq);
+            p.s = scales;
+            p.z = zeros;
+            p.x = xb + (size_t)m0 * K;
+            p.bias = static_cast<const __nv_bfloat16*>(bias);
+            p.y = yb + (size_t)m0 * N;
+            p.N = N;
+            p.K = K;
+            p.nchunk = row_bytes(kind, K) / 16;
+            p.groups = K / 128;
+            p.xm = mg;
+            p.ldx = K;
+            p.ldy = N;
+            const LaunchOpts o{0, 0};
+            prc = plan_variant(*inst, p, o, &pl);
+            if (prc != -2) break;
+        }
+        if (prc == 0) {
+            const int lrc = launch_planned(inst->fn, pl, st);
+            if (lrc) return lrc;
+            m0 += mg;
+            continue;
+        }
+        if (prc != -2 || dflt < 0) return prc;
+        // one x row that no batched launch can stage (very long K): the single-row path
+        const int r = run(kind, Wq, scales, zeros, xb + (size_t)m0 * K, bias, yb + (size_t)m0 * N, N, K, dflt, stream,
+                          nullptr);
+        if (r) return r;
+        m0 += 1;
+    }
+    return 0;
+}
+
 // ------------------------------------------------------------------ layer launch and plans
 
 

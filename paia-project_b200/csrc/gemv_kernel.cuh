@@ -74,6 +74,9 @@ struct Params {
     int ks_log2;                   // log2(KS): warps that share a row
     int groups;                    // K / 128 (INT4 formats)
     int kc, nch, rs, st_bytes;     // TMA kernels: bytes per row per stage, stages per tile, smem row stride, stage size
+    // Batched TMA kernels (x holds xm rows, 1..8, ldx elements apart; y rows ldy elements apart): each x row rides in
+    // its own MMA column, so the weights stream once for all rows.
+    int xm, ldx, ldy;
     int cs_slot;                   // TMA kernels: 64-byte steps a stage slot holds per row
     int mr;                        // TMA kernels: halves per row of a stage's metadata slot
     int ring;                      // TMA kernels: stages in the shared-memory ring

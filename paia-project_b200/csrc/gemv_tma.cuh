@@ -150,16 +150,22 @@ __host__ __device__ constexpr int tma_kx(int K) {
 // multiples); x: Kx x 2 (INT4 integer path: Kx x 3) + 64 (FP8 lo plane at Kx + 64, INT4 planes Kx + 16 apart);
 // INT4 group sums (tma_gsum_words per group); tile partials NB x NC x 16 floats; per consumer warp its x scale
 // (4 floats) and a staging scratch word (kTmaTailBytes).
-template <int F, int NC, int DEC>
-__host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int mr, int st_bytes) {
+// Batched kernels (BAT): x rows xm, each with its own x region, group sums and scale; partial buffers of 16 rows x 8
+// columns; tail = 8 rows' x scales (32 floats) + staging scratch (32 floats).
+constexpr int kTmaTailBytesBat = 256;
+template <int F, int DEC>
+__host__ __device__ constexpr int tma_xrow_bytes(int K) {   // one staged x row (16-byte multiple)
+    return tma_kx<F>(K) * (((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2) + 64;
+}
+template <int F, int NC, int DEC, bool BAT = false>
+__host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int mr, int st_bytes, int xm = 1) {
     const int kp = tma_kx<F>(K);
     const size_t mb = (size_t)(tma_meta_bytes<F>(mr) + 15) / 16 * 16;
     const int nb = tma_part_bufs(ring < 2 ? 2 : ring, nch);
-    // x: 2 bytes per element (3 for the INT4 integer path's digit planes)
-    constexpr size_t xb = ((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2;
-    return kTmaBarBytes + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)kp * xb + 64 +
-           ((F == kINT4 || F == kINT4A) ? (size_t)(kp / 128) * tma_gsum_words(DEC) * 4 : 0) + (size_t)nb * NC * 16 * 4 +
-           kTmaTailBytes;
+    const int rows = BAT ? xm : 1;
+    return kTmaBarBytes + (size_t)ring * st_bytes + (size_t)ring * mb + (size_t)rows * tma_xrow_bytes<F, DEC>(K) +
+           ((F == kINT4 || F == kINT4A) ? (size_t)rows * (kp / 128) * tma_gsum_words(DEC) * 4 : 0) +
+           (size_t)nb * NC * 16 * (BAT ? 8 : 1) * 4 + (BAT ? kTmaTailBytesBat : kTmaTailBytes);
 }
 
 // Stage layouts (bytes from the stage base). Chunked and long rows: row r at r x RS, RS = KC (+ 64 when KC is a
@@ -243,8 +249,9 @@ inline void tma_apply_slot(Params& p, GemvOp* ops, long kcs) {
 // stays <= 64 KB) for which the exact layout fits p.ring stages, or, with p.ring 0 (auto), 3 stages (2 if no slot
 // fits 3); the ring then holds as many stages as fit (2..16). Layer mode (p.nops > 0): one slot for every op (next
 // to x of the largest K), each op staged in its own geometry within it; p.K and p.nchunk become the largest K and row.
-template <int F, int NC, int DEC>
+template <int F, int NC, int DEC, bool BAT = false>
 size_t tma_prep(Params& p, size_t cap) {
+    if (BAT != (p.xm > 0) || (BAT && (p.xm > 8 || p.nops > 0 || p.tp_world > 0))) return 0;
     GemvOp* ops = p.host_ops ? p.host_ops : p.ops;
     if (p.nops > 0) {
         int K = 0, nchunk = 0;
@@ -259,11 +266,14 @@ size_t tma_prep(Params& p, size_t cap) {
     const int want = p.ring;
     if (want == 1 || want > kTmaMaxRing) return 0;
     const long top = need < 4096 ? need : 4096;
+    // batched x: no slot below 2 KB per row (smaller pieces make the launch copy-bound); the caller stages fewer x
+    // rows instead
+    const long kmin = BAT ? (top < 2048 ? top : 2048) : 64;
     bool found = false;
     for (int rmin = want >= 2 ? want : 3; !found && rmin >= 2; --rmin) {
-        for (long kcs = top; kcs >= 64; kcs -= 64) {
+        for (long kcs = top; kcs >= kmin; kcs -= 64) {
             tma_apply_slot<F>(p, ops, kcs);
-            if (tma_smem_bytes<F, NC, DEC>(p.K, rmin, p.nch, p.mr, p.st_bytes) <= cap) {
+            if (tma_smem_bytes<F, NC, DEC, BAT>(p.K, rmin, p.nch, p.mr, p.st_bytes, p.xm) <= cap) {
                 found = true;
                 break;
             }
@@ -274,10 +284,11 @@ size_t tma_prep(Params& p, size_t cap) {
     int ring = want;
     if (ring == 0) {
         ring = 2;
-        while (ring < kTmaMaxRing && tma_smem_bytes<F, NC, DEC>(p.K, ring + 1, p.nch, p.mr, p.st_bytes) <= cap) ++ring;
+        while (ring < kTmaMaxRing && tma_smem_bytes<F, NC, DEC, BAT>(p.K, ring + 1, p.nch, p.mr, p.st_bytes, p.xm) <= cap)
+            ++ring;
     }
     p.ring = ring;
-    const size_t total = tma_smem_bytes<F, NC, DEC>(p.K, ring, p.nch, p.mr, p.st_bytes);
+    const size_t total = tma_smem_bytes<F, NC, DEC, BAT>(p.K, ring, p.nch, p.mr, p.st_bytes, p.xm);
     return total <= cap ? total : 0;
 }
 
@@ -447,6 +458,51 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
     }
 }
 
+// Batched INT4 (bf16 128 + n decode, DEC 0): as tma_steps' INT4 DEC 0 branch, but every MMA column is its own x row,
+// so the per-group fold uses the column's own sum of x (gl0: column 2c, gl1: column 2c + 1) and keeps four sums per
+// lane: rows g, g + 8 x columns 2c, 2c + 1.
+template <int F, int NU, bool CHECK>
+__device__ __forceinline__ void tma_steps_i4_bat(float (&acc)[4], const uint8_t* r0p, const uint8_t* r1p,
+                                                 const uint16_t* xl, const float* gl0, const float* gl1,
+                                                 const uint16_t* sc0, const uint16_t* sc1, const uint16_t* zr0,
+                                                 const uint16_t* zr1, int sl, int gs, int c, int nchunk) {
+    constexpr int SK = MmaStep<F>::k;
+    uint4 w0[NU], w1[NU];
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+        w0[u] = *reinterpret_cast<const uint4*>(r0p + 64 * (sl + u));
+        w1[u] = *reinterpret_cast<const uint4*>(r1p + 64 * (sl + u));
+        if (CHECK && 4 * (gs + u) + c >= nchunk) w0[u] = w1[u] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    const uint16_t* xb = xl + (size_t)gs * SK + c * (SK / 4);
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+        float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 xq = *reinterpret_cast<const uint4*>(xb + u * SK + 8 * q);
+            const uint32_t a = (&w0[u].x)[q], b = (&w1[u].x)[q];
+            mma_bf16(d[q & 1], nib_pair_bf16(a, 0), nib_pair_bf16(b, 0), nib_pair_bf16(a, 1), nib_pair_bf16(b, 1),
+                     xq.x, xq.y);
+            mma_bf16(d[q & 1], nib_pair_bf16(a, 2), nib_pair_bf16(b, 2), nib_pair_bf16(a, 3), nib_pair_bf16(b, 3),
+                     xq.z, xq.w);
+        }
+        const float sx0 = gl0[2 * (gs + u)], sx1 = gl1[2 * (gs + u)];
+        const float r[4] = {d[0][0] + d[1][0] - 136.f * sx0, d[0][1] + d[1][1] - 136.f * sx1,
+                            d[0][2] + d[1][2] - 136.f * sx0, d[0][3] + d[1][3] - 136.f * sx1};
+        if constexpr (F == kINT4) {
+            const float s0 = __half2float(__ushort_as_half(sc0[sl + u])), s1 = __half2float(__ushort_as_half(sc1[sl + u]));
+            acc[0] = fmaf(s0, r[0], acc[0]); acc[1] = fmaf(s0, r[1], acc[1]);
+            acc[2] = fmaf(s1, r[2], acc[2]); acc[3] = fmaf(s1, r[3], acc[3]);
+        } else {
+            const float s0 = bf_lo(sc0[sl + u]), s1 = bf_lo(sc1[sl + u]);
+            const float z0 = bf_lo(zr0[sl + u]), z1 = bf_lo(zr1[sl + u]);
+            acc[0] = fmaf(s0, r[0], fmaf(z0, sx0, acc[0])); acc[1] = fmaf(s0, r[1], fmaf(z0, sx1, acc[1]));
+            acc[2] = fmaf(s1, r[2], fmaf(z1, sx0, acc[2])); acc[3] = fmaf(s1, r[3], fmaf(z1, sx1, acc[3]));
+        }
+    }
+}
+
 // Op j of the launch: the single GEMV of Params (nops == 0) or the layer list.
 __device__ __forceinline__ GemvOp tma_op(const Params& p, int j) {
     if (p.op_table) return p.op_table[j];
@@ -473,9 +529,14 @@ __device__ __forceinline__ void wait_count(const unsigned int* c, unsigned int t
     }
 }
 
-template <int F, int NC, int U, int DEC = 0>
+// BAT: batched x (p.xm rows, 1..8): x row m rides in MMA column m (lanes of group g read x row g), every D element
+// is a (weight row, x row) output, partial buffers hold 16 rows x 8 columns per warp, and y row m is written at
+// y + m ldy. Decodes with a per-column fold only: BF16, FP8 DEC 0 (cvt to f16, x scaled per row), INT4 DEC 0.
+template <int F, int NC, int U, int DEC = 0, bool BAT = false>
 __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid_constant__ Params p) {
     constexpr bool I4 = (F == kINT4 || F == kINT4A);
+    static_assert(!BAT || DEC == 0, "batched x uses the per-column decodes");
+    constexpr int PC = BAT ? 8 : 1;                           // partial-sum columns per row
     extern __shared__ __align__(128) uint8_t smem[];
     // geometry shared by every op of the launch (p.K: the largest K, p.nch: the smallest NCH, p.cs_slot: the slot)
     const int ST = p.ring;                                    // 2..16 stages (the host checks)
@@ -492,11 +553,14 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     uint8_t* ring = smem + kTmaBarBytes;
     uint8_t* meta = ring + (size_t)ST * p.st_bytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(meta + (size_t)ST * MB);
-    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)Kpm * ((I4 && DEC == 2) ? 3 : 2) + 64);
+    const int XM = BAT ? p.xm : 1;
+    const int XROW = tma_xrow_bytes<F, DEC>(p.K);             // bytes per staged x row
     constexpr int GW = tma_gsum_words(DEC);
-    float* part = gsum + (I4 ? GW * (Kpm / 128) : 0);
-    float* xscale = part + (size_t)NB * NC * 16;              // [2][4]: the x scale of even and odd ops
-    float* xscr = xscale + 8;                                 // 32 floats of x staging scratch
+    const int GR = I4 ? GW * (Kpm / 128) : 0;                 // group-sum floats per x row
+    float* gsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + (size_t)XM * XROW);
+    float* part = gsum + (size_t)XM * GR;
+    float* xscale = part + (size_t)NB * NC * 16 * PC;         // [2][4] (BAT: [8][4]): the x scale per op / x row
+    float* xscr = xscale + (BAT ? 32 : 8);                    // 32 floats of x staging scratch
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -634,7 +698,23 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     if (op.bias) rbias = __uint_as_float((uint32_t)ld_u16(op.bias + row) << 16);
                 }
                 mbar_wait(&tdone[b], bph, 3);
-                if (mine) {
+                if constexpr (BAT) {
+                    // 16 rows x XM x rows: lane pairs (row r, x row m); row scale first, then x row m's scale
+                    const float* buf = part + (size_t)b * NC * 16 * 8;
+                    for (int idx = lane; idx < 16 * XM; idx += 32) {
+                        const int r = idx & 15, m = idx >> 4, rowb = rb + 16 * t + r;
+                        if (rowb < re) {
+                            float out = 0.f;
+#pragma unroll
+                            for (int w = 0; w < NC; ++w) out += buf[(w * 16 + r) * 8 + m];
+                            if constexpr (F == kFP8)
+                                out = out * ld_f32(reinterpret_cast<const float*>(op.s) + rowb) *
+                                      __uint_as_float((uint32_t)(__float_as_int(xscale[4 * m]) + 127) << 23);
+                            if (op.bias) out += __uint_as_float((uint32_t)ld_u16(op.bias + rowb) << 16);
+                            op.y[(size_t)m * p.ldy + rowb] = __float2bfloat16_rn(out);
+                        }
+                    }
+                } else if (mine) {
                     const float* buf = part + (size_t)b * NC * 16;
                     float total = 0.f;
 #pragma unroll
@@ -699,6 +779,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     TmaAcc<U> A;
     A.zero();
     float acc0 = 0.f, acc1 = 0.f;
+    float acc4[4] = {0.f, 0.f, 0.f, 0.f};                     // batched INT4: rows g, g + 8 x columns 2c, 2c + 1
     int s = 0, b = 0, tg = 0;                                 // ring slot, partial buffer, tiles over all ops
     uint32_t ph = 0, bph = 0;
     for (int jo = 0; jo < nops; ++jo) {
@@ -722,8 +803,16 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
         const int nst = ((re - rb + 15) >> 4) * NCH;
         if (nst > 0) {                                        // CTA-uniform: a CTA without rows of the op skips x
-            stage_x<F, DEC, tma_gsum_words(DEC)>(XSrc{op.x, op.K, op.act, Kp}, xs, gsum, xscale + 4 * (jo & 1), xscr,
-                                                 tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+            if constexpr (BAT) {
+                for (int m = 0; m < XM; ++m)                  // every x row: its own region, group sums and scale
+                    stage_x<F, DEC, tma_gsum_words(DEC)>(
+                        XSrc{op.x + (size_t)m * p.ldx, op.K, 0, Kp},
+                        reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(xs) + (size_t)m * XROW), gsum + m * GR,
+                        xscale + 4 * m, xscr, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+            } else {
+                stage_x<F, DEC, tma_gsum_words(DEC)>(XSrc{op.x, op.K, op.act, Kp}, xs, gsum, xscale + 4 * (jo & 1),
+                                                     xscr, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+            }
             consumer_barrier(1, NC * 32);
         }
         if (jo == 0 && tid == 0) {
@@ -732,6 +821,15 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         }
         const uint16_t* sa = reinterpret_cast<const uint16_t*>(op.s);
         const uint16_t* za = reinterpret_cast<const uint16_t*>(op.z);
+        // batched: lanes of group g feed MMA column g with x row g (columns past the last row repeat it, unused)
+        const uint16_t* xl = xs;
+        const float *gl0 = gsum, *gl1 = gsum;
+        if constexpr (BAT) {
+            xl = reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(xs) +
+                                                   (size_t)(g < XM ? g : XM - 1) * XROW);
+            gl0 = gsum + (2 * c < XM ? 2 * c : XM - 1) * GR;
+            gl1 = gsum + (2 * c + 1 < XM ? 2 * c + 1 : XM - 1) * GR;
+        }
         int t = 0, j = 0;
         for (int i = 0; i < nst; ++i) {
             const int r0 = rb + 16 * t;
@@ -768,21 +866,42 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             const int gb = j * CS;                            // global step of stage-local step 0
             const int sfull = SF - gb < sb0 ? SF - gb : sb0;  // steps below sfull are whole
             int sl = sa0;
+            if constexpr (BAT && I4) {
+#pragma unroll 1
+                for (; sl + U <= sfull; sl += U)
+                    tma_steps_i4_bat<F, U, false>(acc4, r0p, r1p, xl, gl0, gl1, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                                  op.nchunk);
+                for (; sl < sb0; ++sl)
+                    tma_steps_i4_bat<F, 1, false>(acc4, r0p, r1p, xl, gl0, gl1, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                                  op.nchunk);
+            } else {
 #pragma unroll 1                                      // a compact loop: instruction fetch stalls dominate INT4
-            for (; sl + U <= sfull; sl += U)
-                tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                            op.nchunk, Kp + 16);
-            for (; sl < sfull; ++sl)
-                tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                            op.nchunk, Kp + 16);
-            for (; sl < sb0; ++sl)                            // the ragged last step of the row
-                tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xs, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                           op.nchunk, Kp + 16);
+                for (; sl + U <= sfull; sl += U)
+                    tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                                op.nchunk, Kp + 16);
+                for (; sl < sfull; ++sl)
+                    tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                                op.nchunk, Kp + 16);
+                for (; sl < sb0; ++sl)                        // the ragged last step of the row
+                    tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
+                                               op.nchunk, Kp + 16);
+            }
 
             if (last) {
-                // tile end: this warp's partial sums of rows g, g + 8 -> buffer b for the epilogue warp
-                float s0, s1;
-                if constexpr (I4) {
+                // tile end: this warp's partial sums of rows g, g + 8 -> buffer b for the epilogue warp (batched:
+                // rows g, g + 8 x columns 2c, 2c + 1)
+                float s0 = 0.f, s1 = 0.f;
+                float sb[4] = {0.f, 0.f, 0.f, 0.f};
+                if constexpr (BAT && I4) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) { sb[e] = acc4[e]; acc4[e] = 0.f; }
+                } else if constexpr (BAT) {
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) sb[e] += A.a[u][0][e] + A.a[u][1][e];
+                    A.zero();
+                } else if constexpr (I4) {
                     s0 = acc0; s1 = acc1;
                     if constexpr (DEC == 2) {                     // digits 0-1 (lane c = 0) + digit 2 (c = 1)
                         s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
@@ -790,7 +909,6 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     }
                     acc0 = acc1 = 0.f;
                 } else {
-                    s0 = 0.f; s1 = 0.f;
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
                         if constexpr (F == kFP8 && DEC == 3) {    // columns 0 (x hi) + 1 (x lo)
@@ -805,8 +923,14 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 }
                 if (tg >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile tg - NB
                 ++tg;
-                float* buf = part + (size_t)b * NC * 16;
-                if (c == 0) { buf[warp * 16 + m0] = s0; buf[warp * 16 + m1] = s1; }
+                float* buf = part + (size_t)b * NC * 16 * PC;
+                if constexpr (BAT) {
+                    float* r0b = buf + (warp * 16 + m0) * 8 + 2 * c;
+                    float* r1b = buf + (warp * 16 + m1) * 8 + 2 * c;
+                    r0b[0] = sb[0]; r0b[1] = sb[1]; r1b[0] = sb[2]; r1b[1] = sb[3];
+                } else if (c == 0) {
+                    buf[warp * 16 + m0] = s0; buf[warp * 16 + m1] = s1;
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tdone[b]);         // release: this warp's partials of the tile
                 if (++b == NB) { b = 0; bph ^= 1u; }

@@ -23,6 +23,10 @@ static const Variant kInt4F16[] = {PB2_TMA_NC(kINT4, 6, 1)};
 static const Variant kInt4aF16[] = {PB2_TMA_NC(kINT4A, 6, 1)};
 static const Variant kInt4I8[] = {PB2_TMA_NC(kINT4, 7, 2)};
 static const Variant kInt4aI8[] = {PB2_TMA_NC(kINT4A, 7, 2)};
+// batched x (math 9): x rows in the MMA columns, per-column decodes (BF16, FP8 cvt to f16, INT4 bf16 128 + n)
+#define PB2_TMA_BAT(F) {0, 2, 8, 0, 1, 9, &gemv_tma_kernel<F, 8, 2, 0, true>, nullptr, &tma_prep<F, 8, 0, true>},
+static const Variant kBat[4] = {PB2_TMA_BAT(kBF16) PB2_TMA_BAT(kFP8) PB2_TMA_BAT(kINT4) PB2_TMA_BAT(kINT4A)};
+#undef PB2_TMA_BAT
 #undef PB2_TMA_NC
 #undef PB2_TMA_U
 #undef PB2_TMA_H
@@ -31,6 +35,11 @@ static const Variant kInt4aI8[] = {PB2_TMA_NC(kINT4A, 7, 2)};
 #define PB2_N(t) (int)(sizeof(t) / sizeof(t[0]))
 const Variant* tma_instances(int fmt, int math, int* n) {
     *n = 0;
+    if (math == 9) {
+        if (fmt < 0 || fmt > 3) return nullptr;
+        *n = 1;
+        return &kBat[fmt];
+    }
     if (fmt == kFP8) {
         if (math == 5) { *n = PB2_N(kFp8); return kFp8; }
         if (math == 6) { *n = PB2_N(kFp8Alu); return kFp8Alu; }

@@ -95,6 +95,8 @@ class GemvLib:
         lib.paia_gemv_tp_wait.restype = I
         lib.paia_gemv_tp_wait.argtypes = [P, ctypes.c_uint, P]
         # --- B200 additions
+        lib.paia_gemv_batched.restype = I
+        lib.paia_gemv_batched.argtypes = [I, P, P, P, P, P, P, I, I, I, P]
         lib.paia_gemv_layer.restype = I
         lib.paia_gemv_layer.argtypes = [I, I, I, ctypes.POINTER(GemvOp), P, P]
         lib.paia_gemv_plan_create.restype = I
@@ -265,6 +267,11 @@ class GemvLib:
     def tp_wait(self, counters_ptr, per_call, stream=None):
         self._check(self._lib.paia_gemv_tp_wait(counters_ptr, per_call & 0xFFFFFFFF, self._st(stream)),
                     "paia_gemv_tp_wait")
+
+    def batched(self, kind, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, M, N, K, stream=None):
+        """Y[M, N] = X[M, K] . W^T (+ bias): M activation rows against one weight stream (x, y row-major bf16)."""
+        self._check(self._lib.paia_gemv_batched(_KINDS[kind], Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr,
+                                                 M, N, K, self._st(stream)), "paia_gemv_batched")
 
     def layer(self, kind, ops, counters_ptr, math=0, stream=None):
         """One launch for a sequence of GEMVs of one format. `ops`: a list of dicts (or GemvOp) with Wq, scales,

@@ -291,13 +291,17 @@ def tma_part_bufs(ring, nch):
     return (ring - 1 + nch - 1) // nch + 2
 
 
-def tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec=0):
+def tma_smem_bytes(fmt, NC, K, ring, nch, mr, st_bytes, dec=0, xm=0):
+    """Mirror of tma_smem_bytes; xm > 0: the batched kernel with xm x rows."""
     SK = MMA_STEP_K[fmt]
     kp = (K + SK - 1) // SK * SK
     nb = tma_part_bufs(max(ring, 2), nch)
     i4 = fmt.startswith("int4")
-    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, mr)) + kp * (3 if i4 and dec == 2 else 2) + 64
-            + (kp // 128 * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * 4 + 160)
+    rows = xm if xm else 1
+    xrow = kp * (3 if i4 and dec == 2 else 2) + 64
+    return (640 + ring * (st_bytes + tma_meta_bytes(fmt, mr)) + rows * xrow
+            + (rows * (kp // 128) * (8 if dec == 2 else 2) * 4 if i4 else 0) + nb * NC * 16 * (8 if xm else 1) * 4
+            + (256 if xm else 160))
 
 
 BLOCK_ROW = 3072                                               # kTmaBlockRow
@@ -347,7 +351,7 @@ def tma_apply_slot(fmt, K, rowbytes, kcs, ops):
     return kcs, min(g[0] for g in geos), max(g[2] for g in geos), st, mr, geos
 
 
-def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
+def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0):
     """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged.
     Layer mode (`ops`: a list of (N, K)): K is the largest K, one slot size (kc = the slot's bytes per row) for all
     ops, nch the smallest op NCH, rs the largest op row stride, and a seventh element, the list of per-op
@@ -358,11 +362,12 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
     if ring == 1 or ring > 16:
         return None
     top = min((rowbytes + 63) // 64 * 64, 4096)
+    kmin = min(top, 2048) if xm else 64
     geo = None
     for rmin in ([ring] if ring >= 2 else [3, 2]):
-        for kcs in range(top, 63, -64):
+        for kcs in range(top, kmin - 1, -64):
             kc, nch, rs, st, mr, geos = tma_apply_slot(fmt, K, rowbytes, kcs, ops)
-            if tma_smem_bytes(fmt, NC, K, rmin, nch, mr, st, dec) <= cap:
+            if tma_smem_bytes(fmt, NC, K, rmin, nch, mr, st, dec, xm) <= cap:
                 geo = (kc, nch, rs, st, mr, geos)
                 break
         if geo:
@@ -372,9 +377,9 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None):
     kc, nch, rs, st, mr, geos = geo
     if ring == 0:
         ring = 2
-        while ring < 16 and tma_smem_bytes(fmt, NC, K, ring + 1, nch, mr, st, dec) <= cap:
+        while ring < 16 and tma_smem_bytes(fmt, NC, K, ring + 1, nch, mr, st, dec, xm) <= cap:
             ring += 1
-    total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st, dec)
+    total = tma_smem_bytes(fmt, NC, K, ring, nch, mr, st, dec, xm)
     if total > cap:
         return None
     return (kc, nch, rs, st, ring, total) + ((geos,) if ops else ())
@@ -655,3 +660,30 @@ def test_tma_prep_geometry():
     # the largest K the C ABI accepts still stages (smaller pieces)
     for fmt in ("bf16", "fp8", "int4"):
         assert tma_prep(fmt, 8, 98304, 2) is not None
+
+
+def batched_groups(fmt, M, K):
+    """Mirror of paia_gemv_batched's grouping: launches of up to 8 x rows, each as many as fit (0: a single-row call)."""
+    out, m0 = [], 0
+    while m0 < M:
+        mg = min(8, M - m0)
+        while mg >= 1 and tma_prep(fmt, 8, K, 0, SMEM_CAP, 0, xm=mg) is None:
+            mg -= 1
+        out.append(mg)
+        m0 += max(mg, 1)
+    return out
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int4", "int4_asym"])
+def test_batched_geometry(fmt):
+    """Batched x: every real shape stages at least one x row next to a 2+ stage ring, short rows take 8 x rows per
+    launch, and the replay of the weight stream (unchanged by the x rows) holds."""
+    for K in (3584, 4096, 14336, 18944):
+        geo = tma_prep(fmt, 8, K, 0, SMEM_CAP, 0, xm=1)
+        assert geo is not None and geo[4] >= 2, (fmt, K)
+    for K in (3584, 4096):
+        assert batched_groups(fmt, 16, K) == [8, 8], (fmt, K, batched_groups(fmt, 16, K))
+    g = batched_groups(fmt, 16, 14336)
+    assert sum(max(v, 1) for v in g) == 16 and min(g) >= 1, g
+    kc, nch, rs, st, ring, smem = tma_prep(fmt, 8, 4096, 0, SMEM_CAP, 0, xm=8)
+    replay_tma_op(fmt, 300, 4096, 8, 2, kc, nch, rs, st, ring, smem, SMEM_CAP, 7, (kc + 63) // 64)
