@@ -529,12 +529,13 @@ int paia_gemv_batched(int kind, const void* Wq, const void* scales, const void* 
         if (is_default_tuple(kind, tab[v])) { dflt = v; break; }
     const auto* xb = static_cast<const __nv_bfloat16*>(x);
     auto* yb = static_cast<__nv_bfloat16*>(y);
-    // groups of up to 8 x rows per launch, as many as fit next to the ring; each launch streams the weights once
+    // groups of up to 8 x rows per launch, as many as fit next to the ring; each launch streams the weights once. A
+    // group of one row takes the single-row path (its decodes are faster than the batched ones).
     for (int m0 = 0; m0 < M;) {
         int mg = M - m0 < 8 ? M - m0 : 8;
         Planned pl;
         int prc = -2;
-        for (; mg >= 1; --mg) {
+        for (; mg >= 2; --mg) {
             Params p{};
             p.W = static_cast<const uint8_t*>(Wq);
             p.s = scales;
@@ -560,7 +561,7 @@ int paia_gemv_batched(int kind, const void* Wq, const void* scales, const void* 
             continue;
         }
         if (prc != -2 || dflt < 0) return prc;
-        // one x row that no batched launch can stage (very long K): the single-row path
+        // one row (or rows that no batched launch can stage): the single-row path
         const int r = run(kind, Wq, scales, zeros, xb + (size_t)m0 * K, bias, yb + (size_t)m0 * N, N, K, dflt, stream,
                           nullptr);
         if (r) return r;

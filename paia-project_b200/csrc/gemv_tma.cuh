@@ -270,7 +270,9 @@ size_t tma_prep(Params& p, size_t cap) {
     // rows instead
     const long kmin = BAT ? (top < 2048 ? top : 2048) : 64;
     bool found = false;
-    for (int rmin = want >= 2 ? want : 3; !found && rmin >= 2; --rmin) {
+    // batched x: at least 3 stages (with 2 a launch is latency-bound, measured 2-4x slower than separate calls);
+    // the caller stages fewer x rows instead
+    for (int rmin = want >= 2 ? want : 3; !found && rmin >= (BAT && want == 0 ? 3 : 2); --rmin) {
         for (long kcs = top; kcs >= kmin; kcs -= 64) {
             tma_apply_slot<F>(p, ops, kcs);
             if (tma_smem_bytes<F, NC, DEC, BAT>(p.K, rmin, p.nch, p.mr, p.st_bytes, p.xm) <= cap) {

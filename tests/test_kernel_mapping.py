@@ -364,7 +364,7 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0):
     top = min((rowbytes + 63) // 64 * 64, 4096)
     kmin = min(top, 2048) if xm else 64
     geo = None
-    for rmin in ([ring] if ring >= 2 else [3, 2]):
+    for rmin in ([ring] if ring >= 2 else ([3] if xm else [3, 2])):
         for kcs in range(top, kmin - 1, -64):
             kc, nch, rs, st, mr, geos = tma_apply_slot(fmt, K, rowbytes, kcs, ops)
             if tma_smem_bytes(fmt, NC, K, rmin, nch, mr, st, dec, xm) <= cap:
@@ -663,13 +663,14 @@ def test_tma_prep_geometry():
 
 
 def batched_groups(fmt, M, K):
-    """Mirror of paia_gemv_batched's grouping: launches of up to 8 x rows, each as many as fit (0: a single-row call)."""
+    """Mirror of paia_gemv_batched's grouping: launches of 2 to 8 x rows, each as many as fit with >= 3 stages of >= 2 KB
+    pieces; 1 = a single-row call."""
     out, m0 = [], 0
     while m0 < M:
         mg = min(8, M - m0)
-        while mg >= 1 and tma_prep(fmt, 8, K, 0, SMEM_CAP, 0, xm=mg) is None:
+        while mg >= 2 and tma_prep(fmt, 8, K, 0, SMEM_CAP, 0, xm=mg) is None:
             mg -= 1
-        out.append(mg)
+        out.append(max(mg, 1))
         m0 += max(mg, 1)
     return out
 
@@ -679,11 +680,12 @@ def test_batched_geometry(fmt):
     """Batched x: every real shape stages at least one x row next to a 2+ stage ring, short rows take 8 x rows per
     launch, and the replay of the weight stream (unchanged by the x rows) holds."""
     for K in (3584, 4096, 14336, 18944):
-        geo = tma_prep(fmt, 8, K, 0, SMEM_CAP, 0, xm=1)
-        assert geo is not None and geo[4] >= 2, (fmt, K)
+        geo = tma_prep(fmt, 8, K, 0, SMEM_CAP, 0, xm=2)
+        assert geo is not None and geo[4] >= 3, (fmt, K)
     for K in (3584, 4096):
         assert batched_groups(fmt, 16, K) == [8, 8], (fmt, K, batched_groups(fmt, 16, K))
-    g = batched_groups(fmt, 16, 14336)
-    assert sum(max(v, 1) for v in g) == 16 and min(g) >= 1, g
+    for K in (14336, 18944):
+        g = batched_groups(fmt, 16, K)
+        assert sum(g) == 16 and max(g) >= 2, g
     kc, nch, rs, st, ring, smem = tma_prep(fmt, 8, 4096, 0, SMEM_CAP, 0, xm=8)
     replay_tma_op(fmt, 300, 4096, 8, 2, kc, nch, rs, st, ring, smem, SMEM_CAP, 7, (kc + 63) // 64)
