@@ -12,7 +12,8 @@ The steps rotate over L distinct layers (L * 208 MiB > 4 x L2), so weights alway
 value   = algorithmic bytes (e4m3 weights + fp32 row scales) of all steps / device time of the K steps, GB/s,
           max over ranks; at N > 1 every rank runs its own layers (weak scaling, no data-path collective).
 e2e     = the same metric through the public Python API (ctypes -> C ABI, eager launches), with each step's x copied
-          host->device from pinned memory and the layer output copied device->host inside the timed region.
+          host->device from pinned memory and the layer output copied device->host inside the timed region; the
+          copies overlap the neighbouring steps' compute on two copy streams (serial_value: all on one stream).
 roofline: the dominant (and only) kernel of the step is the FP8 GEMV kernel; achieved = algorithmic bytes / time.
 cpu_baseline: the reference's CPU path (dequantise + chunked fp32 matmul, oracle/cpu_reference.py) on the host cores.
 --impl reference: that CPU path alone, as the reference arm (rank 0 only).
@@ -200,26 +201,27 @@ class Gemv:
         fn = L.paia_gemv_int4_asym_bias
         return lambda: fn(W, s, z, xp, b, yp, N, K, v, P(cur(dev)))
 
-    def api_call(self, x, y):
-        """The public op API a user calls (paia_gemv.loader.GemvLib methods)."""
-        W, xp, yp = self.W.data_ptr(), x.data_ptr(), y.data_ptr()
+    def api_call(self, x, y, stream=None):
+        """The public op API a user calls (paia_gemv.loader.GemvLib methods); stream None = torch's current one."""
+        W, xp, yp, st = self.W.data_ptr(), x.data_ptr(), y.data_ptr(), stream
         if self.kind == "bf16":
             if self.bias is not None:
-                return self.lib.bf16_bias(W, xp, self.bias.data_ptr(), yp, self.N, self.K, self.variant)
-            return self.lib.bf16(W, xp, yp, self.N, self.K, self.variant)
+                return self.lib.bf16_bias(W, xp, self.bias.data_ptr(), yp, self.N, self.K, self.variant, st)
+            return self.lib.bf16(W, xp, yp, self.N, self.K, self.variant, st)
         if self.kind == "fp8":
             if self.bias is not None:
-                return self.lib.fp8_bias(W, self.s.data_ptr(), xp, self.bias.data_ptr(), yp, self.N, self.K, self.variant)
-            return self.lib.fp8(W, self.s.data_ptr(), xp, yp, self.N, self.K, self.variant)
+                return self.lib.fp8_bias(W, self.s.data_ptr(), xp, self.bias.data_ptr(), yp, self.N, self.K,
+                                         self.variant, st)
+            return self.lib.fp8(W, self.s.data_ptr(), xp, yp, self.N, self.K, self.variant, st)
         if self.kind == "int4":
             if self.bias is not None:
                 return self.lib.int4_bias(W, self.s.data_ptr(), xp, self.bias.data_ptr(), yp, self.N, self.K,
-                                          self.variant)
-            return self.lib.int4(W, self.s.data_ptr(), xp, yp, self.N, self.K, self.variant)
+                                          self.variant, st)
+            return self.lib.int4(W, self.s.data_ptr(), xp, yp, self.N, self.K, self.variant, st)
         if self.bias is not None:
             return self.lib.int4_asym_bias(W, self.s.data_ptr(), self.z.data_ptr(), xp, self.bias.data_ptr(), yp,
-                                           self.N, self.K, self.variant)
-        return self.lib.int4_asym(W, self.s.data_ptr(), self.z.data_ptr(), xp, yp, self.N, self.K, self.variant)
+                                           self.N, self.K, self.variant, st)
+        return self.lib.int4_asym(W, self.s.data_ptr(), self.z.data_ptr(), xp, yp, self.N, self.K, self.variant, st)
 
 
 def variant_for(lib, kind, N, K, tuned):
@@ -266,9 +268,9 @@ class Layer:
             if rc:
                 raise RuntimeError(f"launch failed with code {rc}")
 
-    def step_api(self):
+    def step_api(self, stream=None):
         for gm, x, y in zip(self.gemvs, self.xs, self.ys):
-            gm.api_call(x, y)
+            gm.api_call(x, y, stream)
 
     def weight_bytes(self):
         return sum(gm.weight_bytes() for gm in self.gemvs)
@@ -530,33 +532,78 @@ def run_main(args, rank, world, local_rank):
         del copies, xs, ys, calls
     torch.cuda.empty_cache()
 
-    # e2e through the public API with host buffers (eager launches, async copies, one sync at the end)
+    # e2e through the public API with host buffers: eager launches, every step's x copied host->device from pinned
+    # memory and its layer output device->host, one sync at the end. Headline: the copies on two copy streams, so a
+    # step's input lands while the previous step computes and its output drains while the next one does (events
+    # order each copy against the compute that reads or overwrites its buffer). Also reported: all on one stream.
     x_host = torch.empty(layers[0].x.numel(), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(layers[0].x.cpu())
     y_host = torch.empty(layers[0].ys[-1].numel(), dtype=torch.bfloat16).pin_memory()
-    for i in range(min(args.warmup, 2 * L)):
+    main = torch.cuda.current_stream()
+    main_h = main.cuda_stream
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    done = [torch.cuda.Event() for _ in range(L)]       # layer slot's step finished (its x read, its output written)
+    x_in = [torch.cuda.Event() for _ in range(L)]       # layer slot's x landed
+    y_out = [torch.cuda.Event() for _ in range(L)]      # layer slot's output copied out
+
+    def copy_on(stream, dst, src):
+        torch.cuda.set_stream(stream)                   # ~5 us of host time; the stream context manager takes ~16
+        dst.copy_(src, non_blocking=True)
+        torch.cuda.set_stream(main)
+
+    def h2d(i):
+        j = i % L
+        s_in.wait_event(done[j])                        # step i - L has read this slot's x
+        copy_on(s_in, layers[j].x, x_host)
+        x_in[j].record(s_in)
+
+    def piped_step(i):
+        j = i % L
+        lay = layers[j]
+        main.wait_event(x_in[j])
+        main.wait_event(y_out[j])                       # step i - L's output has been copied out
+        lay.step_api(main_h)
+        done[j].record(main)
+        s_out.wait_event(done[j])
+        copy_on(s_out, y_host, lay.ys[-1])
+        y_out[j].record(s_out)
+        h2d(i + 1)                                      # the next step's input, behind this step's compute
+
+    def serial_step(i):
         lay = layers[i % L]
         lay.x.copy_(x_host, non_blocking=True)
         lay.step_api()
         y_host.copy_(lay.ys[-1], non_blocking=True)
+
+    def e2e_time(step, first):
+        for i in range(args.warmup):
+            step(first + i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for i in range(args.steps):
+            step(first + args.warmup + i)
+        a1.record()
+        torch.cuda.synchronize()
+        t = a0.elapsed_time(a1)
+        if world > 1:
+            t = torch.tensor([t], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t = t.item()
+        return t
+
+    e2e_serial_ms = e2e_time(serial_step, 0)
+    h2d(0)
+    e2e_ms = e2e_time(piped_step, 0)
+    main.wait_stream(s_in)
+    main.wait_stream(s_out)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record()
-    for i in range(args.steps):
-        lay = layers[i % L]
-        lay.x.copy_(x_host, non_blocking=True)
-        lay.step_api()
-        y_host.copy_(lay.ys[-1], non_blocking=True)
-    a1.record()
-    torch.cuda.synchronize()
-    e2e_ms = a0.elapsed_time(a1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
+    if not bool(torch.isfinite(y_host.float()).all()):
+        raise RuntimeError("e2e: non-finite layer output copied to the host")
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+    e2e_serial_value = total_bytes / (e2e_serial_ms * 1e-3) / 1e9
 
     peak, peak_src = measured_peaks()
     # roofline of the dominant kernel (gate_up: over half of the layer's bytes), from its per-launch device time
@@ -593,8 +640,12 @@ def run_main(args, rank, world, local_rank):
             "us_per_layer": round(ms_max * 1e3 / args.steps, 3),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": layers[0].x.numel() * 2,
                     "d2h_bytes_per_step": layers[0].ys[-1].numel() * 2,
+                    "serial_value": round(e2e_serial_value, 2),
                     "how": "public API (paia_gemv.loader ctypes -> C ABI), eager launches; per step pinned H2D of x, "
-                           "4 GEMVs, D2H of the layer output; CUDA events around all K steps"},
+                           "4 GEMVs, D2H of the layer output; CUDA events around all K steps. value: the copies on "
+                           "two copy streams (step i+1's input lands while step i computes, step i's output drains "
+                           "while step i+1 computes; events order every copy against the compute that reads or "
+                           "overwrites its buffer). serial_value: copies and GEMVs in order on one stream"},
             "gpu_launches": launches,
             "clocks": clocks,
             "check_rel_l2_vs_torch": round(check_err, 6),
