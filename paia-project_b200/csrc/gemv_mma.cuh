@@ -330,7 +330,8 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         // within 2^12 of max|x|, bf16 carrying 8 significant bits; smaller ones keep an error below 2^-21 max|x|),
         // split into three signed base-128 digits d0 + 128 d1 + 128^2 d2, each an int8 plane of Kpad bytes at
         // xs + d (Kpad + 16) with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
-        // Per 128-group g: the digit sums S_d (int) at gsum[8g + d] and sum(v) (float) at gsum[8g + 4].
+        // Per 128-group g: the digit sums S_d (int) at gsum[8g + d], sum(v) (float) at gsum[8g + 4], and the
+        // symmetric offsets 8 (S_0 + 128 S_1) and 8 128^2 S_2 (floats, exact) at gsum[8g + 5] and gsum[8g + 6].
         // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
         float m = 0.f;
         bool bad = false;
@@ -407,6 +408,8 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
 #pragma unroll
                 for (int d = 0; d < 3; ++d) gi[8 * gg + d] = sd[d];
                 gsum[8 * gg + 4] = (float)sd[0] + 128.f * (float)sd[1] + 16384.f * (float)sd[2];
+                gsum[8 * gg + 5] = 8.f * ((float)sd[0] + 128.f * (float)sd[1]);
+                gsum[8 * gg + 6] = 131072.f * (float)sd[2];
             }
         }, xc, map);
     } else if constexpr (DEC == 1) {

@@ -371,33 +371,37 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
             }
         }
     } else if constexpr (DEC == 2) {
-        // INT4, integer MMA: nibbles -> u8 (one LOP3 for the low nibbles, a shift and a LOP3 for the high ones),
-        // against x as three int8 digit planes; lane group g reads plane g (g < 3), so MMA column d carries digit d
-        // and one m16n8k32 yields the three exact digit dot products of 32 weights of 16 rows. Per group:
-        // sum_d (D_d - 8 S_d) 128^d, lanes c = 0 / 1 holding digits 0-1 / 2 (column 3 and c = 2, 3 are unused).
+        // INT4, integer MMA against x as three int8 digit planes; lane group g reads plane g (g < 3), so MMA column d
+        // carries digit d. One LOP3 per word and nibble half: low nibbles go in as u8 n (chain L), high nibbles
+        // unshifted as u8 16 n (chain H), each mma.sync taking two words of one half against the matching even / odd
+        // x of those words. Per group: sum_d 128^d (L_d + H_d / 16 - 8 S_d) = sum_d (16 L_d + H_d) 128^d / 16 - C,
+        // with C = 8 sum_d 128^d S_d of the lane's digits staged per group (lanes c = 0 / 1 hold digits 0-1 / 2;
+        // c = 2, 3 carry unused columns and are never read). 16 L + H stays below 2^21, exact as a float.
         const int grp = (int)(threadIdx.x & 31) >> 2;
         // (lanes of group 3, an unused column, read plane 1 so that no quarter-warp meets a bank twice)
         const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp < 3 ? grp : 1) * xlo_off +
                             (size_t)gs * 128 + 32 * c;
-        const int* gi = reinterpret_cast<const int*>(gsum);
-        const float flo = c == 0 ? 1.f : (c == 1 ? 16384.f : 0.f);
-        const float fhi = c == 0 ? 128.f : 0.f;
+        const float flo = c == 0 ? 0.0625f : (c == 1 ? 1024.f : 0.f);
+        const float fhi = c == 0 ? 8.f : 0.f;
 #pragma unroll
         for (int u = 0; u < NU; ++u) {
             const uint4 xa = *reinterpret_cast<const uint4*>(xp + 128 * u);
             const uint4 xq = *reinterpret_cast<const uint4*>(xp + 128 * u + 16);
             const uint32_t bx[8] = {xa.x, xa.y, xa.z, xa.w, xq.x, xq.y, xq.z, xq.w};
-            int de[4] = {0, 0, 0, 0}, dq[4] = {0, 0, 0, 0};
+            int dl[4] = {0, 0, 0, 0}, dh[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t a = (&w0[u].x)[q], b = (&w1[u].x)[q];
-                mma_u8s8((q & 1) ? dq : de, a & 0x0F0F0F0Fu, b & 0x0F0F0F0Fu, (a >> 4) & 0x0F0F0F0Fu,
-                         (b >> 4) & 0x0F0F0F0Fu, bx[2 * q], bx[2 * q + 1]);
+            for (int h = 0; h < 2; ++h) {                     // words 2h, 2h + 1 of rows g (w0) and g + 8 (w1)
+                const uint32_t a0 = (&w0[u].x)[2 * h], b0 = (&w1[u].x)[2 * h];
+                const uint32_t a1 = (&w0[u].x)[2 * h + 1], b1 = (&w1[u].x)[2 * h + 1];
+                mma_u8s8(dl, a0 & 0x0F0F0F0Fu, b0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, b1 & 0x0F0F0F0Fu, bx[4 * h],
+                         bx[4 * h + 2]);
+                mma_u8s8(dh, a0 & 0xF0F0F0F0u, b0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, b1 & 0xF0F0F0F0u, bx[4 * h + 1],
+                         bx[4 * h + 3]);
             }
             const int gidx = 8 * (gs + u);
-            const int slo = gi[gidx + 2 * (c & 1)], shi = c == 0 ? gi[gidx + 1] : 0;
-            const float r0 = (float)(de[0] + dq[0] - 8 * slo) * flo + (float)(de[1] + dq[1] - 8 * shi) * fhi;
-            const float r1 = (float)(de[2] + dq[2] - 8 * slo) * flo + (float)(de[3] + dq[3] - 8 * shi) * fhi;
+            const float cg = gsum[gidx + 5 + (c & 1)];
+            const float r0 = fmaf((float)(16 * dl[0] + dh[0]), flo, fmaf((float)(16 * dl[1] + dh[1]), fhi, -cg));
+            const float r1 = fmaf((float)(16 * dl[2] + dh[2]), flo, fmaf((float)(16 * dl[3] + dh[3]), fhi, -cg));
             if constexpr (F == kINT4) {
                 acc0 = fmaf(__half2float(__ushort_as_half(sc0[sl + u])), r0, acc0);
                 acc1 = fmaf(__half2float(__ushort_as_half(sc1[sl + u])), r1, acc1);
