@@ -807,6 +807,42 @@ def run_copy_sweep(args):
     return 0
 
 
+def run_tile_sweep(args):
+    """Where a launch's time goes: the default kernel at K = 4096 and 14336 with 1, 2, 4 and 8 tiles (16 rows) per
+    CTA (N = 148 x 16 x tiles), cold (weights rotated through more than L2) and hot (one weight copy replayed, when it
+    fits in L2), next to the HBM time of its bytes at the measured copy peak. The slope over tiles is the streaming
+    cost per tile, the intercept the fixed cost of a launch; hot = cold means the consumers, not HBM, set the pace."""
+    import torch
+    from paia_gemv import load_lib, timing
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    peak, _ = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    l2 = timing.l2_bytes()
+    for kind in args.kinds.split(","):
+        for K in (4096, 14336):
+            row = {"kind": kind, "K": K, "cols": ["cold_us", "hot_us", "hbm_us"]}
+            for tiles in (1, 2, 4, 8):
+                N = 148 * 16 * tiles
+                vid, _ = variant_for(lib, kind, N, K, None)
+                first = Gemv(lib, kind, N, K, g, "tiles", variant=vid)
+                n = max(2, timing.plan_rotation(first.weight_bytes(), l2))
+                copies = [first] + [Gemv(lib, kind, N, K, g, "tiles", variant=vid, random_codes=True)
+                                    for _ in range(n - 1)]
+                xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in copies]
+                ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in copies]
+                calls = [c.launcher(x, y) for c, x, y in zip(copies, xs, ys)]
+                cold = timing.median(timing.time_graph(calls, samples=9))
+                hot = (timing.median(timing.time_graph([calls[0]] * n, samples=9))
+                       if first.weight_bytes() < 0.5 * l2 else None)
+                row[f"tiles_{tiles}"] = [round(cold, 2), None if hot is None else round(hot, 2),
+                                         round(first.weight_bytes() / peak / 1e3, 2)]
+                del copies, xs, ys, calls, first
+                torch.cuda.empty_cache()
+            print(json.dumps(row), flush=True)
+    return 0
+
+
 def run_batched(args):
     """M > 1 activation rows (paia_gemv_batched) on the Llama-3.1-8B shapes: us per call and weight GB/s for M = 1, 2,
     4, 8, 16, graph mode over L2-rotated weight copies, against M separate batch-1 calls of the default path."""
@@ -1055,6 +1091,8 @@ def main():
     ap.add_argument("--batched", action="store_true", help="M > 1 activation rows (paia_gemv_batched)")
     ap.add_argument("--copy-sweep", action="store_true",
                     help="TMA kernel on gate_up at explicit ring depths (copy size vs copy count)")
+    ap.add_argument("--tile-sweep", action="store_true",
+                    help="launch time against tiles per CTA, cold and hot (fixed cost vs streaming cost)")
     ap.add_argument("--decode", action="store_true",
                     help="decode us/token: per-op launches vs one launch per layer vs one plan per token")
     args = ap.parse_args()
@@ -1073,6 +1111,8 @@ def main():
         return run_families(args)
     if args.decode:
         return run_decode(args)
+    if args.tile_sweep:
+        return run_tile_sweep(args)
     if args.copy_sweep:
         return run_copy_sweep(args)
     if args.batched:
