@@ -374,6 +374,13 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0):
             break
     if geo is None:
         return None
+    if fmt == "fp8" and dec == 3 and not xm and ring == 0 and not ops and geo[1] > 1:
+        # chunked e4m3 rows: 4 stages of pieces >= 2.5 KB when they fit (kTmaMinPiece4)
+        for kcs in range(top, 2560 - 1, -64):
+            cand = tma_apply_slot(fmt, K, rowbytes, kcs, ops)
+            if tma_smem_bytes(fmt, NC, K, 4, cand[1], cand[4], cand[3], dec, xm) <= cap:
+                geo = cand
+                break
     kc, nch, rs, st, mr, geos = geo
     if ring == 0:
         ring = 2
@@ -420,7 +427,7 @@ def meta_copy_u16(mod, T, e0, n, slot, lanes=32):
         assert got.get(off + e - e0) == e, (mod, T, e0, n, e)
 
 
-def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
+def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1, dec=0):
     """Replay of gemv_tma_kernel: per CTA the producer streams T x NCH stages through a ring of ST stages (two block
     copies per whole-row stage, else one copy per valid row, KC bytes except the ragged last chunk) while the
     consumers split each stage's 64-byte steps into NC equal ranges of <= U-step iterations. Checks copies in bounds
@@ -428,7 +435,7 @@ def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1):
     and group, bias) in range, every output stored once, conflict-free fragment loads, and that the full/empty
     mbarrier protocol always makes progress."""
     cap = share_cap(share)
-    geo = tma_prep(fmt, NC, K, ring, cap)
+    geo = tma_prep(fmt, NC, K, ring, cap, dec)
     assert geo is not None, (fmt, K, NC, ring, share)
     KC, NCH, RS, ST_BYTES, ST, smem = geo
     G = grid(N, sms, per_sm)
@@ -620,6 +627,19 @@ def test_tma_mapping_exactly_once(fmt):
             assert K > 16384 or ring == 16, (fmt, K, ring, share)   # only long rows or deep rings may not fit
             continue
         replay_tma(fmt, N, K, NC, ring, U, sms=rnd.choice((148, 7, 1)), per_sm=rnd.choice((1, 2)), share=share)
+
+
+def test_fp8_chunked_rows_take_four_stages():
+    """The default FP8 decode (e4m3 tensor cores) stages chunked rows in a 4-stage ring of >= 2.5 KB pieces, whole
+    rows keep one piece per row; the long-K projections replay cleanly in that geometry."""
+    assert tma_prep("fp8", 8, 4096, 0, SMEM_CAP, 3)[:5] == tma_prep("fp8", 8, 4096, 0, SMEM_CAP, 0)[:5]
+    for N, K in ((4096, 14336), (3584, 18944), (4096, 11008), (37, 98304), (300, 8208)):
+        kc, nch, rs, st, ring, smem = tma_prep("fp8", 8, K, 0, SMEM_CAP, 3)
+        if K > 65536:                                  # x leaves no room for 4 such stages: the 3-stage geometry
+            assert (kc, nch, rs, st, ring, smem) == tma_prep("fp8", 8, K, 0, SMEM_CAP, 0), K
+        else:
+            assert nch > 1 and kc >= 2560 and ring >= 4 and smem <= SMEM_CAP, (K, kc, nch, ring)
+        replay_tma("fp8", N, K, 8, 0, 2, sms=148 if N > 1000 else 7, dec=3)
 
 
 LAYERS = {
