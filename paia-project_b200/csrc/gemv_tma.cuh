@@ -764,12 +764,12 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 if (++b == NB) { b = 0; bph ^= 1u; }
             }
             if (p.nops > 0) {
-                // this CTA's rows of op jo are in memory: release them, then count the CTA in
-                __threadfence();
+                // this CTA's rows of op jo are stored: the warp barrier orders every lane's stores before lane 0's
+                // release fence (cumulative), whose relaxed add then counts the CTA in without a round trip
                 __syncwarp();
                 if (lane == 0) {
-                    __threadfence();
-                    atomicAdd(&p.layer_done[jo], 1u);
+                    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" :: "l"(&p.layer_done[jo]) : "memory");
                 }
             }
         }
