@@ -692,7 +692,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 cp_async_arrive(&full[s]);
                 __syncwarp();                                 // plain-load halves stored before the closing arrival
                 if (lane == 0) mbar_arrive(&full[s]);
-                if (++s == ST) { s = 0; if (g >= ST) ph ^= 1u; }    // waits from round 1 on: parity 0, 1, 0, ...
+                if (++s == ST) { s = 0; if (g >= ST) ph ^= 1u; }    // waits from the second pass on: parity 0, 1, 0, ...
                 if (++j == NCH) { j = 0; ++t; }
             }
         }

@@ -1,6 +1,6 @@
 """Generate the golden vectors in tests/golden/golden_v1.npz from the REFERENCE'S OWN CODE.
 
-Run in a container where the read-only reference checkout exists (default /root/reference, or $PAIA_REFERENCE):
+Run where the read-only reference checkout exists (its location in $PAIA_REFERENCE, else the default in REF below):
 
     python tests/golden/make_golden.py
 
