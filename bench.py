@@ -3,21 +3,23 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}] [--sweep]
 
-Workload (the one the headline metric is quoted on): the Llama-3.1-8B FP8 W8A16 decode-layer GEMV
-sequence at batch 1 -- qkv 6144x4096 -> o 4096x4096 -> gate_up 28672x4096 -> down 4096x14336, each GEMV reading the
-previous one's output as x (o reads qkv[:4096], down reads gate_up[:14336]). One step = one decode layer (4 launches).
-Weights ~ N(0, 0.02) quantised to e4m3 with a per-row fp32 scale, x ~ N(0, 1) bf16, synthetic (no checkpoints).
-The steps rotate over L distinct layers (L * 208 MiB > 4 x L2), so weights always stream from HBM.
+Workload (BASELINE config 5 at every N; its shapes are configs 2 and 3's): one step = the Llama-3.1-8B lm_head
+128256x4096 and fused gate_up 28672x4096 in FP8 W8A16 (e4m3 + fp32 row scale) and in INT4 g128 (asymmetric: bf16
+scale + bf16 zero), batch 1 -- four GEMVs. On N GPUs (torchrun, one process per GPU) each rank holds N-th of every
+matrix's rows and one fused kernel per op stores its outputs into every rank's y over NVLink; on 1 GPU the four
+GEMVs run whole (the default path). Weights ~ N(0, 0.02), x ~ N(0, 1) bf16, synthetic; each rank rotates over
+copies of its shards so the weights stream from HBM (>= 4 x L2).
 
-value   = algorithmic bytes (e4m3 weights + fp32 row scales) of all steps / device time of the K steps, GB/s,
-          max over ranks; at N > 1 every rank runs its own layers (weak scaling, no data-path collective).
-e2e     = the same metric through the public Python API (ctypes -> C ABI, eager launches), with each step's x copied
-          host->device from pinned memory and the layer output copied device->host inside the timed region; the
-          copies overlap the neighbouring steps' compute on two copy streams (serial_value: all on one stream).
-roofline: the dominant (and only) kernel of the step is the FP8 GEMV kernel; achieved = algorithmic bytes / time.
-cpu_baseline: the reference's CPU path (dequantise + chunked fp32 matmul, oracle/cpu_reference.py) on the host cores.
+value   = full weight bytes (weights + scales / zeros of all four matrices) per step x steps / device time of the K
+          steps (CUDA events around a graph replay, max over ranks), GB/s. Strong scaling: the work is fixed.
+e2e     = the same metric through the public API (GemvLib methods; ShardedGemv.fused on > 1 GPU) with a pinned x
+          copied in and every full y copied out each step, in stream order.
+roofline: the dominant kernel (FP8 lm_head rows of the rank): algorithmic bytes / per-launch device time.
+cpu_baseline: the reference's CPU path (weights dequantised once, per-call chunked fp32 matmul) on the host cores.
 --impl reference: that CPU path alone, as the reference arm (rank 0 only).
---sweep: per-shape / per-format / per-model table as JSON lines, plus decode us/token.
+Extra keys (1 GPU): the FP8 decode layer (qkv, o, gate_up, down chained), every format's per-shape microseconds on
+every Llama / Qwen decode shape, decode microseconds per token.
+--sweep, --tp, --families, --decode, --batched, --copy-sweep, --tile-sweep, --one: the studies behind profiles/.
 """
 import argparse
 import datetime
@@ -34,7 +36,10 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "paia-project_b200"))
 
-METRIC = "GEMV achieved HBM GB/s, Llama-3.1-8B FP8 W8A16 decode-layer sweep (qkv, o, gate_up, down), batch 1"
+METRIC = ("GEMV achieved HBM GB/s (weights + scales / device time), Llama-3.1-8B lm_head 128256x4096 + gate_up "
+          "28672x4096 in FP8 W8A16 and INT4 g128, batch 1, rows sharded over the GPUs (BASELINE config 5)")
+WORKLOAD = ("llama31_8b lm_head 128256x4096 + gate_up_fused 28672x4096, fp8 w8a16 and int4 g128 (asym), batch 1, "
+            "row-sharded tensor parallel over n_gpus (1 GPU: whole matrices)")
 FALLBACK_HBM_GBS = 6650.0
 REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
@@ -334,110 +339,265 @@ def check_layer(layer):
     return max(errs)
 
 
+# ----------------------------------------------------------------------------------------------- headline workload
+
+# Llama-3.1-8B lm_head and fused gate_up in FP8 W8A16 and INT4 g128 (the asymmetric bf16
+# scale + zero format of config 3), batch 1; rows sharded over the ranks of the launch (one GPU: the whole matrices).
+HEADLINE = (("fp8", "lm_head"), ("fp8", "gate_up_fused"), ("int4_asym", "lm_head"), ("int4_asym", "gate_up_fused"))
+HEADLINE_MODEL = "llama31_8b"
+
+
+def format_bytes(kind, N, K):
+    """Algorithmic bytes of an N x K weight matrix in a format: weights + scales / zeros (the roofline numerator)."""
+    if kind == "bf16":
+        return 2 * N * K
+    if kind == "fp8":
+        return N * K + 4 * N
+    if kind == "int4":
+        return N * K // 2 + N * K // 64
+    return N * K // 2 + N * K // 32
+
+
+def headline_bytes():
+    return sum(format_bytes(k, *synthetic_shape(n)) for k, n in HEADLINE)
+
+
+def synthetic_shape(name, model=HEADLINE_MODEL):
+    from paia_gemv import synthetic
+    return synthetic.SHAPES[model][name]
+
+
+class HeadlineOp:
+    """One op of the headline step on this rank: its row shard in `n` L2-rotation copies (copy 0 holds quantised
+    weights of this rank's rows, the others valid random codes of the format), and on > 1 GPU the TP objects."""
+
+    def __init__(self, lib, kind, name, world, rank, n, g, bufs=None):
+        import torch
+        from paia_gemv import tp
+        self.kind, self.name = kind, name
+        self.N, self.K = synthetic_shape(name)
+        r0, r1 = tp.shard_rows(self.N, world, rank)
+        self.r0, self.nl = r0, r1 - r0
+        self.world = world
+        vid, _ = variant_for(lib, kind, self.nl, self.K, load_tuned())
+        self.copies = [Gemv(lib, kind, self.nl, self.K, g, name, variant=vid, random_codes=(c > 0)) for c in range(n)]
+        self.ys = [torch.empty(self.nl, dtype=torch.bfloat16, device="cuda") for _ in range(n)]
+        self.sg = None
+        if world > 1:
+            self.sg = [tp.ShardedGemv(lib, kind, c.W, c.s, c.z, None, self.N, self.K, buffers=bufs) for c in self.copies]
+
+    def shard_bytes(self):
+        return self.copies[0].weight_bytes()
+
+    def launcher(self, c, x):
+        """Zero-argument launch of copy c: the default-path GEMV (1 GPU) or the fused TP call."""
+        if self.sg is None:
+            return self.copies[c].launcher(x, self.ys[c])
+        sg = self.sg[c]
+
+        def call():
+            sg.fused(x)                    # raises on a nonzero return code
+            return 0
+        return call
+
+    def output(self, c):
+        return self.ys[c] if self.sg is None else self.sg[c].y
+
+    def api_call(self, c, x, stream=None):
+        """The public API call a user makes for copy c (GemvLib method, or ShardedGemv.fused)."""
+        if self.sg is None:
+            self.copies[c].api_call(x, self.ys[c], stream)
+            return self.ys[c]
+        return self.sg[c].fused(x, stream)
+
+
+def torch_reference(gm, x):
+    """fp32 dequantise-then-matmul on the device with torch (the sanity check; the CPU oracle is test-only)."""
+    from paia_gemv import quant
+    if gm.kind == "bf16":
+        deq = gm.W.float()
+    elif gm.kind == "fp8":
+        deq = quant.dequant_fp8(gm.W, gm.s)
+    elif gm.kind == "int4":
+        deq = quant.dequant_int4(gm.W, gm.s)
+    else:
+        deq = quant.dequant_int4_asym(gm.W, gm.s, gm.z)
+    ref = deq @ x.float()
+    if gm.bias is not None:
+        ref = ref + gm.bias.float()
+    return ref
+
+
+def check_headline(ops, x, world):
+    """Before timing, on every rank: each op's rows of this rank against torch fp32 (rel L2 <= 1e-3 after bf16
+    rounding), and on > 1 GPU the fused peer-store y equal bit for bit to the NCCL all-gather y (which proves the
+    exchange). Returns (worst rel L2, all fused == NCCL)."""
+    import torch
+    worst, same = 0.0, True
+    for op in ops:
+        gm = op.copies[0]
+        op.launcher(0, x)()
+        torch.cuda.synchronize()
+        y = op.output(0)
+        mine = y if world == 1 else y[op.r0:op.r0 + op.nl]
+        ref = torch_reference(gm, x).to(torch.bfloat16).float()
+        worst = max(worst, ((mine.float() - ref).norm() / ref.norm()).item())
+        if world > 1:
+            yf = y.clone()
+            yn = op.sg[0].nccl(x).clone()
+            torch.cuda.synchronize()
+            same = same and bool(torch.equal(yf.view(torch.int16), yn.view(torch.int16)))
+    return worst, same
+
+
+def time_ops_graph(calls_per_step, steps_per_replay, samples=10, warmup=3):
+    """Device microseconds per step of a CUDA graph holding `steps_per_replay` steps (each a list of launches),
+    CUDA events on the capturing stream; the same count of launches on every rank."""
+    import torch
+
+    def fn():
+        for i in range(steps_per_replay):
+            for c in calls_per_step[i % len(calls_per_step)]:
+                rc = c()
+                if rc:
+                    raise RuntimeError(f"launch failed with code {rc}")
+    gph = capture(fn)
+    for _ in range(warmup):
+        gph.replay()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(samples):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out.append(e0.elapsed_time(e1) * 1e3 / steps_per_replay)
+    del gph
+    return statistics.median(out)
+
+
+def max_over_ranks(vals, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 # ----------------------------------------------------------------------------------------------- CPU baseline
 
-def cpu_layer_operands(kind="fp8", model="llama31_8b", seed=0):
-    """Seeded CPU operands of one decode layer: (name, N, K, W, s, z, x) per GEMV."""
+def cpu_headline_operands(frac, seed=0):
+    """Seeded CPU operands of the headline step, the first `frac` of every op's rows (a bounded sample of the same
+    workload): (kind, rows, K, W, s, z, x) per op."""
     import torch
     from paia_gemv import quant, synthetic
     g = synthetic.generator(seed)
     ops = []
-    for name in synthetic.LAYER_SEQUENCE:
-        N, K = synthetic.SHAPES[model][name]
-        W = synthetic.weights_f32(N, K, g)
+    for kind, name in HEADLINE:
+        N, K = synthetic_shape(name)
+        rows = max(1, int(round(N * frac)))
+        W = synthetic.weights_f32(rows, K, g)
         x = synthetic.activation_bf16(K, g)
         if kind == "fp8":
             q, s = quant.quantize_fp8_rowwise(W)
-            ops.append((name, N, K, q, s, None, x))
-        elif kind == "bf16":
-            ops.append((name, N, K, W.to(torch.bfloat16), None, None, x))
-        elif kind == "int4":
-            p, s = quant.quantize_int4_g128(W)
-            ops.append((name, N, K, p, s, None, x))
+            ops.append((kind, rows, K, q, s, None, x))
         else:
-            p, s, z = quant.quantize_int4_asym(W)
-            ops.append((name, N, K, p, s, z, x))
+            p_, s, z = quant.quantize_int4_asym(W)
+            ops.append((kind, rows, K, p_, s, z, x))
         del W
     return ops
 
 
-def cpu_run_layer(ops, frac, kind="fp8"):
-    """The reference's CPU path over the first frac of every GEMV's rows; returns (bytes, dequant s, matmul s)."""
+def cpu_prepare(ops):
+    """The reference op's build step: dequantise every sampled op once (ours_quant.py:99, :138). Returns
+    ([(x, Wdeq)], algorithmic bytes of the sample, seconds spent dequantising)."""
     import cpu_reference as C
-    nbytes, td, tm = 0, 0.0, 0.0
-    for (name, N, K, W, s, z, x) in ops:
-        rows = max(1, int(round(N * frac)))
-        Wr = W[:rows]
-        sr = None if s is None else s[:rows]
-        zr = None if z is None else z[:rows]
-        _, a, b = C.gemv(kind, x, Wr, sr, zr)
-        td += a
-        tm += b
-        nbytes += Wr.numel() * Wr.element_size() + sum(t.numel() * t.element_size() for t in (sr, zr) if t is not None)
-    return nbytes, td, tm
+    prepared, nbytes = [], 0
+    t0 = time.perf_counter()
+    for (kind, rows, K, W, s, z, x) in ops:
+        prepared.append((x, C.dequant(kind, W, s, z)))
+        nbytes += format_bytes(kind, rows, K)
+    return prepared, nbytes, time.perf_counter() - t0
 
 
-def cpu_baseline(target_s=15.0, kind="fp8"):
+def cpu_step(prepared):
+    """The reference's per-call CPU work for every sampled op: the chunked fp32 matmul (ours_quant.py:69-71)."""
+    import cpu_reference as C
+    for x, deq in prepared:
+        C.matmul(x, deq)
+
+
+def cpu_calibrate(target_step_s):
+    """Row fraction whose per-step matmul takes about target_step_s on this host (measured on a 1/16 sample)."""
+    probe = 1.0 / 16
+    prepared, _, _ = cpu_prepare(cpu_headline_operands(probe))
+    cpu_step(prepared)
+    t0 = time.perf_counter()
+    cpu_step(prepared)
+    t = max(time.perf_counter() - t0, 1e-4)
+    return max(1e-3, min(1.0, probe * target_step_s / t))
+
+
+def cpu_baseline(target_s=15.0):
+    """The reference's CPU path for the headline workload on this host's cores: weights dequantised once (reported
+    apart), then the timed per-call chunked fp32 matmul over a bounded row sample, median of many reps."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import cpu_reference as C
     threads = C.set_threads()
-    ops = cpu_layer_operands(kind)
+    frac = cpu_calibrate(0.05)
+    prepared, nbytes, t_deq = cpu_prepare(cpu_headline_operands(frac))
+    cpu_step(prepared)
     t0 = time.perf_counter()
-    cpu_run_layer(ops, 1.0, kind)               # warm-up and calibration
-    t_layer = time.perf_counter() - t0
-    frac = 1.0 if t_layer * 3 <= target_s else max(0.02, target_s / 3 / t_layer)
-    reps = max(3, min(20, int(target_s / max(t_layer * frac, 1e-3))))
-    times, tds, tms, nb = [], [], [], 0
+    cpu_step(prepared)
+    t1 = max(time.perf_counter() - t0, 1e-4)
+    reps = max(10, min(2000, int(target_s / t1)))
+    times = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        nb, td, tm = cpu_run_layer(ops, frac, kind)
+        cpu_step(prepared)
         times.append(time.perf_counter() - t0)
-        tds.append(td)
-        tms.append(tm)
     med = statistics.median(times)
-    return {"value": nb / med / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": (f"{'all' if frac == 1.0 else f'{frac:.3f} of the'} rows of one Llama-3.1-8B {kind} decode layer "
-                       f"(qkv, o, gate_up, down; {nb / 2**20:.1f} MiB): dequantise + fp32 matmul in 8192-row chunks "
-                       f"(the reference harness's CPU reference path), median of {reps} reps after 1 warm-up; "
-                       f"dequant {statistics.median(tds) * 1e3:.1f} ms + matmul {statistics.median(tms) * 1e3:.1f} ms "
-                       f"per rep; CPU {C.cpu_model()}, torch threads {threads}, os.cpu_count {os.cpu_count()}"),
-            "ms_per_layer": med * 1e3 / frac}
+    return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": (f"{frac:.4f} of the rows of each headline op (Llama-3.1-8B lm_head and gate_up in FP8 and INT4 "
+                       f"asym; {nbytes / 2**20:.1f} MiB of format bytes): per call the chunked fp32 matmul over "
+                       f"weights dequantised once, as the reference op's check (paia-bench ours_quant.py:69-71 over "
+                       f"the dequantisation of :99, :138); median of {reps} reps after 1 warm-up; CPU {C.cpu_model()},"
+                       f" torch threads {threads}, os.cpu_count {os.cpu_count()}"),
+            "dequant_s_once": round(t_deq, 4)}
 
 
 # ----------------------------------------------------------------------------------------------- arms
 
 def run_reference_arm(args, rank, world):
-    """--impl reference: the reference's CPU implementation on this host's cores; rank 0 only."""
+    """--impl reference: the reference's CPU implementation of the headline workload on this host's cores (weights
+    dequantised once, then the per-call chunked fp32 matmul), rank 0 only; the other ranks exit without work."""
     if rank != 0:
         return 0
     sys.path.insert(0, str(ROOT / "oracle"))
     import cpu_reference as C
     threads = C.set_threads()
-    ops = cpu_layer_operands("fp8")
-    t0 = time.perf_counter()
-    cpu_run_layer(ops, 1.0)
-    t_layer = time.perf_counter() - t0
-    budget = 150.0
-    frac = min(1.0, budget / max(1, args.steps + args.warmup) / t_layer)
-    frac = max(frac, 1e-3)
+    budget = 120.0
+    frac = cpu_calibrate(budget / max(1, args.steps + args.warmup))
+    prepared, nbytes, t_deq = cpu_prepare(cpu_headline_operands(frac))
     for _ in range(args.warmup):
-        cpu_run_layer(ops, frac)
-    nbytes = 0
+        cpu_step(prepared)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        nb, _, _ = cpu_run_layer(ops, frac)
-        nbytes += nb
+        cpu_step(prepared)
     dt = time.perf_counter() - t0
-    value = nbytes / dt / 1e9
-    sample = (f"each step: {frac:.4f} of the rows of every GEMV of one Llama-3.1-8B FP8 decode layer "
-              f"({nbytes / args.steps / 2**20:.2f} MiB), dequantise + fp32 matmul in 8192-row chunks (the reference "
-              f"harness's CPU reference path, restated in oracle/cpu_reference.py); CPU {C.cpu_model()}, "
+    value = nbytes * args.steps / dt / 1e9
+    sample = (f"each step: {frac:.4f} of the rows of every headline op (Llama-3.1-8B lm_head and gate_up in FP8 and "
+              f"INT4 asym; {nbytes / 2**20:.2f} MiB of format bytes), the chunked fp32 matmul over weights "
+              f"dequantised once (dequantisation {t_deq * 1e3:.0f} ms, untimed, as the reference op does it at build "
+              f"time); the reference harness's CPU path restated in oracle/cpu_reference.py; CPU {C.cpu_model()}, "
               f"{threads} torch threads")
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,0.02) weights quantised to e4m3, N(0,1) bf16 x)",
-            "config": {"workload": "llama31_8b fp8 w8a16 decode-layer GEMV sweep, batch 1", "device": "cpu"},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to e4m3 / asymmetric int4 g128, N(0,1) bf16 x)",
+            "config": {"workload": WORKLOAD, "device": "cpu"},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -448,45 +608,54 @@ def run_reference_arm(args, rank, world):
 def run_main(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
-    from paia_gemv import load_lib, synthetic, timing
+    from paia_gemv import load_lib, synthetic, timing, tp
     torch.cuda.set_device(local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     lib = load_lib()
-    tuned = load_tuned()
-    kind, model = "fp8", "llama31_8b"
     g = torch.Generator(device="cuda").manual_seed(1000 * rank + 1)
     l2 = timing.l2_bytes()
-    probe = Layer(lib, kind, model, g, tuned)
-    lbytes = probe.weight_bytes()
-    L = max(4, math.ceil(4 * l2 / lbytes))
-    layers = [probe] + [Layer(lib, kind, model, g, tuned) for _ in range(L - 1)]
-    check_err = check_layer(layers[0])
-    if not check_err <= 1e-3:
-        raise RuntimeError(f"device sanity check failed: rel L2 {check_err:.3e} against torch fp32")
+    # per-rank bytes of one step (this rank's shards), and L2 rotation over n copies of every shard
+    step_shard = sum(format_bytes(k, synthetic_shape(n)[0] // world, synthetic_shape(n)[1]) for k, n in HEADLINE)
+    n = timing.plan_rotation(step_shard, l2)
+    bufs = {}
+    if world > 1:
+        for _, name in HEADLINE:
+            N = synthetic_shape(name)[0]
+            if N not in bufs:
+                bufs[N] = tp.TpBuffers(lib, N, torch.device("cuda", local_rank))
+    ops = [HeadlineOp(lib, kind, name, world, rank, n, g, bufs.get(synthetic_shape(name)[0])) for kind, name in HEADLINE]
+    gx = torch.Generator(device="cuda").manual_seed(7)                # x is the same on every rank
+    x = torch.randn(ops[0].K, device="cuda", generator=gx).to(torch.bfloat16)
+    check_err, same = check_headline(ops, x, world)
+    bad = max_over_ranks([0.0 if (check_err <= 1e-3 and same) else 1.0, check_err], world)
+    if bad[0]:
+        raise RuntimeError(f"headline check failed on some rank: worst rel L2 {bad[1]:.3e} against torch fp32, "
+                           f"fused == NCCL on this rank: {same}")
+    lib.device_error(1)
 
-    def run_steps(n):
-        for i in range(n):
-            layers[i % L].step()
+    steps_calls = [[op.launcher(c, x) for op in ops] for c in range(n)]
 
-    # graphs: one full rotation (L steps) and a tail, so exactly K (or W) steps run
-    g_round = capture(lambda: run_steps(L))
+    def run_steps(k):
+        for i in range(k):
+            for c in steps_calls[i % n]:
+                rc = c()
+                if rc:
+                    raise RuntimeError(f"launch failed with code {rc}")
+
+    # graphs: one full rotation (n steps) and the tails, so exactly K (or W) steps run, the same on every rank
+    g_round = capture(lambda: run_steps(n))
     tails = {}
+    for k in {args.steps % n, args.warmup % n} - {0}:
+        tails[k] = capture(lambda k=k: run_steps(k))
 
-    def replay(n):
-        for _ in range(n // L):
+    def replay(k):
+        for _ in range(k // n):
             g_round.replay()
-        r = n % L
-        if r:
-            if r not in tails:
-                tails[r] = capture(lambda: run_steps(r))
-            tails[r].replay()
+        if k % n:
+            tails[k % n].replay()
 
-    if args.steps % L:
-        tails[args.steps % L] = capture(lambda: run_steps(args.steps % L))
-    if args.warmup % L and args.warmup % L not in tails:
-        tails[args.warmup % L] = capture(lambda: run_steps(args.warmup % L))
     sampler = ClockSampler(local_rank)
     sampler.start()
     replay(args.warmup)
@@ -501,163 +670,211 @@ def run_main(args, rank, world, local_rank):
     e1.record()
     torch.cuda.synchronize()
     t_host1 = time.perf_counter()
-    if world > 1:
-        dist.barrier()
-    ms = e0.elapsed_time(e1)
     sampler.stop()
     clocks = sampler.summary(t_host0, t_host1)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = t.item()
-    total_bytes = lbytes * args.steps * world
+    ms = e0.elapsed_time(e1)
+    err = lib.device_error(1)
+    ms_max, err_max = max_over_ranks([ms, float(err)], world)
+    if err_max:
+        raise RuntimeError(f"device error {int(err_max)} during the timed steps")
+    del g_round, tails
+    total_bytes = headline_bytes() * args.steps
     value = total_bytes / (ms_max * 1e-3) / 1e9
-    launches = 4 * args.steps * world
+    launches = len(HEADLINE) * args.steps * world
 
-    # per-shape GEMV microseconds (graph mode, each shape alone, L2-rotated random-code copies)
-    per_shape = {}
-    for gi, name in enumerate(synthetic.LAYER_SEQUENCE):
-        N, K = synthetic.SHAPES[model][name]
-        ref = layers[0].gemvs[gi]
-        n = timing.plan_rotation(ref.weight_bytes(), l2)
-        copies = [ref] + [Gemv(lib, kind, N, K, g, name, variant=ref.variant, random_codes=True) for _ in range(n - 1)]
-        xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in copies]
-        ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in copies]
-        calls = [c.launcher(x, y) for c, x, y in zip(copies, xs, ys)]
-        us = timing.median(timing.time_graph(calls, samples=15))
-        wb = ref.weight_bytes()
-        per_shape[name] = {"N": N, "K": K, "us": round(us, 3), "GBps": round(wb / us / 1e3, 1),
-                           "variant": layers[0].gemvs[gi].variant}
-        del copies, xs, ys, calls
-    torch.cuda.empty_cache()
+    # per-op device time inside the same kind of graph (every rank the same launches), max over ranks
+    reps = max(n, (32 // n) * n)
+    per_op = {}
+    for op in ops:
+        us = time_ops_graph([[op.launcher(c, x)] for c in range(n)], reps)
+        per_op[f"{op.kind}:{op.name}"] = us
+    keys = list(per_op)
+    per_op = dict(zip(keys, max_over_ranks([per_op[k] for k in keys], world)))
 
-    # e2e through the public API with host buffers: eager launches, every step's x copied host->device from pinned
-    # memory and its layer output device->host, one sync at the end. Headline: the copies on two copy streams, so a
-    # step's input lands while the previous step computes and its output drains while the next one does (events
-    # order each copy against the compute that reads or overwrites its buffer). Also reported: all on one stream.
-    x_host = torch.empty(layers[0].x.numel(), dtype=torch.bfloat16).pin_memory()
-    x_host.copy_(layers[0].x.cpu())
-    y_host = torch.empty(layers[0].ys[-1].numel(), dtype=torch.bfloat16).pin_memory()
-    main = torch.cuda.current_stream()
-    main_h = main.cuda_stream
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-    done = [torch.cuda.Event() for _ in range(L)]       # layer slot's step finished (its x read, its output written)
-    x_in = [torch.cuda.Event() for _ in range(L)]       # layer slot's x landed
-    y_out = [torch.cuda.Event() for _ in range(L)]      # layer slot's output copied out
-
-    def copy_on(stream, dst, src):
-        torch.cuda.set_stream(stream)                   # ~5 us of host time; the stream context manager takes ~16
-        dst.copy_(src, non_blocking=True)
-        torch.cuda.set_stream(main)
-
-    def h2d(i):
-        j = i % L
-        s_in.wait_event(done[j])                        # step i - L has read this slot's x
-        copy_on(s_in, layers[j].x, x_host)
-        x_in[j].record(s_in)
-
-    def piped_step(i):
-        j = i % L
-        lay = layers[j]
-        main.wait_event(x_in[j])
-        main.wait_event(y_out[j])                       # step i - L's output has been copied out
-        lay.step_api(main_h)
-        done[j].record(main)
-        s_out.wait_event(done[j])
-        copy_on(s_out, y_host, lay.ys[-1])
-        y_out[j].record(s_out)
-        h2d(i + 1)                                      # the next step's input, behind this step's compute
-
-    def serial_step(i):
-        lay = layers[i % L]
-        lay.x.copy_(x_host, non_blocking=True)
-        lay.step_api()
-        y_host.copy_(lay.ys[-1], non_blocking=True)
-
-    def e2e_time(step, first):
-        for i in range(args.warmup):
-            step(first + i)
+    # NCCL all-gather baseline of the same step (> 1 GPU): the same kernel into the local slice, then
+    # all_gather_into_tensor, eager, max over ranks
+    nccl = None
+    if world > 1:
+        def nccl_step(i):
+            for op in ops:
+                op.sg[i % n].nccl(x)
+        for i in range(2 * n):
+            nccl_step(i)
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        dist.barrier()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
-        for i in range(args.steps):
-            step(first + args.warmup + i)
+        for i in range(reps):
+            nccl_step(i)
         a1.record()
         torch.cuda.synchronize()
-        t = a0.elapsed_time(a1)
-        if world > 1:
-            t = torch.tensor([t], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t = t.item()
-        return t
+        nccl_us = max_over_ranks([a0.elapsed_time(a1) * 1e3 / reps], world)[0]
+        nccl = {"us_per_step": round(nccl_us, 3), "GBps": round(headline_bytes() / nccl_us / 1e3, 1),
+                "how": "per op: the same TMA kernel into the local slice, then torch.distributed "
+                       "all_gather_into_tensor (NCCL) on the compute stream, eager launches, max over ranks"}
 
-    e2e_serial_ms = e2e_time(serial_step, 0)
-    h2d(0)
-    e2e_ms = e2e_time(piped_step, 0)
-    main.wait_stream(s_in)
-    main.wait_stream(s_out)
+    # e2e through the public API with host buffers: every step x copied in from pinned memory, the four ops called
+    # eagerly through the user-facing API (GemvLib methods; ShardedGemv.fused on > 1 GPU), every op's full y copied
+    # out to pinned memory, all in stream order on one stream; CUDA events, max over ranks
+    x_host = torch.empty(x.numel(), dtype=torch.bfloat16).pin_memory()
+    x_host.copy_(x.cpu())
+    y_host = [torch.empty(op.N, dtype=torch.bfloat16).pin_memory() for op in ops]
+    x_dev = [torch.empty_like(x) for _ in range(n)]
+
+    def e2e_step(i):
+        c = i % n
+        x_dev[c].copy_(x_host, non_blocking=True)
+        for op, yh in zip(ops, y_host):
+            y = op.api_call(c, x_dev[c])
+            yh.copy_(y, non_blocking=True)
+
+    for i in range(max(3, args.warmup // 10)):
+        e2e_step(i)
     torch.cuda.synchronize()
-    if not bool(torch.isfinite(y_host.float()).all()):
-        raise RuntimeError("e2e: non-finite layer output copied to the host")
-    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
-    e2e_serial_value = total_bytes / (e2e_serial_ms * 1e-3) / 1e9
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(n, min(args.steps, 200))
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    b1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks([b0.elapsed_time(b1)], world)[0]
+    if not all(bool(torch.isfinite(yh.float()).all()) for yh in y_host):
+        raise RuntimeError("e2e: non-finite output copied to the host")
+    e2e_value = headline_bytes() * e2e_steps / (e2e_ms * 1e-3) / 1e9
 
+    # roofline of the dominant kernel: FP8 lm_head (this rank's shard), bytes per launch / per-launch device time
     peak, peak_src = measured_peaks()
-    # roofline of the dominant kernel (gate_up: over half of the layer's bytes), from its per-launch device time
-    dom = per_shape["gate_up_fused"]
-    dom_bytes = layers[0].gemvs[synthetic.LAYER_SEQUENCE.index("gate_up_fused")].weight_bytes()
-    achieved = dom_bytes / (dom["us"] * 1e-6) / 1e9
+    dom = ops[0]
+    dom_us = per_op[f"{dom.kind}:{dom.name}"]
+    dom_bytes = dom.shard_bytes()
+    achieved = dom_bytes / (dom_us * 1e-6) / 1e9
     traffic = kernel_traffic()
+    tr = (traffic or {}).get("fp8_lm_head_dram_bytes_per_launch")
+    tr_ranks = (traffic or {}).get("fp8_lm_head_rows")
+
+    extras = {}
+    if world == 1 and not args.no_extras:
+        del steps_calls
+        for op in ops:
+            op.copies = op.ys = None
+        torch.cuda.empty_cache()
+        extras = run_extras(lib, g, l2, peak, args)
+
     result = None
     if rank == 0:
         cb = None
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_baseline()
-            cb = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items() if k != "ms_per_layer"}
+            cb = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items()}
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp8 e4m3 weights x bf16 x, fp32 accumulate)",
-            "data": "synthetic (seeded N(0,0.02) weights quantised to e4m3 + fp32 row scale, N(0,1) bf16 x)",
-            "config": {"workload": "llama31_8b fp8 w8a16 decode-layer GEMV sweep: qkv 6144x4096 -> o 4096x4096 -> "
-                                   "gate_up 28672x4096 -> down 4096x14336, batch 1, chained",
-                       "layers_rotated": L, "bytes_per_step": lbytes,
-                       "l2": f"inputs larger than L2: rotation over {L} layers = {L * lbytes / 2**20:.0f} MiB "
-                             f"> 4 x L2 ({l2 / 2**20:.0f} MiB)",
-                       "launch": "CUDA graph of back-to-back launches with programmatic dependent launch",
-                       "per_gpu_layers": "each rank streams its own layers" if world > 1 else None},
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 accumulate (fp8 e4m3 / int4 weights x bf16 x on the tensor cores)",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to e4m3 + fp32 row scale and to asymmetric int4 "
+                    "g128 with bf16 scale + zero, N(0,1) bf16 x)",
+            "config": {"workload": WORKLOAD, "rows_per_rank": {f"{op.kind}:{op.name}": op.nl for op in ops},
+                       "rotation_copies": n, "bytes_per_step_all_ranks": headline_bytes(),
+                       "l2": f"inputs larger than L2: each rank rotates over {n} copies of its shards = "
+                             f"{n * step_shard / 2**20:.0f} MiB >= 4 x L2 ({l2 / 2**20:.0f} MiB)",
+                       "launch": ("CUDA graph of back-to-back launches with programmatic dependent launch"
+                                  + ("; each op one fused TMA kernel per rank: peer stores of every output into "
+                                     "every rank's y over NVLink, per-source start / arrival counts, CTA 0 waits "
+                                     "for all ranks" if world > 1 else "")),
+                       "parallelism": f"row-sharded tensor parallel x{world}" if world > 1 else "1 GPU"},
+            "per_op_us": {k: round(v, 3) for k, v in per_op.items()},
+            "us_per_step": round(ms_max * 1e3 / args.steps, 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src + " (burst copy)",
-                         "traffic": (traffic or {}).get("fp8_gate_up_dram_bytes_per_launch"),
+                         "traffic": (round(tr * dom.nl / tr_ranks) if tr and tr_ranks else None),
+                         "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of "
+                                            "this kernel (profiles/traffic.json), scaled by rows" if tr else None),
                          "algorithmic_bytes_per_launch": dom_bytes,
-                         "kernel": "pb2::gemv_tma_kernel<FP8, 8, 2, 3> (gate_up 28672x4096: e4m3 weights + fp32 "
-                                   "row scales per launch, timed per launch with CUDA events over L2-rotated copies)",
-                         "layer_achieved": round(lbytes * args.steps / (ms * 1e-3) / 1e9, 1)},
-            "per_shape_us": per_shape,
-            "us_per_layer": round(ms_max * 1e3 / args.steps, 3),
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": layers[0].x.numel() * 2,
-                    "d2h_bytes_per_step": layers[0].ys[-1].numel() * 2,
-                    "serial_value": round(e2e_serial_value, 2),
-                    "how": "public API (paia_gemv.loader ctypes -> C ABI), eager launches; per step pinned H2D of x, "
-                           "4 GEMVs, D2H of the layer output; CUDA events around all K steps. value: the copies on "
-                           "two copy streams (step i+1's input lands while step i computes, step i's output drains "
-                           "while step i+1 computes; events order every copy against the compute that reads or "
-                           "overwrites its buffer). serial_value: copies and GEMVs in order on one stream"},
+                         "kernel": f"pb2::gemv_tma_kernel<FP8, 8, 2, 3> ({dom.name} {dom.nl}x{dom.K} rows of this "
+                                   f"rank: e4m3 weights + fp32 row scales; per-launch time from CUDA events over a "
+                                   f"graph of rotated launches{', including the exchange' if world > 1 else ''})"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 2,
+                    "d2h_bytes_per_step": sum(op.N * 2 for op in ops), "steps": e2e_steps,
+                    "how": "public API (paia_gemv.loader GemvLib methods; tp.ShardedGemv.fused on > 1 GPU), eager "
+                           "launches; per step a pinned H2D of x, the four ops, a pinned D2H of every op's full y, "
+                           "all in order on one stream; CUDA events around all steps, max over ranks"},
             "gpu_launches": launches,
             "clocks": clocks,
-            "check_rel_l2_vs_torch": round(check_err, 6),
+            "check_rel_l2_vs_torch": round(bad[1], 7),
         }
+        if world > 1:
+            result["fused_equals_nccl_bitwise"] = True
+            result["nccl_all_gather"] = nccl
+        result.update(extras)
         if cb is not None:
             result["cpu_baseline"] = cb
     if world > 1:
         dist.barrier()
+        for op in ops:
+            op.sg = None
+        for b in bufs.values():
+            b.close()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
     return 0
+
+
+def run_extras(lib, g, l2, peak, args):
+    """1-GPU extra keys of the bench line: the FP8 decode layer (the previous headline), every format's per-shape
+    microseconds on every Llama-3.1-8B and Qwen2.5-7B decode shape, and decode microseconds per token."""
+    import torch
+    from paia_gemv import synthetic, timing
+    out = {}
+    # the Llama-3.1-8B FP8 decode layer: qkv -> o -> gate_up -> down chained, rotated over >= 4 x L2 of layers
+    tuned = load_tuned()
+    probe = Layer(lib, "fp8", "llama31_8b", g, tuned)
+    lbytes = probe.weight_bytes()
+    L = max(4, math.ceil(4 * l2 / lbytes))
+    layers = [probe] + [Layer(lib, "fp8", "llama31_8b", g, tuned, random_codes=True) for _ in range(L - 1)]
+    us_layer = time_ops_graph([lay.calls for lay in layers], L * max(1, 40 // L))
+    out["decode_layer_fp8"] = {"us_per_layer": round(us_layer, 3), "GBps": round(lbytes / us_layer / 1e3, 1),
+                               "frac_of_peak": round(lbytes / us_layer / 1e3 / peak, 4),
+                               "how": "Llama-3.1-8B FP8 qkv -> o -> gate_up -> down, each reading the previous "
+                                      "output, CUDA graph with PDL, rotated over " + str(L) + " layers"}
+    del layers, probe
+    torch.cuda.empty_cache()
+    shapes = {}
+    for kind in ("bf16", "fp8", "int4", "int4_asym"):
+        for model in ("llama31_8b", "qwen25_7b"):
+            for name in ("qkv_fused", "o_proj", "gate_up_fused", "down_proj", "lm_head"):
+                N, K = synthetic.SHAPES[model][name]
+                vid, tup = variant_for(lib, kind, N, K, tuned)
+                bias = model == "qwen25_7b" and name == "qkv_fused"
+                first = Gemv(lib, kind, N, K, g, name, bias=bias, variant=vid, random_codes=True)
+                nc = timing.plan_rotation(first.weight_bytes(), l2)
+                copies = [first] + [Gemv(lib, kind, N, K, g, name, bias=bias, variant=vid, random_codes=True)
+                                    for _ in range(nc - 1)]
+                xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in copies]
+                ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in copies]
+                calls = [c.launcher(xx, yy) for c, xx, yy in zip(copies, xs, ys)]
+                us = timing.median(timing.time_graph(calls, samples=9))
+                wb = first.weight_bytes()
+                shapes[f"{kind}:{model}:{name}"] = {"N": N, "K": K, "variant": tup, "us": round(us, 3),
+                                                    "GBps": round(wb / us / 1e3, 1),
+                                                    "frac": round(wb / us / 1e3 / peak, 4)}
+                del copies, xs, ys, calls, first
+                torch.cuda.empty_cache()
+    out["per_shape_us"] = shapes
+    tokens = {}
+    for kind in ("bf16", "fp8", "int4", "int4_asym"):
+        for model in ("llama31_8b", "qwen25_7b"):
+            d = decode_token(lib, kind, model, g, tuned, peak, "per_op", reps=5)
+            tokens[f"{kind}:{model}"] = {"us_per_token": d["decode_us_per_token"], "GBps": d["GBps"],
+                                         "frac": d["frac_of_peak"]}
+    out["decode_us_per_token"] = tokens
+    out["decode_how"] = ("per token: every layer's qkv, o, gate_up, down chained (distinct weights per layer, Qwen qkv "
+                         "with bias), then the lm_head; one CUDA graph with PDL (the reference's per-token sum of "
+                         "per-op launches, paia-bench analyze_e4.py:177-196, measured as one sequence)")
+    return out
 
 
 def run_sweep(args):
@@ -1053,6 +1270,83 @@ def run_tp(args, rank, world, local_rank):
     return 0
 
 
+def run_tune(args):
+    """Per-shape variant choice for B200 written to paia-project_b200/tuned/b200.json in the reference's tuned-table
+    schema (src/tools/dev_sweep_bf16.py:90-99: per N x K the best (R, U, W, S, H) with its us and GB/s and the top 5 with
+    their % of the best; keys shapes / fp8_shapes / int4_shapes, plus int4_asym_shapes), which bench.py and the
+    reference's op adapters (paia-bench ours_bf16.py:32-38, ours_quant.py:29-36, platform tag "b200") read. Every real
+    Llama-3.1-8B / Qwen2.5-7B decode shape; graph mode over L2-rotated copies. Candidates: the default tuple, the TMA-fed
+    variants (R = 0) and, for N <= 1024 (where the CUDA-core instances run) or with --tune-all, every tuple. A variant
+    is kept only if its output matches the default variant's (rel L2 <= 1e-3)."""
+    import torch
+    from paia_gemv import load_lib, synthetic, timing
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    peak, _ = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(11)
+    l2 = timing.l2_bytes()
+    out_f = ROOT / "paia-project_b200" / "tuned" / "b200.json"
+    tuned = json.loads(out_f.read_text()) if out_f.exists() else {}
+    tuned["platform"] = "b200"
+    tuned["device"] = torch.cuda.get_device_name(0)
+    defaults = {"bf16": (2, 4, 4, 0, 1), "fp8": (2, 2, 4, 0, 1), "int4": (4, 2, 4, 0, 1), "int4_asym": (4, 2, 4, 0, 1)}
+    keys = {"bf16": "shapes", "fp8": "fp8_shapes", "int4": "int4_shapes", "int4_asym": "int4_asym_shapes"}
+    tables = {"bf16": lib.variants, "fp8": lib.variants_fp8, "int4": lib.variants_int4,
+              "int4_asym": lib.variants_int4_asym}
+    shapes = sorted({s for m in synthetic.SHAPES.values() for s in m.values()})
+    for kind in args.kinds.split(","):
+        kmult = {"bf16": 8, "fp8": 16}.get(kind, 128)
+        tuned.setdefault(keys[kind], {})
+        table = tables[kind]
+        tup = lambda v: tuple(v[k] for k in "RUWSH")            # noqa: E731
+        dflt = next(v["id"] for v in table if tup(v) == defaults[kind])
+        for (N, K) in shapes:
+            if K % kmult:
+                continue
+            cand = [v for v in table if args.tune_all or N <= 1024 or v["R"] == 0 or v["id"] == dflt]
+            first = Gemv(lib, kind, N, K, g, "tune", variant=dflt)
+            n = timing.plan_rotation(first.weight_bytes(), l2)
+            copies = [first] + [Gemv(lib, kind, N, K, g, "tune", variant=dflt, random_codes=True) for _ in range(n - 1)]
+            xs = [torch.randn(K, device="cuda", generator=g).to(torch.bfloat16) for _ in copies]
+            ys = [torch.empty(N, device="cuda", dtype=torch.bfloat16) for _ in copies]
+            first.variant = dflt
+            first.launcher(xs[0], ys[0])()
+            torch.cuda.synchronize()
+            ref = ys[0].float().clone()
+            rows = []
+            for v in cand:
+                for c in copies:
+                    c.variant = v["id"]
+                calls = [c.launcher(xx, yy) for c, xx, yy in zip(copies, xs, ys)]
+                rc = calls[0]()
+                torch.cuda.synchronize()
+                if rc:
+                    continue                                    # the variant cannot run this shape (-2)
+                err = ((ys[0].float() - ref).norm() / ref.norm()).item()
+                if not err <= 1e-3:
+                    print(json.dumps({"kind": kind, "N": N, "K": K, "variant": tup(v), "rejected_rel_l2": err}))
+                    continue
+                us = timing.median(timing.time_graph(calls, samples=5, target_ms=1.0))
+                rows.append((us, v))
+            rows.sort(key=lambda r: r[0])
+            wb = first.weight_bytes()
+            best_us, best = rows[0]
+            tuned[keys[kind]][f"{N}x{K}"] = {
+                "variant": {k: best[k] for k in "RUWSH"}, "us": round(best_us, 3),
+                "gbps": round(wb / best_us / 1e3, 1), "frac_of_peak": round(wb / best_us / 1e3 / peak, 4),
+                "top5": [{"variant": {k: v[k] for k in "RUWSH"}, "pct_of_best": round(100 * best_us / us, 1)}
+                         for us, v in rows[:5]],
+                "candidates": len(rows), "dev_only": True, "when": time.strftime("%Y-%m-%d %H:%M")}
+            print(json.dumps({"kind": kind, "N": N, "K": K, "best": tup(best), "us": round(best_us, 3),
+                              "default_us": round(next(u for u, v in rows if v["id"] == dflt), 3)}), flush=True)
+            del copies, xs, ys, first
+            torch.cuda.empty_cache()
+    out_f.parent.mkdir(parents=True, exist_ok=True)
+    out_f.write_text(json.dumps(tuned, indent=1) + "\n")
+    print(json.dumps({"wrote": str(out_f.relative_to(ROOT))}))
+    return 0
+
+
 def run_one(args):
     """A few launches of one shape through the default path (the C ABI call a user makes), for profilers: no timing."""
     import torch
@@ -1084,10 +1378,13 @@ def main():
     ap.add_argument("--sweep", action="store_true")
     ap.add_argument("--kinds", default="bf16,fp8,int4,int4_asym")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the 1-GPU extra keys (decode layer, shapes, tokens)")
     ap.add_argument("--one", default=None, help="profiling aid: KIND:NxK, e.g. fp8:28672x4096 (default variant)")
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
     ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
     ap.add_argument("--launches", type=int, default=4)
+    ap.add_argument("--tune", action="store_true", help="per-shape variant sweep -> paia-project_b200/tuned/b200.json")
+    ap.add_argument("--tune-all", action="store_true", help="with --tune: every tuple on every shape")
     ap.add_argument("--batched", action="store_true", help="M > 1 activation rows (paia_gemv_batched)")
     ap.add_argument("--copy-sweep", action="store_true",
                     help="TMA kernel on gate_up at explicit ring depths (copy size vs copy count)")
@@ -1105,6 +1402,8 @@ def main():
         return run_reference_arm(args, rank, world)
     if args.sweep:
         return run_sweep(args)
+    if args.tune:
+        return run_tune(args)
     if args.one:
         return run_one(args)
     if args.families:

@@ -58,25 +58,33 @@ int paia_gemv_int4_naive(const void* Wq, const void* scales, const void* x, void
 int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, void* y, void* scratch_bf16, int N, int K,
                            void* stream);
 
-/* No reference counterpart. paia_gemv_int4_unfused with library-owned scratch: the bf16 dequantised weights go to a
- * file-scope device array of 16 Mi elements (32 MiB), so the call allocates nothing. N * K above 16777216 (e.g. more
- * than 4096 x 4096) returns -2; other checks and codes as paia_gemv_int4_unfused (a >0 cudaError_t also when the
- * array's address cannot be looked up). Overlapping calls (two streams or threads) share the array and race; make
- * the first call on each device before any stream capture (it looks the address up with a runtime call). */
+/* No reference counterpart. paia_gemv_int4_unfused for callers that cannot hand the library a scratch buffer: a
+ * serving engine whose memory pool owns the whole HBM budget, a plain C host with no device allocator of its own, or
+ * a latency-critical loop where cudaMalloc / cudaFree would synchronise the device. The bf16 dequantised weights go
+ * to a file-scope device array of 16 Mi elements (32 MiB, held by every GPU that loads the library until the process
+ * exits), so the call allocates nothing. N * K above 16777216 (e.g. more than 4096 x 4096) returns -2; other checks
+ * and codes as paia_gemv_int4_unfused (a >0 cudaError_t also when the array's address cannot be looked up). The
+ * array keeps the last call's contents; each call overwrites the N * K elements it reads, so nothing needs clearing.
+ * Calls that overlap on the GPU (two streams, or two host threads) share the array and race. The first call on each
+ * device looks the array's address up with a runtime call and caches it: make that first call before any stream
+ * capture, and not across a cudaDeviceReset (the cached address does not survive it). */
 int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
                                   void* stream);
 
 /* ---- Row-sharded tensor parallelism (no reference kernel; BASELINE config 5, survey row 8e) ----
  * Rank `rank` of `world` (<= 8) holds rows [rank N_local, (rank+1) N_local) of W (and their scales/zeros/bias) and
  * computes them with the TMA-fed kernel, storing every output to every rank's full-size y (world * N_local bf16;
- * y_all[r] = rank r's buffer as mapped in this process, e.g. through CUDA IPC) at rank * N_local + row. Each CTA then
- * adds 1 to every rank's arrival counter (flag_all[r] = &counters_r[0], counters_r two zero-initialised uint32 in
- * rank r's memory, 8-byte aligned) with system-scope atomics. paia_gemv_tp_ctas gives the CTAs per launch (each
- * launch adds per_call = world * ctas to every counter); paia_gemv_tp_wait advances the local call epoch
- * (counters[1], in device memory, so captured CUDA graphs stay correct) and makes the stream wait until
- * counters[0] reaches epoch * per_call (wrap-safe compare), giving up after ~1 s with error code 6 in
- * paia_gemv_device_error(). Same argument checks and codes as the per-format calls; -2 also for a bad
- * world/rank/pointer or a shape the TMA kernel cannot stage. */
+ * y_all[r] = rank r's buffer as mapped in this process, e.g. through CUDA IPC) at rank * N_local + row.
+ * flag_all[r] = rank r's counter block: 32 zero-initialised uint32 in rank r's memory, 16-byte aligned (word 0: calls
+ * completed on r; words 8 + s: CTAs of rank s done storing into r; words 16 + s: calls rank s has started). Each call
+ * tells every rank that this rank has started it; each CTA stores into a rank's y only once that rank has started the
+ * same call (so a rank's readers of the previous y, earlier in its stream, are done), then counts itself in on every
+ * rank with system-scope atomics; CTA 0 waits until all CTAs of every rank have counted in, so this rank's y is
+ * complete when the launch ends (no separate wait; captured CUDA graphs stay correct, the counts live in device
+ * memory). Both waits give up after ~1 s with error code 8 (start) or 6 (arrivals) in paia_gemv_device_error();
+ * after that, zero every rank's counter block before the next call. Same argument checks and codes as the per-format
+ * calls; -2 also for a bad world/rank/pointer or a shape the TMA kernel cannot stage. paia_gemv_tp_ctas gives the
+ * CTAs of one launch (the same on every rank). */
 int paia_gemv_tp(int kind, const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
                  void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
                  void* stream);
@@ -89,7 +97,6 @@ int paia_gemv_tp_free(void* ptr);
 int paia_gemv_ipc_handle(const void* ptr, void* handle64);
 int paia_gemv_ipc_open(const void* handle64, void** ptr);
 int paia_gemv_ipc_close(void* ptr);
-int paia_gemv_tp_wait(unsigned int* counters, unsigned int per_call, void* stream);
 
 /* ---- B200 additions (no reference kernel; the reference's survey of this path proposes them) ---- */
 

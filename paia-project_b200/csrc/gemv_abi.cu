@@ -124,14 +124,31 @@ using namespace pb2;
 namespace {
 inline bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (uintptr_t)(a - 1)) == 0; }
 
-const Variant* table_of(int fmt, int* n) {
-    switch (fmt) {
-        case kBF16: return table_bf16(n);
-        case kFP8: return table_fp8(n);
-        case kINT4: return table_int4(n);
-        case kINT4A: return table_int4a(n);
-        default: *n = 0; return nullptr;
+// A format's public variant table: the reference's tuple grid (ids and order as the reference numbers them), then
+// the TMA-fed B200 variants (R = 0). Built once.
+struct PublicTable {
+    std::vector<Variant> v[4];
+    PublicTable() {
+        for (int f = 0; f < 4; ++f) {
+            int n = 0, m = 0;
+            const Variant* t = f == kBF16 ? table_bf16(&n) : f == kFP8 ? table_fp8(&n) : f == kINT4 ? table_int4(&n)
+                                                                                                  : table_int4a(&n);
+            const Variant* e = tma_public(f, &m);
+            v[f].assign(t, t + n);
+            v[f].insert(v[f].end(), e, e + m);
+        }
     }
+};
+const PublicTable& public_tables() {
+    static const PublicTable t;
+    return t;
+}
+
+const Variant* table_of(int fmt, int* n) {
+    if (fmt < 0 || fmt > 3) { *n = 0; return nullptr; }
+    const std::vector<Variant>& t = public_tables().v[fmt];
+    *n = (int)t.size();
+    return t.data();
 }
 
 // Shape and alignment contract of each format (the reference's checks, plus the bias and zero pointers).
@@ -173,8 +190,7 @@ bool is_default_tuple(int fmt, const Variant& v) {
 }
 
 // B200 path behind the default tuples, chosen per shape from the kernel-family comparison on B200 (every real
-// Llama-3.1-8B / Qwen2.5-7B shape, each format, alone and in decode-layer chains; profiles/
-// gemv_kernel_family_compare_b200.md):
+// Llama-3.1-8B / Qwen2.5-7B shape, each format, alone and in decode-layer chains; `bench.py --families`):
 //   * N <= 1024 (k/v projections): the tuple's own CUDA-core instance (it splits K across warps; 16-row tiles leave
 //     most SMs with a single partial tile) - signalled by returning -2;
 //   * otherwise the TMA-fed tensor-core kernel with the decode measured fastest (BF16 as is, FP8 e4m3 straight into
@@ -182,16 +198,18 @@ bool is_default_tuple(int fmt, const Variant& v) {
 //     (Alone, the register-fed kernel wins a few long-K INT4 shapes by up to 15%; inside the chained decode layer,
 //     which is how the op runs, the TMA kernel is faster for every INT4 layer sequence measured.)
 // Returns -2 when the chosen kernel cannot stage the shape (the caller then runs the tuple's own instance).
-int launch_b200_default(int fmt, const Params& p, cudaStream_t st) {
+// pdl = false: the launch waits for the whole preceding grid (no programmatic dependent launch), for callers whose
+// weights the preceding kernel writes.
+int launch_b200_default(int fmt, const Params& p, cudaStream_t st, bool pdl = true) {
     if (p.N <= 1024) return -2;
-    static const int maths[4][2] = {{5, 0}, {8, 0}, {7, 5}, {7, 5}};   // first choice, then a fallback (0: none)
+    static const int maths[4][2] = {{5, 0}, {8, 5}, {7, 5}, {7, 5}};   // first choice, then a fallback (0: none)
     for (int k = 0; k < 2; ++k) {
         const int math = maths[fmt][k];
         if (!math) break;
         const Variant* inst = find_instance(fmt, 0, 2, 8, math);
         if (!inst) continue;
         Variant v = *inst;
-        v.H = 1;
+        v.H = pdl ? 1 : 0;
         const LaunchOpts o{0, 0};
         const int rc = launch_variant(v, p, o, st);
         if (rc != -2) return rc;
@@ -241,13 +259,12 @@ int default_bf16_variant() {   // (R, U, W, S, H) = (2, 4, 4, 0, 1), looked up b
     return 0;
 }
 
-__device__ int g_device_error;   // written only by kernels whose bounded waits gave up (tensor-parallel path)
 }  // namespace
 
 namespace pb2tp {   // tensor-parallel helpers (named, outside the C linkage block: they hold a kernel)
 // The TMA-fed kernel every TP launch uses (the only one with the peer-store epilogue): the format's default decode.
 const Variant* tp_instance(int fmt, const Params& p, Variant* out) {
-    static const int maths[4][2] = {{5, 0}, {8, 0}, {7, 5}, {7, 5}};
+    static const int maths[4][2] = {{5, 0}, {8, 5}, {7, 5}, {7, 5}};
     for (int k = 0; k < 2; ++k) {
         const int math = maths[fmt][k];
         if (!math) break;
@@ -262,30 +279,6 @@ const Variant* tp_instance(int fmt, const Params& p, Variant* out) {
     return nullptr;
 }
 
-// One thread advances this rank's call epoch (counters[1]) and waits (bounded, ~1 s) until the arrival counter
-// (counters[0], incremented by every rank's CTAs) reaches epoch * per_call (wrap-safe); on timeout it records error
-// code 6 and returns, so the host reads an error instead of a hang. The epoch lives in device memory, so a captured
-// CUDA graph of TP calls stays correct on every replay.
-__global__ void tp_wait_kernel(unsigned int* counters, unsigned int per_call) {
-    if (threadIdx.x != 0) return;
-    const unsigned int epoch = counters[1] + 1u;
-    counters[1] = epoch;
-    const unsigned int expected = epoch * per_call;
-    uint64_t t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-        unsigned int v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counters) : "memory");
-        if ((int)(v - expected) >= 0) return;
-        uint64_t t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (t - t0 > 1000000000ull) {
-            atomicCAS(&g_device_error, 0, 6);
-            return;
-        }
-        __nanosleep(200);
-    }
-}
 }  // namespace pb2tp
 
 
@@ -322,7 +315,7 @@ int fill_ops(int kind, int nops, const paia_gemv_op* ops, pb2::GemvOp* out, int*
 // The TMA instance of a layer launch and its geometry: math 0 = the format's default decode (then a fallback when it
 // cannot stage the sequence), one CTA per SM so that every CTA is resident.
 int plan_layer(int kind, int math, Params& p, const Variant** inst_out, Planned* pl) {
-    static const int maths[4][2] = {{5, 0}, {8, 0}, {7, 5}, {7, 5}};
+    static const int maths[4][2] = {{5, 0}, {8, 5}, {7, 5}, {7, 5}};
     const int first = math ? math : maths[kind][0], second = math ? 0 : maths[kind][1];
     for (int m : {first, second}) {
         if (m < 5) break;
@@ -341,11 +334,11 @@ extern "C" {
 
 // ------------------------------------------------------------------ the reference's ABI
 
-int paia_gemv_bf16_variant_count(void) { int n = 0; table_bf16(&n); return n; }
+int paia_gemv_bf16_variant_count(void) { int n = 0; table_of(kBF16, &n); return n; }
 
 int paia_gemv_bf16_variant_info(int v, int* R, int* U, int* W, int* S, int* H) {
     int n = 0;
-    const Variant* t = table_bf16(&n);
+    const Variant* t = table_of(kBF16, &n);
     if (v < 0 || v >= n) return -1;
     *R = t[v].R; *U = t[v].U; *W = t[v].W; *S = t[v].S; *H = t[v].H;
     return 0;
@@ -355,14 +348,14 @@ int paia_gemv_bf16(const void* W, const void* x, void* y, int N, int K, int vari
     return run(kBF16, W, nullptr, nullptr, x, nullptr, y, N, K, variant, stream, nullptr);
 }
 
-int paia_gemv_fp8_variant_count(void) { int n = 0; table_fp8(&n); return n; }
+int paia_gemv_fp8_variant_count(void) { int n = 0; table_of(kFP8, &n); return n; }
 int paia_gemv_fp8_variant_info(int v, int* R, int* U, int* W, int* H) { return info4(kFP8, v, R, U, W, H); }
 
 int paia_gemv_fp8(const void* Wq, const void* scale, const void* x, void* y, int N, int K, int variant, void* stream) {
     return run(kFP8, Wq, scale, nullptr, x, nullptr, y, N, K, variant, stream, nullptr);
 }
 
-int paia_gemv_int4_variant_count(void) { int n = 0; table_int4(&n); return n; }
+int paia_gemv_int4_variant_count(void) { int n = 0; table_of(kINT4, &n); return n; }
 int paia_gemv_int4_variant_info(int v, int* R, int* U, int* W, int* H) { return info4(kINT4, v, R, U, W, H); }
 
 int paia_gemv_int4(const void* Wq, const void* scales, const void* x, void* y, int N, int K, int variant, void* stream) {
@@ -380,15 +373,38 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
     if (N <= 0 || K <= 0 || (K & 127) || !aligned(Wq, 16) || !aligned(x, 16) || !aligned(scales, 2) ||
         !aligned(scratch_bf16, 16))
         return -2;
-    const int rc = launch_int4_dequant(Wq, scales, scratch_bf16, N, K, static_cast<cudaStream_t>(stream));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int rc = launch_int4_dequant(Wq, scales, scratch_bf16, N, K, st);
     if (rc) return rc;
-    return paia_gemv_bf16(scratch_bf16, x, y, N, K, default_bf16_variant(), stream);
+    // The BF16 GEMV (the default tuple's path, as gemv_quant.cu:96 runs it) reads the scratch the dequantisation grid
+    // has just written, so it is launched without programmatic dependent launch: its kernels start streaming W before
+    // their grid-dependency wait, and only a full stream-order dependency makes the previous grid's writes visible.
+    const int arc = check_args(kBF16, scratch_bf16, nullptr, nullptr, x, nullptr, y, N, K);
+    if (arc) return arc;
+    Params p{};
+    p.W = static_cast<const uint8_t*>(scratch_bf16);
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.y = static_cast<__nv_bfloat16*>(y);
+    p.N = N;
+    p.K = K;
+    p.nchunk = row_bytes(kBF16, K) / 16;
+    p.groups = K / 128;
+    const int brc = launch_b200_default(kBF16, p, st, false);
+    if (brc != -2) return brc;
+    int n = 0;
+    Variant v = table_bf16(&n)[default_bf16_variant()];
+    v.H = 0;
+    const LaunchOpts none{0, 0};
+    return launch_variant(v, p, none, st);
 }
 
-// Unfused INT4 with library-owned scratch. The scratch is a file-scope device array (module-load storage, not an
-// allocation in this call); its device address is looked up once per device with cudaGetSymbolAddress. Calls that
-// overlap in time (two streams, or two host threads) share the array and race; the first call on a device should
-// come before any stream capture, since the lookup is a host-side runtime call.
+// Unfused INT4 with library-owned scratch, for callers that cannot pass a scratch buffer (a memory pool that owns
+// all of HBM, a C host without a device allocator, a loop where cudaMalloc / cudaFree would synchronise the device).
+// The scratch is a file-scope device array (module-load storage, not an allocation in this call); its device
+// address is looked up once per device with cudaGetSymbolAddress, with that device current, and cached (the cache
+// does not survive cudaDeviceReset). Calls that overlap on the GPU (two streams, or two host threads) share the array
+// and race; it keeps the last call's contents, and every call overwrites the N x K elements it reads. The first call
+// on a device should come before any stream capture, since the lookup is a host-side runtime call.
 namespace {
 constexpr size_t kStaticScratchElems = (size_t)16 << 20;       // 16 Mi bf16 = 32 MiB (e.g. N x K = 4096 x 4096)
 static __device__ __align__(256) __nv_bfloat16 g_static_scratch[kStaticScratchElems];
@@ -423,7 +439,7 @@ int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const v
                  void* stream) {
     if (kind < 0 || kind > 3 || world < 1 || world > 8 || rank < 0 || rank >= world || !y_all || !flag_all) return -2;
     for (int r = 0; r < world; ++r)
-        if (!y_all[r] || !flag_all[r] || !aligned(y_all[r], 2) || !aligned(flag_all[r], 4)) return -2;
+        if (!y_all[r] || !flag_all[r] || !aligned(y_all[r], 2) || !aligned(flag_all[r], 16)) return -2;
     const int rc = check_args(kind, Wq, s, z, x, bias, y_all[rank], N_local, K);
     if (rc) return rc;
     Params p{};
@@ -438,6 +454,7 @@ int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const v
     p.nchunk = row_bytes(kind, K) / 16;
     p.groups = K / 128;
     p.tp_world = world;
+    p.tp_rank = rank;
     p.tp_off = rank * N_local;
     for (int r = 0; r < world; ++r) {
         p.tp_y[r] = static_cast<__nv_bfloat16*>(y_all[r]);
@@ -503,13 +520,6 @@ int paia_gemv_tp_ctas(int kind, int N_local, int K) {
     const LaunchOpts o{0, 0};
     if (launch_variant(v, p, o, nullptr, &G)) return -2;
     return (int)G;
-}
-
-int paia_gemv_tp_wait(unsigned int* counters, unsigned int per_call, void* stream) {
-    if (!counters || !aligned(counters, 8) || per_call == 0) return -2;
-    pb2tp::tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counters, per_call);
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? 0 : (int)e;
 }
 
 // ------------------------------------------------------------------ batched x (M > 1)
@@ -644,7 +654,7 @@ int paia_gemv_plan_destroy(paia_gemv_plan* plan) {
 
 const char* paia_gemv_version(void) { return "paia-gemv-b200 1.0 (sm_100a)"; }
 
-int paia_gemv_int4_asym_variant_count(void) { int n = 0; table_int4a(&n); return n; }
+int paia_gemv_int4_asym_variant_count(void) { int n = 0; table_of(kINT4A, &n); return n; }
 int paia_gemv_int4_asym_variant_info(int v, int* R, int* U, int* W, int* H) { return info4(kINT4A, v, R, U, W, H); }
 
 int paia_gemv_int4_asym(const void* Wq, const void* scales, const void* zeros, const void* x, void* y, int N, int K,
@@ -714,16 +724,8 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
     return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));
 }
 
-// Device-side error word of the current device (0 = none); clear != 0 resets it. Synchronous (a symbol copy).
-int paia_gemv_device_error(int clear) {
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
-    if (clear && v) {
-        const int zero = 0;
-        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
-    }
-    if (v) return v;
-    return tma_device_error(clear);        // bounded mbarrier waits of the TMA-fed kernels
-}
+// Device-side error word of the current device (0 = none; the codes of the TMA-fed kernels' bounded waits, 6 and 8
+// from the tensor-parallel exchange); clear != 0 resets it. Synchronous (a symbol copy).
+int paia_gemv_device_error(int clear) { return tma_device_error(clear); }
 
 }  // extern "C"

@@ -60,6 +60,8 @@ struct GemvOp {
     int N, K, nchunk, groups, nch, act, kc, rs;
 };
 constexpr int kMaxOps = 6;             // ops carried in the kernel parameters
+// Tensor-parallel counter block of one rank (uint32 words): epoch, then per-source arrival and ready counts.
+constexpr int kTpEpoch = 0, kTpArrive = 8, kTpReady = 16, kTpCounterWords = 32;
 constexpr int kMaxPlanOps = 4096;       // ops of a plan (device-memory op table)
 
 struct Params {
@@ -81,10 +83,13 @@ struct Params {
     int mr;                        // TMA kernels: halves per row of a stage's metadata slot
     int ring;                      // TMA kernels: stages in the shared-memory ring
     int pre;                       // TMA kernels: stages streamed before x is staged (0 = the whole ring)
-    // Row-sharded tensor parallelism (TMA kernels; tp_world = 0: off). This rank computes rows [0, N) of its shard and
-    // stores each output to every rank's full-size y (peer memory over NVLink) at tp_off + row; when a CTA is done
-    // it adds 1 to every rank's arrival counter (system-scope atomics), which paia_gemv_tp_wait waits on.
-    int tp_world, tp_off;
+    // Row-sharded tensor parallelism (TMA kernels; tp_world = 0: off). Rank tp_rank computes rows [0, N) of its shard
+    // and stores each output to every rank's full-size y (peer memory over NVLink) at tp_off + row. tp_flag[r] is
+    // rank r's counter block (kTpCounterWords uint32): [kTpEpoch] calls completed on r, [kTpArrive + s] CTAs of rank
+    // s that finished their stores into r, [kTpReady + s] calls rank s has started (its readers of the previous y are
+    // done). CTA 0 of each launch waits for every rank's CTAs before the grid ends, so y is complete when the kernel
+    // is; no rank stores into a peer's y before that peer has started the same call.
+    int tp_world, tp_off, tp_rank;
     __nv_bfloat16* tp_y[8];
     unsigned int* tp_flag[8];
     // Layer mode (TMA kernels; nops = 0: off, the single GEMV above). One persistent cooperative launch runs ops

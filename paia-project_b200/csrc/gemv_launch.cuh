@@ -157,6 +157,7 @@ const Variant* table_int4a(int* n);
 const Variant* find_instance(int fmt, int R, int U, int W, int math);
 const Variant* mma_instances(int fmt, int math, int* n);
 const Variant* tma_instances(int fmt, int math, int* n);
+const Variant* tma_public(int fmt, int* n);                  // the TMA variants appended to each format's table
 int tma_device_error(int clear);
 
 }  // namespace pb2

@@ -101,6 +101,15 @@ __device__ __forceinline__ uint32_t nib_hi_f16(uint32_t w) { return (w & 0x00F00
 template <int F>
 __host__ __device__ constexpr int mma_kpad(int K) { return (K + MmaStep<F>::k - 1) / MmaStep<F>::k * MmaStep<F>::k; }
 
+// Decodes that stage x as four byte planes (FP8 e4m3 terms, DEC 3; INT4 int8 digits, DEC 2): bytes from plane q to
+// plane q + 1 for a staged length kp. The lanes of one quarter-warp read two planes at the same step offset, so
+// consecutive planes start in different halves of the 32 banks (FP8 reads 16-byte pieces of 64-byte steps: planes
+// 64 bytes apart modulo 128; INT4 reads 16-byte pieces 32 bytes apart in 128-byte steps: planes 16 bytes apart).
+template <int F, int DEC>
+__host__ __device__ constexpr int x_plane_stride(int kp) {
+    return (F == kFP8 && DEC == 3) ? ((kp + 127) & ~127) + 64 : kp + 16;
+}
+
 // Shared memory: x [Kpad] 16-bit values, then (INT4) sum of x per 128-group [Kpad/128] floats, then the partial sums
 // of straddling tiles [NW][2][16] floats, then two words (FP8: the exponent e and 2^-e).
 template <int F, int NW>
@@ -228,10 +237,13 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         x_blocks<0, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) { reinterpret_cast<uint4*>(xs)[i] = v; }, nullptr, map);   // K % 8 == 0
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     } else if constexpr (F == kFP8 && DEC == 3) {
-        // x * 2^-e (max|x| * 2^-e in [128, 256)) split into two e4m3 terms hi + lo, bytes in natural order: hi at xs,
-        // lo at xs + Kpad + 64 bytes. hi = RN(v) keeps 4 significant bits and lo = RN(v - hi) the next 4, so hi + lo == v
-        // exactly for |v| >= 2^-2 (bf16 carries 8 significant bits); smaller values keep an absolute error below
-        // 2^-10, i.e. < 2^-17 of max|x|.
+        // v = x * 2^-e (max|x| * 2^-e in [128, 256)) as four e4m3 terms in two exponent tiers, one byte plane each
+        // (bytes in natural order, plane q at xs + q x_plane_stride): hi0 = RN(v) keeps 4 significant bits and
+        // lo0 = RN(v - hi0) the next 4, so hi0 + lo0 == v exactly for |v| >= 2^-2 (bf16 carries 8 significant bits).
+        // Below that lo0 (or hi0) falls into the e4m3 subnormals and the rest r = v - hi0 - lo0 (|r| <= 2^-10, exact
+        // in fp32) goes into tier 1 at 2^16 r: hi1 = RN(2^16 r), lo1 = RN(2^16 r - hi1). The kernel weighs tier 1 by
+        // 2^-16, so x is reproduced exactly for every element within 2^25 of max|x| (an outlier channel of an LLM
+        // activation leaves the ordinary elements exact), and smaller ones keep an error below 2^-33 of max|x|.
         float m = 0.f;
         uint4 xc[XR] = {};
         x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
@@ -256,28 +268,30 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         }
         sync();
         const float inv = xscale[1];
-        uint8_t* xh = reinterpret_cast<uint8_t*>(xs);
-        uint8_t* xl = xh + Kp + 64;          // +64: hi and lo reads of one quarter-warp fall in different banks
+        uint8_t* x0 = reinterpret_cast<uint8_t*>(xs);
+        const int ps = x_plane_stride<F, DEC>(Kp);
         x_blocks<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
-            uint2 h = make_uint2(0u, 0u), l = make_uint2(0u, 0u);
+            uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
             if (8 * i < p.K) {
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-                uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float a = bf_lo(vv[j]) * inv, b = bf_hi(vv[j]) * inv;
-                    const __nv_fp8x2_storage_t hp = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
-                    const float2 hf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(hp, __NV_E4M3)));
-                    const __nv_fp8x2_storage_t lp =
-                        __nv_cvt_float2_to_fp8x2(make_float2(a - hf.x, b - hf.y), __NV_SATFINITE, __NV_E4M3);
-                    hw[j >> 1] |= (uint32_t)hp << (16 * (j & 1));
-                    lw[j >> 1] |= (uint32_t)lp << (16 * (j & 1));
+                    float2 r = make_float2(bf_lo(vv[j]) * inv, bf_hi(vv[j]) * inv);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        // term q of the pair; every residual r - t is exact in fp32, and so is the tier step 2^16
+                        const __nv_fp8x2_storage_t t = __nv_cvt_float2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
+                        w[q][j >> 1] |= (uint32_t)t << (16 * (j & 1));
+                        if (q < 3) {
+                            const float2 tf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(t, __NV_E4M3)));
+                            r = make_float2(r.x - tf.x, r.y - tf.y);
+                            if (q == 1) r = make_float2(r.x * 65536.f, r.y * 65536.f);
+                        }
+                    }
                 }
-                h = make_uint2(hw[0], hw[1]);
-                l = make_uint2(lw[0], lw[1]);
             }
-            reinterpret_cast<uint2*>(xh)[i] = h;
-            reinterpret_cast<uint2*>(xl)[i] = l;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) reinterpret_cast<uint2*>(x0 + (size_t)q * ps)[i] = make_uint2(w[q][0], w[q][1]);
         }, xc, map);
     } else if constexpr (F == kFP8) {
         // max |x| over the CTA, then x * 2^-e in f16 (exact while max|x| * 2^-e < 2^15 and values stay normal)
@@ -326,12 +340,14 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
             reinterpret_cast<uint4*>(xs)[i] = o;
         }, xc, map);
     } else if constexpr (DEC == 2) {
-        // INT4 for the integer MMA: v = x * 2^s rounded to an integer of magnitude <= 2^20 (exact for every element
-        // within 2^12 of max|x|, bf16 carrying 8 significant bits; smaller ones keep an error below 2^-21 max|x|),
-        // split into three signed base-128 digits d0 + 128 d1 + 128^2 d2, each an int8 plane of Kpad bytes at
-        // xs + d (Kpad + 16) with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
+        // INT4 for the integer MMA: v = x * 2^s rounded to an integer of magnitude <= 2^27 (exact for every element
+        // within 2^19 of max|x|, bf16 carrying 8 significant bits, so an outlier channel of an LLM activation leaves
+        // the ordinary elements exact; smaller ones keep an error below 2^-28 max|x|), split into four signed base-128
+        // digits d0 + 128 d1 + 128^2 d2 + 128^3 d3, each an int8 plane of Kpad bytes at xs + d (Kpad + 16) with every
+        // 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
         // Per 128-group g: the digit sums S_d (int) at gsum[8g + d], sum(v) (float) at gsum[8g + 4], and the
-        // symmetric offsets 8 (S_0 + 128 S_1) and 8 128^2 S_2 (floats, exact) at gsum[8g + 5] and gsum[8g + 6].
+        // symmetric offsets 8 (S_0 + 128 S_1) and 8 128^2 (S_2 + 128 S_3) (floats, exact) at gsum[8g + 5] and
+        // gsum[8g + 6].
         // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
         float m = 0.f;
         bool bad = false;
@@ -358,7 +374,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
                 inv = __int_as_float(0x7FC00000);                         // NaN or infinity in x
             } else if (mm > 0.f) {
                 const int ex = (int)((__float_as_uint(mm) >> 23) & 0xFF) - 127;   // floor(log2) (subnormal: -127)
-                sh = 19 - (ex < -126 ? -126 : ex);                        // max|x| * 2^sh in [2^19, 2^20)
+                sh = 26 - (ex < -126 ? -126 : ex);                        // max|x| * 2^sh in [2^26, 2^27)
                 sh = sh > 126 ? 126 : sh;                                 // 2^-sh stays a normal float
                 inv = __uint_as_float((uint32_t)(127 - sh) << 23);
             }
@@ -374,42 +390,44 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         int* gi = reinterpret_cast<int*>(gsum);
         x_blocks_all<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             // blocks past K / 8 arrive as zeros and stage as zero digits
-            int sd[3] = {0, 0, 0};
+            int sd[4] = {0, 0, 0, 0};
             if (i < Kp / 8) {
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-                int dg[3][8];
+                int dg[4][8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const float xf = (j & 1) ? bf_hi(vv[j >> 1]) : bf_lo(vv[j >> 1]);
-                    // v = x 2^sh exactly (an integer, |v| <= 2^20); t = v + 64 (1 + 128 + 128^2) >= 0 splits into
-                    // base-128 digits u0 + 128 u1 + 128^2 u2, and d = u - 64 gives v = d0 + 128 d1 + 128^2 d2 with
-                    // d0, d1 in [-64, 63] and d2 in [-64, 64]: integer work and one conversion per element
-                    const int t = __float2int_rn((xf * up) * up2) + 1056832;
+                    // v = x 2^sh exactly (an integer, |v| <= 2^27); t = v + 64 (1 + 128 + 128^2 + 128^3) >= 0 splits
+                    // into base-128 digits u0 + 128 u1 + 128^2 u2 + 128^3 u3, and d = u - 64 gives
+                    // v = d0 + 128 d1 + 128^2 d2 + 128^3 d3 with d0..d2 in [-64, 63] and d3 in [-64, 64]: integer
+                    // work and one conversion per element
+                    const int t = __float2int_rn((xf * up) * up2) + 135274560;
                     dg[0][j] = (t & 127) - 64;
                     dg[1][j] = ((t >> 7) & 127) - 64;
-                    dg[2][j] = (t >> 14) - 64;
+                    dg[2][j] = ((t >> 14) & 127) - 64;
+                    dg[3][j] = (t >> 21) - 64;
                 }
 #pragma unroll
-                for (int d = 0; d < 3; ++d) {
+                for (int d = 0; d < 4; ++d) {
                     sd[d] = ((dg[d][0] + dg[d][1]) + (dg[d][2] + dg[d][3])) + ((dg[d][4] + dg[d][5]) + (dg[d][6] + dg[d][7]));
                     // evens first (x0, x2, x4, x6), then odds: the low nibbles of a byte pair hold the even k
                     const uint32_t e = __byte_perm(__byte_perm(dg[d][0], dg[d][2], 0x0040), __byte_perm(dg[d][4], dg[d][6], 0x0040), 0x5410);
                     const uint32_t o = __byte_perm(__byte_perm(dg[d][1], dg[d][3], 0x0040), __byte_perm(dg[d][5], dg[d][7], 0x0040), 0x5410);
-                    *reinterpret_cast<uint2*>(planes + (size_t)d * (Kp + 16) + 8 * (size_t)i) =
-                        make_uint2(e, o);   // planes Kpad + 16 apart: no bank conflicts between them
+                    *reinterpret_cast<uint2*>(planes + (size_t)d * x_plane_stride<F, DEC>(Kp) + 8 * (size_t)i) =
+                        make_uint2(e, o);
                 }
             }
 #pragma unroll
-            for (int d = 0; d < 3; ++d)
+            for (int d = 0; d < 4; ++d)
 #pragma unroll
                 for (int o = 8; o > 0; o >>= 1) sd[d] += __shfl_xor_sync(0xffffffffu, sd[d], o);   // 16-lane groups
             if (i < Kp / 8 && (i & 15) == 0) {
                 const int gg = i >> 4;
 #pragma unroll
-                for (int d = 0; d < 3; ++d) gi[8 * gg + d] = sd[d];
-                gsum[8 * gg + 4] = (float)sd[0] + 128.f * (float)sd[1] + 16384.f * (float)sd[2];
+                for (int d = 0; d < 4; ++d) gi[8 * gg + d] = sd[d];
+                gsum[8 * gg + 4] = ((float)sd[0] + 128.f * (float)sd[1]) + (16384.f * (float)sd[2] + 2097152.f * (float)sd[3]);
                 gsum[8 * gg + 5] = 8.f * ((float)sd[0] + 128.f * (float)sd[1]);
-                gsum[8 * gg + 6] = 131072.f * (float)sd[2];
+                gsum[8 * gg + 6] = 131072.f * ((float)sd[2] + 128.f * (float)sd[3]);
             }
         }, xc, map);
     } else if constexpr (DEC == 1) {

@@ -33,7 +33,12 @@
 //             and their phases run on across op boundaries, and the consumers of op j wait for every CTA's outputs
 //             of op j - 1 (a per-op completion counter) before they stage x of op j.
 //   waits     every wait gives up after ~2 s (%globaltimer), records an error code that paia_gemv_device_error()
-//             reports, and carries on without waiting, so a fault can never hang the GPU.
+//             reports, and carries on without waiting, so a fault can never hang the GPU; once one wait has given
+//             up, every wait that has run for 1 ms gives up at once, and the producer keeps the CTA alive 200 us for
+//             its copies in flight before it exits.
+//   tp        row-sharded tensor parallelism: the epilogue stores every output into every rank's y over NVLink; the
+//             ranks count calls started and CTAs finished in each other's counter blocks, and CTA 0 waits until every
+//             rank's CTAs are done, so a rank's y is complete when its grid ends (tp_enter / tp_leave).
 #pragma once
 #include "gemv_mma.cuh"
 
@@ -63,12 +68,20 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Whether a bounded wait has already given up (this launch or an earlier one whose error the host has not cleared).
+__device__ __forceinline__ bool tma_aborted() { return *reinterpret_cast<volatile int*>(&g_tma_error) != 0; }
+// A wait that has run for 1 ms checks tma_aborted(): once one wait of any CTA gave up, the launch's pipeline is out
+// of step, so every further wait gives up at once instead of spinning its own full limit.
+constexpr uint64_t kAbortCheckNs = 1000000ull;
+
 // Wait for phase `parity` of m for at most ~2 s; on timeout record `code` and return false (the caller carries on).
 __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, int code) {
     if (mbar_test(m, parity)) return true;
     const uint64_t t0 = global_ns();
     while (!mbar_test(m, parity)) {
-        if (global_ns() - t0 > 2000000000ull) {
+        const uint64_t dt = global_ns() - t0;
+        if (dt > kAbortCheckNs && tma_aborted()) return false;
+        if (dt > 2000000000ull) {
             atomicCAS(&g_tma_error, 0, code);
             return false;
         }
@@ -147,7 +160,7 @@ __host__ __device__ constexpr int tma_kx(int K) {
 }
 
 // Shared-memory layout (bytes): [0,640) mbarriers; ring x st_bytes; metadata ring x tma_meta_bytes (16-byte
-// multiples); x: Kx x 2 (INT4 integer path: Kx x 3) + 64 (FP8 lo plane at Kx + 64, INT4 planes Kx + 16 apart);
+// multiples); x: Kx x 2 + 64, or four byte planes x_plane_stride apart (FP8 e4m3 terms, INT4 integer digits);
 // INT4 group sums (tma_gsum_words per group); tile partials NB x NC x 16 floats; per consumer warp its x scale
 // (4 floats) and a staging scratch word (kTmaTailBytes).
 // Batched kernels (BAT): x rows xm, each with its own x region, group sums and scale; partial buffers of 16 rows x 8
@@ -155,7 +168,9 @@ __host__ __device__ constexpr int tma_kx(int K) {
 constexpr int kTmaTailBytesBat = 256;
 template <int F, int DEC>
 __host__ __device__ constexpr int tma_xrow_bytes(int K) {   // one staged x row (16-byte multiple)
-    return tma_kx<F>(K) * (((F == kINT4 || F == kINT4A) && DEC == 2) ? 3 : 2) + 64;
+    return ((F == kFP8 && DEC == 3) || ((F == kINT4 || F == kINT4A) && DEC == 2))
+               ? 4 * x_plane_stride<F, DEC>(tma_kx<F>(K))          // four byte planes
+               : tma_kx<F>(K) * 2 + 64;
 }
 template <int F, int NC, int DEC, bool BAT = false>
 __host__ __device__ inline size_t tma_smem_bytes(int K, int ring, int nch, int mr, int st_bytes, int xm = 1) {
@@ -333,7 +348,7 @@ template <int F, int DEC, int NU, bool CHECK, int U>
 __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1, const uint8_t* r0p, const uint8_t* r1p,
                                           const uint16_t* xs, const float* gsum, const uint16_t* sc0,
                                           const uint16_t* sc1, const uint16_t* zr0, const uint16_t* zr1, int sl, int gs,
-                                          int c, int nchunk, int xlo_off) {
+                                          int c, int nchunk, int xps) {
     constexpr int SK = MmaStep<F>::k;
     uint4 w0[NU], w1[NU];
 #pragma unroll
@@ -353,11 +368,11 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
             mma_bf16(A.a[u][1], w0[u].z, w1[u].z, w0[u].w, w1[u].w, xv[u].z, xv[u].w);
         }
     } else if constexpr (F == kFP8 && DEC == 3) {
-        // e4m3 weights straight into the tensor cores. x = hi + lo (two e4m3 terms) rides in MMA columns 0 (hi) and
-        // 1 (lo): lanes of group g = 1 supply B column 1, all others column 0's hi bytes, so one mma.sync per 32
-        // weights and row yields both dot products (columns 2-7 repeat hi and are never read).
+        // e4m3 weights straight into the tensor cores. x = hi0 + lo0 + 2^-16 (hi1 + lo1) (four e4m3 terms) rides in
+        // MMA columns 0-3: lanes of group g supply B column g from plane g & 3, so one mma.sync per 32 weights and row
+        // yields all four dot products (columns 4-7 repeat planes 0-3 and are never read).
         const int grp = (int)(threadIdx.x & 31) >> 2;
-        const uint8_t* xb8 = reinterpret_cast<const uint8_t*>(xs) + (size_t)gs * 64 + 16 * c + (grp == 1 ? xlo_off + 48 : 0);
+        const uint8_t* xb8 = reinterpret_cast<const uint8_t*>(xs) + (size_t)gs * 64 + 16 * c + (size_t)(grp & 3) * xps;
         uint4 xv[NU];
 #pragma unroll
         for (int u = 0; u < NU; ++u) xv[u] = *reinterpret_cast<const uint4*>(xb8 + 64 * u);
@@ -390,18 +405,17 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
             }
         }
     } else if constexpr (DEC == 2) {
-        // INT4, integer MMA against x as three int8 digit planes; lane group g reads plane g (g < 3), so MMA column d
-        // carries digit d. One LOP3 per word and nibble half: low nibbles go in as u8 n (chain L), high nibbles
-        // unshifted as u8 16 n (chain H), each mma.sync taking two words of one half against the matching even / odd
-        // x of those words. Per group: sum_d 128^d (L_d + H_d / 16 - 8 S_d) = sum_d (16 L_d + H_d) 128^d / 16 - C,
-        // with C = 8 sum_d 128^d S_d of the lane's digits staged per group (lanes c = 0 / 1 hold digits 0-1 / 2;
-        // c = 2, 3 carry unused columns and are never read). 16 L + H stays below 2^21, exact as a float.
+        // INT4, integer MMA against x as four int8 digit planes; lane group g reads plane g & 3, so MMA column d
+        // carries digit d (columns 4-7 repeat them and are never read). One LOP3 per word and nibble half: low
+        // nibbles go in as u8 n (chain L), high nibbles unshifted as u8 16 n (chain H), each mma.sync taking two words
+        // of one half against the matching even / odd x of those words. Per group:
+        // sum_d 128^d (L_d + H_d / 16 - 8 S_d) = sum_d (16 L_d + H_d) 128^d / 16 - C, with C = 8 sum_d 128^d S_d of the
+        // lane's digits staged per group (lanes c = 0 / 1 hold digits 0-1 / 2-3; c = 2, 3 hold unused columns).
+        // 16 L + H stays below 2^21, so every product with 128^d / 16 is an exact float.
         const int grp = (int)(threadIdx.x & 31) >> 2;
-        // (lanes of group 3, an unused column, read plane 1 so that no quarter-warp meets a bank twice)
-        const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp < 3 ? grp : 1) * xlo_off +
-                            (size_t)gs * 128 + 32 * c;
+        const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp & 3) * xps + (size_t)gs * 128 + 32 * c;
         const float flo = c == 0 ? 0.0625f : (c == 1 ? 1024.f : 0.f);
-        const float fhi = c == 0 ? 8.f : 0.f;
+        const float fhi = c == 0 ? 8.f : (c == 1 ? 131072.f : 0.f);
 #pragma unroll
         for (int u = 0; u < NU; ++u) {
             const uint4 xa = *reinterpret_cast<const uint4*>(xp + 128 * u);
@@ -546,11 +560,73 @@ __device__ __forceinline__ void wait_count(const unsigned int* c, unsigned int t
         unsigned int v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
         if (v >= target) return;
-        if (global_ns() - t0 > 2000000000ull) {
+        const uint64_t dt = global_ns() - t0;
+        if (dt > kAbortCheckNs && tma_aborted()) return;
+        if (dt > 2000000000ull) {
             atomicCAS(&g_tma_error, 0, code);
             return;
         }
         __nanosleep(32);
+    }
+}
+
+// ---------------------------------------------------------------- row-sharded tensor parallelism (tp_world > 0)
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* a) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_add_sys(unsigned int* a, unsigned int v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" :: "l"(a), "r"(v) : "memory");
+}
+// Bounded wait (~1 s over all of them) until blk[base + s] reaches target (wrap-safe) for every rank s but `skip`;
+// on timeout records `code` and returns false.
+__device__ __forceinline__ bool tp_wait_counts(const unsigned int* blk, int base, int world, int skip,
+                                               unsigned int target, int code) {
+    const uint64_t t0 = global_ns();
+    for (int s = 0; s < world; ++s) {
+        if (s == skip) continue;
+        while ((int)(ld_acquire_sys(blk + base + s) - target) < 0) {
+            const uint64_t dt = global_ns() - t0;
+            if (dt > kAbortCheckNs && tma_aborted()) return false;
+            if (dt > 1000000000ull) {
+                atomicCAS(&g_tma_error, 0, code);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+// Start of a TP call in one CTA's epilogue warp, after the grid-dependency wait (so the previous call on this rank has
+// ended): returns the calls this rank has completed, e. CTA 0 tells every rank that this rank has started call e + 1,
+// which orders its readers of call e's y (earlier in its stream) before any peer's stores of this call; then the CTA
+// waits (bounded, error 8) until every other rank has started call e + 1 before it stores into their y.
+__device__ __forceinline__ unsigned int tp_enter(const Params& p, int lane) {
+    const unsigned int* mine = p.tp_flag[p.tp_rank];
+    const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(mine + kTpEpoch);
+    if (lane == 0) {
+        if (blockIdx.x == 0)
+            for (int r = 0; r < p.tp_world; ++r) red_add_sys(p.tp_flag[r] + kTpReady + p.tp_rank, 1u);
+        tp_wait_counts(mine, kTpReady, p.tp_world, p.tp_rank, e + 1u, 8);
+    }
+    __syncwarp();
+    return e;
+}
+// End of a TP call in one CTA's epilogue warp: every lane's stores into the ranks' y are released (warp barrier, then
+// a system-scope fence by lane 0, cumulative) before this CTA counts itself in on every rank. CTA 0 then waits
+// (bounded, error 6) until all CTAs of every rank have counted in on this rank, and advances the epoch: the grid ends
+// only when this rank's y is complete.
+__device__ __forceinline__ void tp_leave(const Params& p, int lane, unsigned int e) {
+    __syncwarp();
+    if (lane == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int r = 0; r < p.tp_world; ++r) red_add_sys(p.tp_flag[r] + kTpArrive + p.tp_rank, 1u);
+        if (blockIdx.x == 0) {
+            unsigned int* mine = p.tp_flag[p.tp_rank];
+            tp_wait_counts(mine, kTpArrive, p.tp_world, -1, (e + 1u) * gridDim.x, 6);
+            *reinterpret_cast<volatile unsigned int*>(mine + kTpEpoch) = e + 1u;
+        }
     }
 }
 
@@ -696,6 +772,12 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 if (++j == NCH) { j = 0; ++t; }
             }
         }
+        if (lane == 0 && tma_aborted()) {
+            // a wait gave up, so the consumers may not have waited for every stage: keep the CTA (and its shared
+            // memory) alive for 200 us, long enough for this warp's copies in flight to land
+            const uint64_t t0 = global_ns();
+            while (global_ns() - t0 < 200000ull) __nanosleep(1000);
+        }
         return;
     }
 
@@ -706,6 +788,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         // (deterministic), scaled, and stored; the buffer is handed back to the consumers. In layer mode, once all
         // of an op's tiles are stored the CTA counts itself in on the op's counter.
         grid_dependency_wait();                               // y is written only after the preceding grid is done
+        const unsigned int tp_e = p.tp_world > 0 ? tp_enter(p, lane) : 0u;
         int b = 0;
         uint32_t bph = 0;
         for (int jo = 0; jo < nops; ++jo) {
@@ -773,15 +856,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 }
             }
         }
-        if (p.tp_world > 0) {
-            // this CTA's outputs are on every rank: make them visible system-wide, then count the CTA in everywhere
-            __threadfence_system();
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_system();
-                for (int r = 0; r < p.tp_world; ++r) atomicAdd_system(p.tp_flag[r], 1u);
-            }
-        }
+        if (p.tp_world > 0) tp_leave(p, lane, tp_e);          // this CTA's outputs are on every rank
         if (p.nops > 0) consumer_barrier(2, (NC + 1) * 32);    // this CTA's consumers are past their last wait
         if (p.nops > 0 && lane == 0) {
             // the last CTA through every op zeroes the counters for the next launch (every CTA's consumers have
@@ -824,6 +899,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const int S = (op.nchunk + 3) >> 2;                   // 64-byte steps per row
         const int SF = op.nchunk >> 2;                        // steps whose four 16-byte chunks are all in the row
         const int Kp = tma_kx<F>(op.K);
+        const int xps = x_plane_stride<F, DEC>(Kp);           // byte planes of x (FP8 DEC 3, INT4 DEC 2)
         const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
         const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
         const int nst = ((re - rb + 15) >> 4) * NCH;
@@ -903,13 +979,13 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
 #pragma unroll 1                                      // a compact loop: instruction fetch stalls dominate INT4
                 for (; sl + U <= sfull; sl += U)
                     tma_steps<F, DEC, U, false>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                                op.nchunk, Kp + 16);
+                                                op.nchunk, xps);
                 for (; sl < sfull; ++sl)
                     tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                                op.nchunk, Kp + 16);
+                                                op.nchunk, xps);
                 for (; sl < sb0; ++sl)                        // the ragged last step of the row
                     tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                               op.nchunk, Kp + 16);
+                                               op.nchunk, xps);
             }
 
             if (last) {
@@ -936,13 +1012,17 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 } else {
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
-                        if constexpr (F == kFP8 && DEC == 3) {    // columns 0 (x hi) + 1 (x lo)
+                        if constexpr (F == kFP8 && DEC == 3) {    // lanes c = 0: columns 0 + 1 (tier 0); c = 1: 2 + 3
                             s0 += (A.a[u][0][0] + A.a[u][0][1]) + (A.a[u][1][0] + A.a[u][1][1]);
                             s1 += (A.a[u][0][2] + A.a[u][0][3]) + (A.a[u][1][2] + A.a[u][1][3]);
                         } else {
                             s0 += A.a[u][0][0] * f0 + A.a[u][1][0] * f1;
                             s1 += A.a[u][0][2] * f0 + A.a[u][1][2] * f1;
                         }
+                    }
+                    if constexpr (F == kFP8 && DEC == 3) {        // + 2^-16 tier 1 (exact scaling)
+                        s0 = fmaf(__shfl_down_sync(0xffffffffu, s0, 1), 1.52587890625e-05f, s0);
+                        s1 = fmaf(__shfl_down_sync(0xffffffffu, s1, 1), 1.52587890625e-05f, s1);
                     }
                     A.zero();
                 }

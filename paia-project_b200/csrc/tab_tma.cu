@@ -1,8 +1,9 @@
 // TMA-fed tensor-core kernel instances (gemv_tma.cuh). math 5 = default weight decode of the format, and for FP8
 // math 6 = ALU bit decode, math 7 = split cvt/ALU decode, math 8 = e4m3 weights straight into e4m3 mma against x
-// split into two e4m3 terms; for INT4 math 6 = f16 nibble decode (1024 + n / 1024 + 16 n), math 7 = u8 nibbles
-// against x as int8 digits in an integer MMA (exact group sums). Tuple knobs: W = consumer warps (plus one producer warp),
-// U = 64-byte steps per consumer iteration. The ring depth and the shared-memory share are launch options.
+// split into four e4m3 terms in two exponent tiers; for INT4 math 6 = f16 nibble decode (1024 + n / 1024 + 16 n),
+// math 7 = u8 nibbles against x as int8 digits in an integer MMA (exact group sums). Tuple knobs: W = consumer warps
+// (plus one producer warp), U = 64-byte steps per consumer iteration. The ring depth and the shared-memory share are
+// launch options.
 #include "gemv_launch.cuh"
 #include "gemv_tma.cuh"
 
@@ -32,7 +33,33 @@ static const Variant kBat[4] = {PB2_TMA_BAT(kBF16) PB2_TMA_BAT(kFP8) PB2_TMA_BAT
 #undef PB2_TMA_H
 #undef PB2_TMA
 
+// The TMA-fed kernel as public variants of every format's table (after the reference's tuple grid): R = 0 marks them
+// (no reference tuple has R = 0), U = steps per consumer iteration {2, 4}, W = consumer warps {4, 8, 16}, S = 0,
+// H = PDL {0, 1}; the format's default decode (BF16 5, FP8 8, INT4 / INT4A 7), the ring as deep as fits. A tuned
+// table (src/tuned/<platform>.json) can name them per shape through the unchanged op adapters.
+#define PB2_TP(F, NC, U, H, M, DEC) {0, U, NC, 0, H, M, &gemv_tma_kernel<F, NC, U, DEC>, nullptr, &tma_prep<F, NC, DEC>},
+#define PB2_TP_H(F, NC, U, M, DEC) PB2_TP(F, NC, U, 0, M, DEC) PB2_TP(F, NC, U, 1, M, DEC)
+#define PB2_TP_U(F, NC, M, DEC) PB2_TP_H(F, NC, 2, M, DEC) PB2_TP_H(F, NC, 4, M, DEC)
+#define PB2_TP_NC(F, M, DEC) PB2_TP_U(F, 4, M, DEC) PB2_TP_U(F, 8, M, DEC) PB2_TP_U(F, 16, M, DEC)
+static const Variant kPubBf16[] = {PB2_TP_NC(kBF16, 5, 0)};
+static const Variant kPubFp8[] = {PB2_TP_NC(kFP8, 8, 3)};
+static const Variant kPubInt4[] = {PB2_TP_NC(kINT4, 7, 2)};
+static const Variant kPubInt4a[] = {PB2_TP_NC(kINT4A, 7, 2)};
+#undef PB2_TP_NC
+#undef PB2_TP_U
+#undef PB2_TP_H
+#undef PB2_TP
+
 #define PB2_N(t) (int)(sizeof(t) / sizeof(t[0]))
+const Variant* tma_public(int fmt, int* n) {
+    switch (fmt) {
+        case kBF16: *n = PB2_N(kPubBf16); return kPubBf16;
+        case kFP8: *n = PB2_N(kPubFp8); return kPubFp8;
+        case kINT4: *n = PB2_N(kPubInt4); return kPubInt4;
+        case kINT4A: *n = PB2_N(kPubInt4a); return kPubInt4a;
+        default: *n = 0; return nullptr;
+    }
+}
 const Variant* tma_instances(int fmt, int math, int* n) {
     *n = 0;
     if (math == 9) {
@@ -68,8 +95,8 @@ const Variant* tma_instances(int fmt, int math, int* n) {
 #undef PB2_N
 
 // Error word of the bounded waits (1 producer gave up on a free stage, 2 consumer on a full stage, 3 epilogue on a
-// tile's partials, 4 consumer on a free partial buffer, 5 producer on the staged x, 7 consumer on the previous op of
-// a layer launch).
+// tile's partials, 4 consumer on a free partial buffer, 5 producer on the staged x, 6 tensor-parallel arrivals of
+// every rank's CTAs, 7 consumer on the previous op of a layer launch, 8 tensor-parallel start of the other ranks).
 int tma_device_error(int clear) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_tma_error, sizeof(int)) != cudaSuccess) { (void)cudaGetLastError(); return -1; }

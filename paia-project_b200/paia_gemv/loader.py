@@ -92,8 +92,6 @@ class GemvLib:
         lib.paia_gemv_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(P)]
         lib.paia_gemv_ipc_close.restype = I
         lib.paia_gemv_ipc_close.argtypes = [P]
-        lib.paia_gemv_tp_wait.restype = I
-        lib.paia_gemv_tp_wait.argtypes = [P, ctypes.c_uint, P]
         # --- B200 additions
         lib.paia_gemv_batched.restype = I
         lib.paia_gemv_batched.argtypes = [I, P, P, P, P, P, P, I, I, I, P]
@@ -176,8 +174,10 @@ class GemvLib:
     STATIC_SCRATCH_ELEMS = 16 << 20
 
     def int4_unfused_static(self, Wq_ptr, scales_ptr, x_ptr, y_ptr, N, K, stream=None):
-        """int4_unfused with the library's own 32 MiB scratch (no allocation per call). N * K must not exceed 16 Mi;
-        concurrent calls race on the shared scratch."""
+        """int4_unfused with the library's own 32 MiB scratch, for callers that cannot allocate device memory on the
+        call path (a memory pool that owns all of HBM, a host without a device allocator, a loop that must not
+        synchronise the device). N * K must not exceed 16 Mi; calls that overlap on the GPU race on the shared
+        scratch; the first call on a device should come before any stream capture."""
         if N * K > self.STATIC_SCRATCH_ELEMS:
             raise RuntimeError(f"paia_gemv_int4_unfused_static: N*K = {N * K} exceeds the static scratch of "
                                f"{self.STATIC_SCRATCH_ELEMS} elements; use int4_unfused with a caller scratch")
@@ -263,10 +263,6 @@ class GemvLib:
 
     def ipc_close(self, ptr):
         self._check(self._lib.paia_gemv_ipc_close(ptr), "paia_gemv_ipc_close")
-
-    def tp_wait(self, counters_ptr, per_call, stream=None):
-        self._check(self._lib.paia_gemv_tp_wait(counters_ptr, per_call & 0xFFFFFFFF, self._st(stream)),
-                    "paia_gemv_tp_wait")
 
     def batched(self, kind, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, M, N, K, stream=None):
         """Y[M, N] = X[M, K] . W^T (+ bias): M activation rows against one weight stream (x, y row-major bf16)."""

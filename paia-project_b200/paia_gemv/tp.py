@@ -5,10 +5,11 @@ with their scales / zeros / bias, and x is replicated. Two ways to assemble y [N
 
 * `ShardedGemv.fused(x)`: one kernel per rank (paia_gemv_tp) whose epilogue stores each output straight into every
   rank's y over NVLink (peer pointers: CUDA IPC handles of the library's own allocations, exchanged through
-  torch.distributed and mapped with paia_gemv_ipc_open), then counts its
-  CTAs in on every rank's arrival counter; `paia_gemv_tp_wait` advances this rank's call epoch (in device memory, so
-  a captured CUDA graph stays correct) and makes the stream wait (bounded) for all ranks' CTAs of this call.
-  Counters only grow: call e expects e * world * ctas arrivals.
+  torch.distributed and mapped with paia_gemv_ipc_open). The ranks count in each other's counter blocks the calls
+  they have started and the CTAs that have finished storing, per source rank; a CTA stores into a rank's y only once
+  that rank has started the same call, and CTA 0 waits until every rank's CTAs are done, so y is complete on this
+  rank when the launch ends (no second launch; the counts live in device memory, so captured CUDA graphs stay
+  correct). Counts only grow: after call e, every per-source arrival count is e * ctas.
 * `ShardedGemv.nccl(x)`: the baseline, the same kernel writing the local slice, then `all_gather_into_tensor`.
 
 `shard_rows` and `assemble` hold the partitioning rule shared by both and by the CPU tests. One process per GPU,
@@ -47,9 +48,20 @@ def _device_view(ptr, n, typestr, device):
     return torch.as_tensor(_CudaArray(ptr, n, typestr), device=device)
 
 
-def expected_arrivals(epoch, world, ctas):
-    """Arrival-counter value after `epoch` completed calls (uint32, wraps)."""
-    return (epoch * world * ctas) & 0xFFFFFFFF
+# Counter block of one rank (uint32 words; kTpEpoch / kTpArrive / kTpReady in the kernel): calls completed here,
+# CTAs of each source rank done storing here, calls each source rank has started.
+COUNTER_WORDS, EPOCH, ARRIVE, READY = 32, 0, 8, 16
+
+
+def expected_counts(epoch, world, ctas):
+    """A rank's counter block after `epoch` completed calls (uint32, wraps): the epoch, ctas * epoch arrivals from
+    every rank and epoch starts of every rank."""
+    blk = [0] * COUNTER_WORDS
+    blk[EPOCH] = epoch & 0xFFFFFFFF
+    for r in range(world):
+        blk[ARRIVE + r] = (epoch * ctas) & 0xFFFFFFFF
+        blk[READY + r] = epoch & 0xFFFFFFFF
+    return blk
 
 
 class TpBuffers:
@@ -64,10 +76,12 @@ class TpBuffers:
         self.lib, self.N, self.group = lib, N, group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
         self._y_mem = lib.tp_alloc(2 * N)
-        self._f_mem = lib.tp_alloc(8)
+        self._f_mem = lib.tp_alloc(4 * COUNTER_WORDS)
         self.y = _device_view(self._y_mem, N, "<i2", device).view(torch.bfloat16)
-        self.flag = _device_view(self._f_mem, 2, "<i4", device)
+        self.flag = _device_view(self._f_mem, COUNTER_WORDS, "<i4", device)
         torch.cuda.synchronize(device)
         mine = (lib.ipc_handle(self._y_mem), lib.ipc_handle(self._f_mem))
         gathered = [None] * self.world
@@ -87,6 +101,17 @@ class TpBuffers:
         self.y_ptrs = (P * self.world)(*y_ptrs)
         self.f_ptrs = (P * self.world)(*f_ptrs)
         dist.barrier(group=group)
+
+    def reset(self):
+        """Zero this rank's counters on every rank at once (collective): after a wait gave up (error 6 or 8) the counts
+        are out of step."""
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.flag.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
 
     def close(self):
         """Unmap the peers' buffers and free this rank's, once every rank is done with them."""
@@ -139,12 +164,12 @@ class ShardedGemv:
         return p(self.Wq), p(self.s), p(self.z), p(self.bias)
 
     def fused(self, x, stream=None):
-        """y on every rank through the peer-store epilogue; returns this rank's full y (valid once the stream
-        reaches the end of the wait)."""
+        """y on every rank through the peer-store epilogue; returns this rank's full y, complete in stream order once
+        the launch ends. The same buffer serves every call: the next call's peer stores wait until this rank has
+        started that call, so readers of y earlier in this rank's stream are safe."""
         W, s, z, b = self._ptrs()
         self.lib.tp(self.kind, W, s, z, x.data_ptr(), b, self.buf.y_ptrs, self.buf.f_ptrs, self.world, self.rank,
                     self.N_local, self.K, stream)
-        self.lib.tp_wait(self.flag.data_ptr(), self.world * self.ctas, stream)
         return self.y
 
     def local(self, x, y_local, stream=None):

@@ -12,7 +12,9 @@ for p in (str(PKG), str(ROOT / "oracle"), str(ROOT)):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-REFERENCE = Path(os.environ.get("PAIA_REFERENCE", "/root/reference"))
+# The reference checkout (pinning only): $PAIA_REFERENCE, else a directory named "reference" beside this repository;
+# tests that need it skip where it is absent (it never exists on the GPU boxes).
+REFERENCE = Path(os.environ["PAIA_REFERENCE"]) if os.environ.get("PAIA_REFERENCE") else ROOT.parent / "reference"
 
 
 def pytest_configure(config):

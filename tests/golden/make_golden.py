@@ -1,6 +1,7 @@
 """Generate the golden vectors in tests/golden/golden_v1.npz from the REFERENCE'S OWN CODE.
 
-Run where the read-only reference checkout exists (its location in $PAIA_REFERENCE, else the default in REF below):
+Run where the read-only reference checkout exists ($PAIA_REFERENCE, else a directory named "reference" beside this
+repository):
 
     python tests/golden/make_golden.py
 
@@ -25,7 +26,7 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
-REF = Path(os.environ.get("PAIA_REFERENCE", "/root/reference"))
+REF = Path(os.environ["PAIA_REFERENCE"]) if os.environ.get("PAIA_REFERENCE") else ROOT.parent / "reference"
 sys.path.insert(0, str(ROOT / "paia-project_b200"))
 sys.path.insert(0, str(REF / "paia-bench"))
 

@@ -36,25 +36,30 @@ def test_no_torch_dependency(lib_path):
 def test_loader_and_variant_tables(lib_path):
     from paia_gemv import loader
     lib = loader.GemvLib(lib_path)
-    assert lib.n_variants == 96 and len(lib.variants_fp8) == 36 and len(lib.variants_int4) == 48
+    # the reference's grids (96 / 36 / 48 tuples, ids as the reference numbers them), then 12 TMA-fed B200 variants
+    assert lib.n_variants == 96 + 12 and len(lib.variants_fp8) == 36 + 12 and len(lib.variants_int4) == 48 + 12
+    assert len(lib.variants_int4_asym) == 48 + 12
     tup = lambda v: (v["R"], v["U"], v["W"], v["S"], v["H"])
+    tma = {(0, U, W, 0, H) for U in (2, 4) for W in (4, 8, 16) for H in (0, 1)}
+    for table, n in ((lib.variants, 96), (lib.variants_fp8, 36), (lib.variants_int4, 48), (lib.variants_int4_asym, 48)):
+        assert {tup(v) for v in table[n:]} == tma and all(v["R"] > 0 for v in table[:n])
     # the tuples the reference's adapters look up by value (ours_bf16.py:22, ours_quant.py:19)
     assert (2, 4, 4, 0, 1) in {tup(v) for v in lib.variants}
     assert (2, 2, 4, 0, 1) in {tup(v) for v in lib.variants_fp8}
     assert (4, 2, 4, 0, 1) in {tup(v) for v in lib.variants_int4}
     # the whole tuple grid of the reference tables
-    assert {tup(v) for v in lib.variants} == {(R, U, W, S, H) for R in (1, 2, 4) for U in (1, 2, 4, 8)
-                                              for W in (4, 8) for S in (0, 1) for H in (0, 1)}
-    assert {tup(v) for v in lib.variants_fp8} == {(R, U, W, 0, H) for R in (1, 2, 4) for U in (1, 2, 4)
-                                                  for W in (4, 8) for H in (0, 1)}
-    assert {tup(v) for v in lib.variants_int4} == {(R, U, W, 0, H) for R in (1, 2, 4, 8) for U in (1, 2, 4)
-                                                   for W in (4, 8) for H in (0, 1)}
+    assert {tup(v) for v in lib.variants[:96]} == {(R, U, W, S, H) for R in (1, 2, 4) for U in (1, 2, 4, 8)
+                                                   for W in (4, 8) for S in (0, 1) for H in (0, 1)}
+    assert {tup(v) for v in lib.variants_fp8[:36]} == {(R, U, W, 0, H) for R in (1, 2, 4) for U in (1, 2, 4)
+                                                       for W in (4, 8) for H in (0, 1)}
+    assert {tup(v) for v in lib.variants_int4[:48]} == {(R, U, W, 0, H) for R in (1, 2, 4, 8) for U in (1, 2, 4)
+                                                        for W in (4, 8) for H in (0, 1)}
     ex = lib.variant_info_ex("int4", 0)
     assert ex["vec_bytes"] == 16 and ex["W"] in (4, 8)
     L = lib._lib
     I = ctypes.c_int
     vals = [I() for _ in range(5)]
-    assert L.paia_gemv_bf16_variant_info(96, *map(ctypes.byref, vals)) == -1
+    assert L.paia_gemv_bf16_variant_info(108, *map(ctypes.byref, vals)) == -1
     assert L.paia_gemv_bf16_variant_info(-1, *map(ctypes.byref, vals)) == -1
     assert "sm_100a" in lib.version
 
@@ -67,7 +72,7 @@ def test_argument_contract_without_gpu(lib_path):
     for fn in ("paia_gemv_bf16",):
         f = getattr(L, fn)
         f.argtypes = [P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
-        assert f(a16, a16, a16, 4, 16, 96, None) == -1          # variant out of range
+        assert f(a16, a16, a16, 4, 16, 108, None) == -1         # variant out of range
         assert f(a16, a16, a16, 4, 16, -1, None) == -1
         assert f(a16, a16, a16, 4, 12, 0, None) == -2           # K % 8
         assert f(a16, a16, a16, 0, 16, 0, None) == -2           # N <= 0
@@ -77,13 +82,13 @@ def test_argument_contract_without_gpu(lib_path):
         assert f(a16, a16, a8, 4, 16, 0, None) == -2            # y
     f = L.paia_gemv_fp8
     f.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
-    assert f(a16, a16, a16, a16, 4, 16, 36, None) == -1
+    assert f(a16, a16, a16, a16, 4, 16, 48, None) == -1
     assert f(a16, a16, a16, a16, 4, 24, 0, None) == -2          # K % 16
     assert f(a16, a2, a16, a16, 4, 16, 0, None) == -2           # scale 4-byte alignment
     assert f(a16, a16, a16, P(0x10001), 4, 16, 0, None) == -2   # y 2-byte alignment
     f = L.paia_gemv_int4
     f.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
-    assert f(a16, a16, a16, a16, 4, 128, 48, None) == -1
+    assert f(a16, a16, a16, a16, 4, 128, 60, None) == -1
     assert f(a16, a16, a16, a16, 4, 192, 0, None) == -2         # K % 128
     assert f(a16, P(0x10001), a16, a16, 4, 128, 0, None) == -2  # scales 2-byte alignment
     f = L.paia_gemv_int4_naive
@@ -95,7 +100,7 @@ def test_argument_contract_without_gpu(lib_path):
     f = L.paia_gemv_int4_asym
     f.argtypes = [P, P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
     assert f(a16, a16, P(0x10001), a16, a16, 4, 128, 0, None) == -2   # zeros 2-byte alignment
-    assert f(a16, a16, a16, a16, a16, 4, 128, 48, None) == -1
+    assert f(a16, a16, a16, a16, a16, 4, 128, 60, None) == -1
     f = L.paia_gemv_bf16_bias
     f.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
     assert f(a16, a16, P(0x10001), a16, 4, 16, 0, None) == -2   # bias 2-byte alignment
@@ -106,7 +111,8 @@ def test_argument_contract_without_gpu(lib_path):
 
 
 def _reference_loader():
-    ref = Path(os.environ.get("PAIA_REFERENCE", "/root/reference")) / "src" / "paia_gemv" / "loader.py"
+    from conftest import REFERENCE
+    ref = REFERENCE / "src" / "paia_gemv" / "loader.py"
     if not ref.exists():
         pytest.skip("reference checkout not present")
     spec = importlib.util.spec_from_file_location("ref_loader", ref)
@@ -121,7 +127,7 @@ def test_reference_loader_loads_this_library(lib_path, monkeypatch):
     mod = _reference_loader()
     monkeypatch.setenv("PAIA_GEMV_LIB", lib_path)
     lib = mod.GemvLib()
-    assert lib.path == lib_path and lib.n_variants == 96
+    assert lib.path == lib_path and lib.n_variants == 96 + 12
     want = {"R": 2, "U": 4, "W": 4, "S": 0, "H": 1}
     assert any(all(v[k] == want[k] for k in "RUWSH") for v in lib.variants)
     with pytest.raises(RuntimeError):

@@ -380,7 +380,7 @@ TMA_CFGS = [(2, 2, 4, 1), (3, 4, 8, 1), (0, 2, 8, 2), (0, 4, 4, 1), (16, 2, 8, 1
 def tma_fits(kind, math, NC, N, K, ring, share):
     """Whether the TMA kernel can stage this shape (the CPU mirror of its shared-memory plan); else the C ABI
     returns -2."""
-    dec = 2 if (kind.startswith("int4") and math == 7) else 0
+    dec = 2 if (kind.startswith("int4") and math == 7) else (3 if (kind == "fp8" and math == 8) else 0)
     return tma_prep(kind, NC, K, ring, share_cap(share), dec) is not None
 
 

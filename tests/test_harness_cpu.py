@@ -11,8 +11,8 @@ import pytest
 
 
 def _bench_root():
-    for cand in (os.environ.get("PAIA_BENCH"),
-                 os.path.join(os.environ.get("PAIA_REFERENCE", "/root/reference"), "paia-bench")):
+    from conftest import REFERENCE
+    for cand in (os.environ.get("PAIA_BENCH"), str(REFERENCE / "paia-bench")):
         if cand and (Path(cand) / "bench" / "run.py").exists():
             return cand
     return None

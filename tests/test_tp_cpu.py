@@ -31,15 +31,17 @@ def test_shard_rows_cover_every_row_once():
         tp.shard_rows(1024, 2, 2)
 
 
-def test_expected_arrivals_wrap():
-    assert tp.expected_arrivals(1, 8, 148) == 8 * 148
-    e = 2 ** 32 // (8 * 148) + 3                       # past the uint32 wrap
-    v = tp.expected_arrivals(e, 8, 148)
-    assert v == (e * 8 * 148) % 2 ** 32
-    # the device wait compares wrap-safely: (int32)(counter - expected) >= 0
-    prev = tp.expected_arrivals(e - 1, 8, 148)
-    assert np.int32(np.uint32(v) - np.uint32(prev)) == 8 * 148
-
+def test_expected_counts_wrap():
+    """Per-source counts after e calls: e starts and e * ctas arrivals from every rank, uint32 wrapping; the device
+    waits compare wrap-safely ((int32)(count - target) >= 0), so one call's step stays positive past the wrap."""
+    blk = tp.expected_counts(1, 8, 148)
+    assert blk[tp.EPOCH] == 1 and blk[tp.ARRIVE:tp.ARRIVE + 8] == [148] * 8 and blk[tp.READY:tp.READY + 8] == [1] * 8
+    assert len(blk) == tp.COUNTER_WORDS and tp.ARRIVE + 8 <= tp.READY and tp.READY + 8 <= tp.COUNTER_WORDS
+    e = 2 ** 32 // 148 + 3                              # past the uint32 wrap of the arrival counts
+    v = tp.expected_counts(e, 8, 148)[tp.ARRIVE]
+    assert v == (e * 148) % 2 ** 32
+    prev = tp.expected_counts(e - 1, 8, 148)[tp.ARRIVE]
+    assert np.int32(np.uint32(v) - np.uint32(prev)) == 148
 
 def _free_port():
     s = socket.socket()

@@ -1,7 +1,9 @@
 """Row-sharded tensor parallelism on the GPU. One GPU: the TP kernel at world 1 equals the same TMA instance bit for
-bit and counts its CTAs in; the bounded arrival wait gives up with an error status (a counter nothing increments)
-and leaves the context usable. Two or more GPUs (skipped otherwise): two NCCL ranks, fused peer-store path and
-NCCL all-gather baseline, both equal to the oracle and to each other bit for bit."""
+bit and leaves its counter block at the expected counts call after call; the bounded waits give up with an error
+status (a rank that never starts, a rank whose CTAs never arrive: counters nothing increments) within ~1 s each and
+leave the context usable. Two or more GPUs (skipped otherwise): two NCCL ranks, fused peer-store path and NCCL
+all-gather baseline, both equal to the oracle and to each other bit for bit, also with one rank running behind the
+other on every call (the next call's peer stores never overwrite a y its rank is still reading)."""
 import ctypes
 import os
 import socket
@@ -37,31 +39,48 @@ def test_tp_world1_matches_tma_instance(L, kind):
     L.launch_ex(kind, 0, 2, 8, TMA_MATH[kind], 1, 0, 0, _ptr(ops.W), _ptr(ops.s), _ptr(ops.z), _ptr(ops.x),
                 _ptr(ops.bias), ref.data_ptr(), N, K)
     y = torch.full((N,), float("nan"), dtype=torch.bfloat16, device="cuda")
-    flag = torch.zeros(2, dtype=torch.int32, device="cuda")
+    from paia_gemv import tp
+    flag = torch.zeros(tp.COUNTER_WORDS, dtype=torch.int32, device="cuda")
     P = ctypes.c_void_p
-    L.tp(kind, _ptr(ops.W), _ptr(ops.s), _ptr(ops.z), _ptr(ops.x), _ptr(ops.bias), (P * 1)(y.data_ptr()),
-         (P * 1)(flag.data_ptr()), 1, 0, N, K)
     ctas = L.tp_ctas(kind, N, K)
-    L.tp_wait(flag.data_ptr(), ctas)
-    torch.cuda.synchronize()
-    assert L.device_error(1) == 0
-    assert flag.tolist() == [ctas, 1]
-    assert np.array_equal(bits(y), bits(ref))
+    for call in (1, 2):
+        y.fill_(float("nan"))
+        L.tp(kind, _ptr(ops.W), _ptr(ops.s), _ptr(ops.z), _ptr(ops.x), _ptr(ops.bias), (P * 1)(y.data_ptr()),
+             (P * 1)(flag.data_ptr()), 1, 0, N, K)
+        torch.cuda.synchronize()
+        assert L.device_error(1) == 0
+        assert flag.tolist() == tp.expected_counts(call, 1, ctas), call
+        assert np.array_equal(bits(y), bits(ref))
     check(ops, bits(y), ops.oracle(with_bias=True)[0], f"tp world 1 {kind}")
 
 
-def test_tp_wait_gives_up_with_an_error_status(L):
-    """A counter that nothing increments: the wait kernel returns after ~1 s, reports code 6, and the GPU keeps
-    working (a GEMV right after it is still correct)."""
+@pytest.mark.parametrize("missing", ["start", "arrivals"])
+def test_tp_waits_give_up_with_an_error_status(L, missing):
+    """World 2 on one GPU with both counter blocks local and no second rank: nothing ever counts rank 1 in. With its
+    start count missing every CTA's start wait gives up (code 8); with the start count preset, CTA 0's arrival wait
+    gives up (code 6). Either way the launch returns within a few seconds (once one wait has given up the others stop
+    at once), and a GEMV right after it is still correct."""
+    import time
+    from paia_gemv import tp
+    N, K = 1000, 1024
+    ops = make("fp8", N, K, seed=2)
     L.device_error(1)
-    flag = torch.zeros(2, dtype=torch.int32, device="cuda")
-    L.tp_wait(flag.data_ptr(), 1)
+    ys = [torch.zeros(2 * N, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    blks = [torch.zeros(tp.COUNTER_WORDS, dtype=torch.int32, device="cuda") for _ in range(2)]
+    if missing == "arrivals":
+        blks[0][tp.READY + 1] = 1000                       # rank 1 "has started": only its arrivals are missing
+    P = ctypes.c_void_p
+    t0 = time.perf_counter()
+    L.tp("fp8", _ptr(ops.W), _ptr(ops.s), None, _ptr(ops.x), None, (P * 2)(ys[0].data_ptr(), ys[1].data_ptr()),
+         (P * 2)(blks[0].data_ptr(), blks[1].data_ptr()), 2, 0, N, K)
     torch.cuda.synchronize()
-    assert L.device_error(1) == 6
-    ops = make("fp8", 300, 1024, seed=2)
+    dt = time.perf_counter() - t0
+    assert L.device_error(1) == (8 if missing == "start" else 6)
+    assert 0.9 < dt < 6.0, dt
     ops.nan_fill()
     ops.call(L, 0)
     torch.cuda.synchronize()
+    assert L.device_error(1) == 0
     check(ops, bits(ops.y), ops.oracle()[0], "fp8 after a timed-out wait")
 
 
@@ -97,6 +116,19 @@ def _two_rank_worker(rank, world, port, kind, result):
     if ok and rank == 0:
         rel = O.rel_l2(bits(y_f), full.oracle()[0])     # bf16 bits against bf16 bits
         ok = rel <= 1e-3
+    if ok:
+        # skewed ranks: rank 1 runs ~50 us behind on every call, alternating two activations; each rank copies y
+        # right after each call (in stream order), and every copy must be that call's result, not the next one's
+        x2 = (full.x.float() * -0.5).to(torch.bfloat16)
+        want = [bits(y_f), bits(g.nccl(x2).clone())]
+        outs = []
+        for i in range(40):
+            if rank == 1:
+                torch.cuda._sleep(100000)
+            outs.append(g.fused(full.x if i % 2 == 0 else x2).clone())
+        torch.cuda.synchronize()
+        err = L.device_error(1)
+        ok = err == 0 and all(np.array_equal(bits(o), want[i % 2]) for i, o in enumerate(outs))
     g.close()
     dist.destroy_process_group()
     result.put((rank, bool(ok), err, rel))
