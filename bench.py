@@ -371,7 +371,7 @@ class HeadlineOp:
     """One op of the headline step on this rank: its row shard in `n` L2-rotation copies (copy 0 holds quantised
     weights of this rank's rows, the others valid random codes of the format), and on > 1 GPU the TP objects."""
 
-    def __init__(self, lib, kind, name, world, rank, n, g, bufs=None):
+    def __init__(self, lib, kind, name, world, rank, n, g, bufs=None, exchange=None):
         import torch
         from paia_gemv import tp
         self.kind, self.name = kind, name
@@ -383,20 +383,25 @@ class HeadlineOp:
         self.copies = [Gemv(lib, kind, self.nl, self.K, g, name, variant=vid, random_codes=(c > 0)) for c in range(n)]
         self.ys = [torch.empty(self.nl, dtype=torch.bfloat16, device="cuda") for _ in range(n)]
         self.sg = None
+        self.exchange = exchange
         if world > 1:
             self.sg = [tp.ShardedGemv(lib, kind, c.W, c.s, c.z, None, self.N, self.K, buffers=bufs) for c in self.copies]
 
     def shard_bytes(self):
         return self.copies[0].weight_bytes()
 
-    def launcher(self, c, x):
-        """Zero-argument launch of copy c: the default-path GEMV (1 GPU) or the fused TP call."""
+    def launcher(self, c, x, deferred=False):
+        """Zero-argument launch of copy c: the default-path GEMV (1 GPU), or the TP call: complete (y whole on every
+        rank when it ends) or deferred (y whole after the step's exchange)."""
         if self.sg is None:
             return self.copies[c].launcher(x, self.ys[c])
-        sg = self.sg[c]
+        sg, ex = self.sg[c], self.exchange
 
         def call():
-            sg.fused(x)                    # raises on a nonzero return code
+            if deferred:
+                sg.deferred(x)             # raises on a nonzero return code
+            else:
+                sg.fused(x)
             return 0
         return call
 
@@ -404,11 +409,12 @@ class HeadlineOp:
         return self.ys[c] if self.sg is None else self.sg[c].y
 
     def api_call(self, c, x, stream=None):
-        """The public API call a user makes for copy c (GemvLib method, or ShardedGemv.fused)."""
+        """The public API call a user makes for copy c (GemvLib method, or ShardedGemv.deferred; the step's
+        exchange completes the outputs)."""
         if self.sg is None:
             self.copies[c].api_call(x, self.ys[c], stream)
             return self.ys[c]
-        return self.sg[c].fused(x, stream)
+        return self.sg[c].deferred(x, stream)
 
 
 def torch_reference(gm, x):
@@ -445,8 +451,16 @@ def check_headline(ops, x, world):
         if world > 1:
             yf = y.clone()
             yn = op.sg[0].nccl(x).clone()
+            y.zero_()
             torch.cuda.synchronize()
-            same = same and bool(torch.equal(yf.view(torch.int16), yn.view(torch.int16)))
+            import torch.distributed as dist
+            dist.barrier()
+            op.launcher(0, x, deferred=True)()
+            op.exchange.run()
+            torch.cuda.synchronize()
+            yd = y.clone()
+            same = (same and bool(torch.equal(yf.view(torch.int16), yn.view(torch.int16)))
+                    and bool(torch.equal(yf.view(torch.int16), yd.view(torch.int16))))
     return worst, same
 
 
@@ -619,13 +633,13 @@ def run_main(args, rank, world, local_rank):
     # per-rank bytes of one step (this rank's shards), and L2 rotation over n copies of every shard
     step_shard = sum(format_bytes(k, synthetic_shape(n)[0] // world, synthetic_shape(n)[1]) for k, n in HEADLINE)
     n = timing.plan_rotation(step_shard, l2)
-    bufs = {}
+    # > 1 GPU: every op its own output buffers (a deferred call per buffer set between two exchanges), one exchange
+    bufs, exchange = [], None
     if world > 1:
-        for _, name in HEADLINE:
-            N = synthetic_shape(name)[0]
-            if N not in bufs:
-                bufs[N] = tp.TpBuffers(lib, N, torch.device("cuda", local_rank))
-    ops = [HeadlineOp(lib, kind, name, world, rank, n, g, bufs.get(synthetic_shape(name)[0])) for kind, name in HEADLINE]
+        exchange = tp.TpExchange(lib, torch.device("cuda", local_rank))
+        bufs = [tp.TpBuffers(lib, synthetic_shape(name)[0], torch.device("cuda", local_rank)) for _, name in HEADLINE]
+    ops = [HeadlineOp(lib, kind, name, world, rank, n, g, bufs[i] if bufs else None, exchange)
+           for i, (kind, name) in enumerate(HEADLINE)]
     gx = torch.Generator(device="cuda").manual_seed(7)                # x is the same on every rank
     x = torch.randn(ops[0].K, device="cuda", generator=gx).to(torch.bfloat16)
     check_err, same = check_headline(ops, x, world)
@@ -635,7 +649,11 @@ def run_main(args, rank, world, local_rank):
                            f"fused == NCCL on this rank: {same}")
     lib.device_error(1)
 
-    steps_calls = [[op.launcher(c, x) for op in ops] for c in range(n)]
+    def exchange_call():
+        exchange.run()
+        return 0
+    steps_calls = [[op.launcher(c, x, deferred=world > 1) for op in ops] + ([exchange_call] if world > 1 else [])
+                   for c in range(n)]
 
     def run_steps(k):
         for i in range(k):
@@ -680,7 +698,7 @@ def run_main(args, rank, world, local_rank):
     del g_round, tails
     total_bytes = headline_bytes() * args.steps
     value = total_bytes / (ms_max * 1e-3) / 1e9
-    launches = len(HEADLINE) * args.steps * world
+    launches = (len(HEADLINE) + (1 if world > 1 else 0)) * args.steps * world
 
     # per-op device time inside the same kind of graph (every rank the same launches), max over ranks
     reps = max(n, (32 // n) * n)
@@ -724,8 +742,10 @@ def run_main(args, rank, world, local_rank):
     def e2e_step(i):
         c = i % n
         x_dev[c].copy_(x_host, non_blocking=True)
-        for op, yh in zip(ops, y_host):
-            y = op.api_call(c, x_dev[c])
+        ys = [op.api_call(c, x_dev[c]) for op in ops]
+        if exchange is not None:
+            exchange.run()
+        for y, yh in zip(ys, y_host):
             yh.copy_(y, non_blocking=True)
 
     for i in range(max(3, args.warmup // 10)):
@@ -781,9 +801,10 @@ def run_main(args, rank, world, local_rank):
                        "l2": f"inputs larger than L2: each rank rotates over {n} copies of its shards = "
                              f"{n * step_shard / 2**20:.0f} MiB >= 4 x L2 ({l2 / 2**20:.0f} MiB)",
                        "launch": ("CUDA graph of back-to-back launches with programmatic dependent launch"
-                                  + ("; each op one fused TMA kernel per rank: peer stores of every output into "
-                                     "every rank's y over NVLink, per-source start / arrival counts, CTA 0 waits "
-                                     "for all ranks" if world > 1 else "")),
+                                  + ("; each op one TMA kernel per rank storing its outputs into every rank's y over "
+                                     "NVLink (deferred form, after a per-buffer start handshake), then one exchange "
+                                     "kernel per step (system fence, per-rank counts, bounded wait) after which "
+                                     "every op's full y is complete on every rank" if world > 1 else "")),
                        "parallelism": f"row-sharded tensor parallel x{world}" if world > 1 else "1 GPU"},
             "per_op_us": {k: round(v, 3) for k, v in per_op.items()},
             "us_per_step": round(ms_max * 1e3 / args.steps, 3),
@@ -798,9 +819,10 @@ def run_main(args, rank, world, local_rank):
                                    f"graph of rotated launches{', including the exchange' if world > 1 else ''})"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 2,
                     "d2h_bytes_per_step": sum(op.N * 2 for op in ops), "steps": e2e_steps,
-                    "how": "public API (paia_gemv.loader GemvLib methods; tp.ShardedGemv.fused on > 1 GPU), eager "
-                           "launches; per step a pinned H2D of x, the four ops, a pinned D2H of every op's full y, "
-                           "all in order on one stream; CUDA events around all steps, max over ranks"},
+                    "how": "public API (paia_gemv.loader GemvLib methods; on > 1 GPU tp.ShardedGemv.deferred and "
+                           "TpExchange.run), eager launches; per step a pinned H2D of x, the four ops, a pinned D2H of "
+                           "every op's full y, all in order on one stream; CUDA events around all steps, max over "
+                           "ranks"},
             "gpu_launches": launches,
             "clocks": clocks,
             "check_rel_l2_vs_torch": round(bad[1], 7),
@@ -815,8 +837,9 @@ def run_main(args, rank, world, local_rank):
         dist.barrier()
         for op in ops:
             op.sg = None
-        for b in bufs.values():
+        for b in bufs:
             b.close()
+        exchange.close()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)

@@ -89,6 +89,19 @@ int paia_gemv_tp(int kind, const void* Wq, const void* scales, const void* zeros
                  void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
                  void* stream);
 int paia_gemv_tp_ctas(int kind, int N_local, int K);
+/* Deferred form, for sequences of TP GEMVs: the kernel only stores its outputs into every rank's y (after the same start
+ * handshake), with no arrival counts and no wait, and y is complete only after the next paia_gemv_tp_exchange on every
+ * rank (its CTAs count themselves in on word 4 of this rank's block once they have read the call count, error 9 if
+ * they do not within ~1 s). Between two exchanges each buffer set (y_all, flag_all) takes at most one call: a second
+ * would overwrite y before it is published. paia_gemv_tp_exchange
+ * (one small kernel, launched in stream order after the calls it publishes): a system-scope fence makes every store of
+ * this rank's earlier kernels visible, the rank counts itself in on every rank's exchange block (xflag_all[r]), and it
+ * waits (bounded, ~1 s, error 6) until every rank has done the same; after it, every y written by deferred calls
+ * before it is complete on this rank. */
+int paia_gemv_tp_deferred(int kind, const void* Wq, const void* scales, const void* zeros, const void* x,
+                          const void* bias, void* const* y_all, unsigned int* const* flag_all, int world, int rank,
+                          int N_local, int K, void* stream);
+int paia_gemv_tp_exchange(unsigned int* const* xflag_all, int world, int rank, void* stream);
 /* Setup of the buffers other ranks map: a zero-filled device allocation (cudaMalloc), its 64-byte CUDA IPC handle,
  * and the mapping of a peer's handle in this process (usable from kernels on the current device; peer access is
  * enabled lazily). Codes: 0, -2 bad argument, >0 cudaError_t. Not for use inside a captured stream. */
@@ -131,7 +144,10 @@ int paia_gemv_variant_info_ex(int kind, int v, paia_gemv_variant_ex* out);
 
 /* Tuning entry point (the B200 analogue of the variant sweep of src/tools/dev_sweep_bf16.py): launch any compiled
  * kernel instance (R, U, W, math) of `kind` with explicit PDL (0/1), warps per row ks (0 = auto) and CTAs per SM
- * (0 = auto). s/z/bias as in the per-format entry points (unused ones may be NULL). -1 if no such instance exists. */
+ * (0 = auto). TMA-fed instances (math >= 5): R = ring stages (<= 1: as many as fit) and ks = shared-memory share
+ * (bits 0-7) | stages streamed before x is staged (bits 8-15) | full tiles as one tiled tensor copy per stage
+ * instead of per-row bulk copies (bit 16; slower on every decode shape measured, kept for comparison).
+ * s/z/bias as in the per-format entry points (unused ones may be NULL). -1 if no such instance exists. */
 int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks, int ctas_per_sm, const void* Wq,
                         const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
                         void* stream);

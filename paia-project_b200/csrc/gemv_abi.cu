@@ -85,6 +85,41 @@ int max_ctas_per_sm(KernelFn fn, int threads, size_t smem) {
     return n;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+    static const EncodeTiledFn fn = []() -> EncodeTiledFn {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<EncodeTiledFn>(f);
+    }();
+    return fn;
+}
+
+// W [N][rb bytes] as a 3-D uint8 tensor (64 bytes, rb / 64 pieces 64 bytes apart, N rows rb bytes apart) with a box of
+// 64 x rs / 64 x 16: one copy lands 16 rows of a stage at row stride rs, x coordinate always 0. A piece past the
+// row end reads zeros (out of bounds). 0 when the shape does not qualify or the driver refuses the map.
+int encode_weight_map(Params& p) {
+    const EncodeTiledFn fn = encode_tiled();
+    const uint64_t rb = (uint64_t)p.nchunk * 16;
+    if (!fn || p.N < 16 || rb % 64 || p.rs % 64 || p.rs / 64 > 256 || ((uintptr_t)p.W & 15)) return 0;
+    const cuuint64_t dims[3] = {64, rb / 64, (cuuint64_t)p.N};
+    const cuuint64_t strides[2] = {64, rb};
+    const cuuint32_t box[3] = {64, (cuuint32_t)(p.rs / 64), 16};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = fn(&p.tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(p.W), dims, strides, box,
+                          es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 1 : 0;
+}
+
 const Variant* find_instance(int fmt, int R, int U, int W, int math) {
     int n = 0;
     if (math >= 5) {                        // TMA-fed: R is the ring depth, a launch option
@@ -434,9 +469,10 @@ int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void
 
 // ------------------------------------------------------------------ row-sharded tensor parallelism
 
-int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const void* x, const void* bias,
-                 void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
-                 void* stream) {
+namespace {
+int tp_launch(int kind, const void* Wq, const void* s, const void* z, const void* x, const void* bias,
+              void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
+              bool defer, void* stream) {
     if (kind < 0 || kind > 3 || world < 1 || world > 8 || rank < 0 || rank >= world || !y_all || !flag_all) return -2;
     for (int r = 0; r < world; ++r)
         if (!y_all[r] || !flag_all[r] || !aligned(y_all[r], 2) || !aligned(flag_all[r], 16)) return -2;
@@ -456,6 +492,7 @@ int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const v
     p.tp_world = world;
     p.tp_rank = rank;
     p.tp_off = rank * N_local;
+    p.tp_defer = defer ? 1 : 0;
     for (int r = 0; r < world; ++r) {
         p.tp_y[r] = static_cast<__nv_bfloat16*>(y_all[r]);
         p.tp_flag[r] = flag_all[r];
@@ -464,6 +501,26 @@ int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const v
     if (!pb2tp::tp_instance(kind, p, &v)) return -2;
     const LaunchOpts o{0, 0};
     return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+int paia_gemv_tp(int kind, const void* Wq, const void* s, const void* z, const void* x, const void* bias,
+                 void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
+                 void* stream) {
+    return tp_launch(kind, Wq, s, z, x, bias, y_all, flag_all, world, rank, N_local, K, false, stream);
+}
+
+int paia_gemv_tp_deferred(int kind, const void* Wq, const void* s, const void* z, const void* x, const void* bias,
+                          void* const* y_all, unsigned int* const* flag_all, int world, int rank, int N_local, int K,
+                          void* stream) {
+    return tp_launch(kind, Wq, s, z, x, bias, y_all, flag_all, world, rank, N_local, K, true, stream);
+}
+
+int paia_gemv_tp_exchange(unsigned int* const* xflag_all, int world, int rank, void* stream) {
+    if (world < 1 || world > 8 || rank < 0 || rank >= world || !xflag_all) return -2;
+    for (int r = 0; r < world; ++r)
+        if (!xflag_all[r] || !aligned(xflag_all[r], 16)) return -2;
+    return launch_tp_exchange(xflag_all, world, rank, static_cast<cudaStream_t>(stream));
 }
 
 // Buffers that other ranks map (full-size y and the arrival counters): plain device allocations, so that their
@@ -716,9 +773,10 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
     p.groups = K / 128;
     LaunchOpts o{ks, ctas_per_sm};
     if (math >= 5) {                        // TMA-fed kernels: R = ring stages (<= 1: auto), ks = shared-memory share
-        o.ring = R <= 1 ? 0 : R;            // (low byte) and stages streamed before x is staged (ks >> 8, 0 = all)
-        o.share = ks & 0xFF;
-        o.pre = ks >> 8;
+        o.ring = R <= 1 ? 0 : R;            // (bits 0-7), stages streamed before x is staged (bits 8-15, 0 = all),
+        o.share = ks & 0xFF;                // tiled tensor copies of full tiles (bit 16)
+        o.pre = (ks >> 8) & 0xFF;
+        o.tensor_on = (ks >> 16) & 1;
         o.ks = 0;
     }
     return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));

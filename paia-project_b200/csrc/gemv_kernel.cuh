@@ -35,6 +35,7 @@
 // Requirements (checked by the C ABI): rows are 16-byte multiples (K % 8 bf16, K % 16 fp8, K % 128 int4), W and x
 // 16-byte aligned, K small enough for x to fit in shared memory (K <= 98304).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -61,7 +62,7 @@ struct GemvOp {
 };
 constexpr int kMaxOps = 6;             // ops carried in the kernel parameters
 // Tensor-parallel counter block of one rank (uint32 words): epoch, then per-source arrival and ready counts.
-constexpr int kTpEpoch = 0, kTpArrive = 8, kTpReady = 16, kTpCounterWords = 32;
+constexpr int kTpEpoch = 0, kTpReaders = 4, kTpArrive = 8, kTpReady = 16, kTpCounterWords = 32;
 constexpr int kMaxPlanOps = 4096;       // ops of a plan (device-memory op table)
 
 struct Params {
@@ -83,13 +84,23 @@ struct Params {
     int mr;                        // TMA kernels: halves per row of a stage's metadata slot
     int ring;                      // TMA kernels: stages in the shared-memory ring
     int pre;                       // TMA kernels: stages streamed before x is staged (0 = the whole ring)
+    // TMA kernels, single GEMV, on request (tensor_on; measured slower than the per-row bulk copies on every decode
+    // shape, so off by default): W as a 3-D tiled tensor (64 bytes x 64-byte pieces of a row x rows) whose 16-row box
+    // lands a whole stage of a full tile in one copy, in the same layout as the per-row copies (row r at r * rs).
+    // tmap_ok: the map was encoded (else per-row copies). tlayout: the stage layout is the one the tensor copy lands
+    // (no blocked 8-row layout), whichever copies fill it.
+    int tensor_on, tlayout, tmap_ok;
+    CUtensorMap tmap_w;
     // Row-sharded tensor parallelism (TMA kernels; tp_world = 0: off). Rank tp_rank computes rows [0, N) of its shard
     // and stores each output to every rank's full-size y (peer memory over NVLink) at tp_off + row. tp_flag[r] is
     // rank r's counter block (kTpCounterWords uint32): [kTpEpoch] calls completed on r, [kTpArrive + s] CTAs of rank
     // s that finished their stores into r, [kTpReady + s] calls rank s has started (its readers of the previous y are
     // done). CTA 0 of each launch waits for every rank's CTAs before the grid ends, so y is complete when the kernel
     // is; no rank stores into a peer's y before that peer has started the same call.
-    int tp_world, tp_off, tp_rank;
+    // tp_defer: the deferred form - the kernel only stores (after the start handshake); paia_gemv_tp_exchange publishes
+    // and waits later. Every CTA counts itself in on [kTpReaders] once it has read the epoch, and in this form CTA 0
+    // advances the epoch only after all of them have.
+    int tp_world, tp_off, tp_rank, tp_defer;
     __nv_bfloat16* tp_y[8];
     unsigned int* tp_flag[8];
     // Layer mode (TMA kernels; nops = 0: off, the single GEMV above). One persistent cooperative launch runs ops

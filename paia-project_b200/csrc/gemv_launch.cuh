@@ -32,6 +32,7 @@ struct LaunchOpts {
     int share = 0;            // TMA kernels: size the CTA for 1/share of the SM's shared memory (0 = 1: all of it);
                               // share 2 with one CTA per SM leaves room for the next kernel's CTA under PDL
     int pre = 0;              // TMA kernels: stages streamed before x is staged (0 = the whole ring)
+    int tensor_on = 0;        // TMA kernels: 1 = tiled tensor copies of full tiles (comparisons; slower, off by default)
 };
 
 int sm_count();                                              // current device, cached
@@ -77,6 +78,7 @@ inline int plan_variant(const Variant& v, const Params& p_in, const LaunchOpts& 
         if (cap > max_dyn_smem()) cap = max_dyn_smem();
         p.ring = o.ring;
         p.pre = o.pre;
+        p.tensor_on = o.tensor_on;
         smem = v.prep(p, cap);
     } else {
         smem = v.smem(p.K);
@@ -159,5 +161,6 @@ const Variant* mma_instances(int fmt, int math, int* n);
 const Variant* tma_instances(int fmt, int math, int* n);
 const Variant* tma_public(int fmt, int* n);                  // the TMA variants appended to each format's table
 int tma_device_error(int clear);
+int launch_tp_exchange(unsigned int* const* flag_all, int world, int rank, cudaStream_t st);
 
 }  // namespace pb2

@@ -340,15 +340,13 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
             reinterpret_cast<uint4*>(xs)[i] = o;
         }, xc, map);
     } else if constexpr (DEC == 2) {
-        // INT4 for the integer MMA: v = x * 2^s rounded to an integer of magnitude <= 2^27 (exact for every element
-        // within 2^19 of max|x|, bf16 carrying 8 significant bits, so an outlier channel of an LLM activation leaves
-        // the ordinary elements exact; smaller ones keep an error below 2^-28 max|x|), split into four signed base-128
-        // digits d0 + 128 d1 + 128^2 d2 + 128^3 d3, each an int8 plane of Kpad bytes at xs + d (Kpad + 16) with every
-        // 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low nibbles).
-        // Per 128-group g: the digit sums S_d (int) at gsum[8g + d], sum(v) (float) at gsum[8g + 4], and the
-        // symmetric offsets 8 (S_0 + 128 S_1) and 8 128^2 (S_2 + 128 S_3) (floats, exact) at gsum[8g + 5] and
-        // gsum[8g + 6].
-        // xscale[1] = 2^-s (NaN when x holds a NaN or an infinity, which then reaches every output).
+        // INT4 for the integer MMA: v = x * 2^s rounded to an integer of magnitude < 2^30 (exact for every element
+        // within 2^22 of max|x|, bf16 carrying 8 significant bits, so an outlier channel of an LLM activation leaves
+        // the ordinary elements exact; smaller ones keep an error below 2^-31 max|x|), split into four signed
+        // base-256 digits d0 + 256 d1 + 256^2 d2 + 256^3 d3 (each in [-128, 127]), each an int8 plane of Kpad bytes
+        // at xs + d x_plane_stride with every 8-block stored as (x0,x2,x4,x6,x1,x3,x5,x7) (even k pair with the low
+        // nibbles). Per 128-group g: sum(v) (float) at gsum[8g + 4] and the symmetric offsets 8 (S_0 + 256 S_1) and
+        // 8 256^2 (S_2 + 256 S_3) (S_d = the group's sum of digit d; floats, exact) at gsum[8g + 5] and gsum[8g + 6].
         float m = 0.f;
         bool bad = false;
         uint4 xc[XR] = {};
@@ -374,7 +372,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
                 inv = __int_as_float(0x7FC00000);                         // NaN or infinity in x
             } else if (mm > 0.f) {
                 const int ex = (int)((__float_as_uint(mm) >> 23) & 0xFF) - 127;   // floor(log2) (subnormal: -127)
-                sh = 26 - (ex < -126 ? -126 : ex);                        // max|x| * 2^sh in [2^26, 2^27)
+                sh = 29 - (ex < -126 ? -126 : ex);                        // max|x| * 2^sh in [2^29, 2^30)
                 sh = sh > 126 ? 126 : sh;                                 // 2^-sh stays a normal float
                 inv = __uint_as_float((uint32_t)(127 - sh) << 23);
             }
@@ -387,47 +385,55 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         const float up = __uint_as_float((uint32_t)(127 + (sh > 0 ? sh / 2 : 0)) << 23);
         const float up2 = __uint_as_float((uint32_t)(127 + (sh > 0 ? sh - sh / 2 : sh)) << 23);
         uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
-        int* gi = reinterpret_cast<int*>(gsum);
+        const int ps = x_plane_stride<F, DEC>(Kp);
         x_blocks_all<2, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) {
             // blocks past K / 8 arrive as zeros and stage as zero digits
-            int sd[4] = {0, 0, 0, 0};
+            int s01 = 0, s23 = 0;                            // digit sums packed two per word: S_a + 65536 S_b
             if (i < Kp / 8) {
                 const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-                int dg[4][8];
+                uint32_t t[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const float xf = (j & 1) ? bf_hi(vv[j >> 1]) : bf_lo(vv[j >> 1]);
-                    // v = x 2^sh exactly (an integer, |v| <= 2^27); t = v + 64 (1 + 128 + 128^2 + 128^3) >= 0 splits
-                    // into base-128 digits u0 + 128 u1 + 128^2 u2 + 128^3 u3, and d = u - 64 gives
-                    // v = d0 + 128 d1 + 128^2 d2 + 128^3 d3 with d0..d2 in [-64, 63] and d3 in [-64, 64]: integer
-                    // work and one conversion per element
-                    const int t = __float2int_rn((xf * up) * up2) + 135274560;
-                    dg[0][j] = (t & 127) - 64;
-                    dg[1][j] = ((t >> 7) & 127) - 64;
-                    dg[2][j] = ((t >> 14) & 127) - 64;
-                    dg[3][j] = (t >> 21) - 64;
+                    // v = x 2^sh exactly (an integer, |v| < 2^30), and t = v + 0x80808080 lies in [0, 2^32): its bytes
+                    // are b_d = d_d + 128, the balanced base-256 digits of v offset by 128 (one add per element)
+                    t[j] = (uint32_t)__float2int_rn((xf * up) * up2) + 0x80808080u;
                 }
+                // 4 x 4 byte transposes (element words -> digit planes), evens then odds; b ^ 0x80 is d as an int8
+                uint32_t pe[4], po[4];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t* out = h ? po : pe;
+                    const uint32_t a = __byte_perm(t[h], t[h + 2], 0x5140), b = __byte_perm(t[h], t[h + 2], 0x7362);
+                    const uint32_t c = __byte_perm(t[h + 4], t[h + 6], 0x5140), d = __byte_perm(t[h + 4], t[h + 6], 0x7362);
+                    out[0] = __byte_perm(a, c, 0x5410) ^ 0x80808080u;
+                    out[1] = __byte_perm(a, c, 0x7632) ^ 0x80808080u;
+                    out[2] = __byte_perm(b, d, 0x5410) ^ 0x80808080u;
+                    out[3] = __byte_perm(b, d, 0x7632) ^ 0x80808080u;
+                }
+                int sd[4];
 #pragma unroll
                 for (int d = 0; d < 4; ++d) {
-                    sd[d] = ((dg[d][0] + dg[d][1]) + (dg[d][2] + dg[d][3])) + ((dg[d][4] + dg[d][5]) + (dg[d][6] + dg[d][7]));
-                    // evens first (x0, x2, x4, x6), then odds: the low nibbles of a byte pair hold the even k
-                    const uint32_t e = __byte_perm(__byte_perm(dg[d][0], dg[d][2], 0x0040), __byte_perm(dg[d][4], dg[d][6], 0x0040), 0x5410);
-                    const uint32_t o = __byte_perm(__byte_perm(dg[d][1], dg[d][3], 0x0040), __byte_perm(dg[d][5], dg[d][7], 0x0040), 0x5410);
-                    *reinterpret_cast<uint2*>(planes + (size_t)d * x_plane_stride<F, DEC>(Kp) + 8 * (size_t)i) =
-                        make_uint2(e, o);
+                    sd[d] = __dp4a((int)pe[d], 0x01010101, __dp4a((int)po[d], 0x01010101, 0));   // |S_d| <= 1024
+                    *reinterpret_cast<uint2*>(planes + (size_t)d * ps + 8 * (size_t)i) = make_uint2(pe[d], po[d]);
                 }
+                s01 = sd[0] + 65536 * sd[1];
+                s23 = sd[2] + 65536 * sd[3];
             }
+            // over the 16 lanes of a group: every sum stays within +-16384, so the packed halves add without loss
 #pragma unroll
-            for (int d = 0; d < 4; ++d)
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) sd[d] += __shfl_xor_sync(0xffffffffu, sd[d], o);   // 16-lane groups
+            for (int o = 8; o > 0; o >>= 1) {
+                s01 += __shfl_xor_sync(0xffffffffu, s01, o);
+                s23 += __shfl_xor_sync(0xffffffffu, s23, o);
+            }
             if (i < Kp / 8 && (i & 15) == 0) {
                 const int gg = i >> 4;
-#pragma unroll
-                for (int d = 0; d < 4; ++d) gi[8 * gg + d] = sd[d];
-                gsum[8 * gg + 4] = ((float)sd[0] + 128.f * (float)sd[1]) + (16384.f * (float)sd[2] + 2097152.f * (float)sd[3]);
-                gsum[8 * gg + 5] = 8.f * ((float)sd[0] + 128.f * (float)sd[1]);
-                gsum[8 * gg + 6] = 131072.f * ((float)sd[2] + 128.f * (float)sd[3]);
+                const int S0 = (int)(short)(s01 & 0xFFFF), S1 = (s01 - S0) >> 16;
+                const int S2 = (int)(short)(s23 & 0xFFFF), S3 = (s23 - S2) >> 16;
+                const float lo = (float)S0 + 256.f * (float)S1, hi = (float)S2 + 256.f * (float)S3;   // exact
+                gsum[8 * gg + 4] = fmaf(hi, 65536.f, lo);
+                gsum[8 * gg + 5] = 8.f * lo;
+                gsum[8 * gg + 6] = 524288.f * hi;
             }
         }, xc, map);
     } else if constexpr (DEC == 1) {

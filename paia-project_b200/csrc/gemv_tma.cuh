@@ -98,6 +98,14 @@ __device__ __forceinline__ void bulk_copy_g2s_ef(void* dst, const void* src, uin
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
                  :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(m)), "l"(pol) : "memory");
 }
+// A box of the 3-D weight map (64 bytes x pieces x 16 rows) at piece `piece`, row `row` (x = 0: 16-byte aligned).
+__device__ __forceinline__ void tensor_copy_g2s_ef(void* dst, const CUtensorMap* map, int piece, int row, uint64_t* m,
+                                                   uint64_t pol) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%2, %3, %4}], [%5], %6;"
+                 :: "r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(piece), "r"(row),
+                    "r"(smem_addr(m)), "l"(pol) : "memory");
+}
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(m)) : "memory");
@@ -208,17 +216,30 @@ __host__ __device__ constexpr int tma_stage_bytes(int rs, bool blocked) {
 // Host: the stage geometry of a row of `nchunk` 16-byte chunks in a slot of `kcs` bytes per row (a multiple of 64):
 // the whole row when it fits (nch 1, kc = row bytes), else nch equal chunks of kc bytes (a multiple of 64), and the
 // row stride of the layout above.
-inline void tma_op_geometry(int nchunk, int kcs, int* nch, int* kc, int* rs) {
+// tensor: the layout the tiled tensor copy lands (never blocked); chunks of an odd number of 64-byte pieces when one fits
+// the slot, so that the row stride needs no padding piece (which the copy would read from the next chunk).
+inline void tma_op_geometry(int nchunk, int kcs, int* nch, int* kc, int* rs, bool tensor = false) {
     const long rb = (long)nchunk * 16;
     long c = rb;
     int n = 1;
     if (rb > kcs) {
         n = (int)((rb + kcs - 1) / kcs);
         c = ((rb + n - 1) / n + 63) / 64 * 64;
+        if (tensor) {
+            for (int m = n; m <= n + 3; ++m) {                // the fewest chunks of an odd piece count
+                long cm = ((rb + m - 1) / m + 63) / 64 * 64;
+                if ((cm / 64) % 2 == 0) cm += 64;
+                if (cm <= kcs && (rb + cm - 1) / cm == m) {
+                    n = m;
+                    c = cm;
+                    break;
+                }
+            }
+        }
     }
     *nch = n;
     *kc = (int)c;
-    if (n == 1 && rb % 64 == 0 && rb < kTmaBlockRow) {
+    if (!tensor && n == 1 && rb % 64 == 0 && rb < kTmaBlockRow) {
         *rs = (int)rb;                                         // blocked layout
     } else {
         const long c64 = (c + 63) / 64 * 64;
@@ -234,9 +255,9 @@ inline void tma_apply_slot(Params& p, GemvOp* ops, long kcs) {
     if (p.nops == 0) {
         const long rb = (long)p.nchunk * 16;
         const long n = (rb + kcs - 1) / kcs;
-        kcs = ((rb + n - 1) / n + 63) / 64 * 64;
-        tma_op_geometry(p.nchunk, (int)kcs, &p.nch, &p.kc, &p.rs);
-        p.st_bytes = tma_stage_bytes(p.rs, tma_blocked(p.nch, p.kc, p.rs));
+        if (!p.tlayout) kcs = ((rb + n - 1) / n + 63) / 64 * 64;
+        tma_op_geometry(p.nchunk, (int)kcs, &p.nch, &p.kc, &p.rs, p.tlayout != 0);
+        p.st_bytes = tma_stage_bytes(p.rs, !p.tlayout && tma_blocked(p.nch, p.kc, p.rs));
         p.mr = tma_meta_row((int)(kcs / 64), p.nch > 1);
     } else {
         int mn = 1 << 30, rs_max = 0, sb_max = 0;
@@ -266,10 +287,15 @@ inline void tma_apply_slot(Params& p, GemvOp* ops, long kcs) {
 // to x of the largest K), each op staged in its own geometry within it; p.K and p.nchunk become the largest K and row.
 constexpr long kTmaMinPiece4 = 2560;                          // smallest row piece of the 4-stage FP8 ring
 
+int encode_weight_map(Params& p);       // host, gemv_abi.cu: 1 when p.tmap_w holds the 16-row box map of p.W
+
 template <int F, int NC, int DEC, bool BAT = false>
 size_t tma_prep(Params& p, size_t cap) {
     if (BAT != (p.xm > 0) || (BAT && (p.xm > 8 || p.nops > 0 || p.tp_world > 0))) return 0;
     GemvOp* ops = p.host_ops ? p.host_ops : p.ops;
+    // on request, a single GEMV whose rows are whole 64-byte pieces streams full tiles as one tiled tensor copy per stage
+    p.tlayout = (p.nops == 0 && !BAT && (p.nchunk & 3) == 0 && p.tensor_on) ? 1 : 0;
+    p.tmap_ok = 0;
     if (p.nops > 0) {
         int K = 0, nchunk = 0;
         for (int j = 0; j < p.nops; ++j) {
@@ -325,7 +351,9 @@ size_t tma_prep(Params& p, size_t cap) {
     }
     p.ring = ring;
     const size_t total = tma_smem_bytes<F, NC, DEC, BAT>(p.K, ring, p.nch, p.mr, p.st_bytes, p.xm);
-    return total <= cap ? total : 0;
+    if (total > cap) return 0;
+    if (p.tlayout && p.W) p.tmap_ok = encode_weight_map(p);
+    return total;
 }
 
 // Accumulators of one consumer warp: two chains per unrolled step (BF16: the two k-halves of a step; FP8: even and odd
@@ -405,17 +433,17 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
             }
         }
     } else if constexpr (DEC == 2) {
-        // INT4, integer MMA against x as four int8 digit planes; lane group g reads plane g & 3, so MMA column d
-        // carries digit d (columns 4-7 repeat them and are never read). One LOP3 per word and nibble half: low
-        // nibbles go in as u8 n (chain L), high nibbles unshifted as u8 16 n (chain H), each mma.sync taking two words
-        // of one half against the matching even / odd x of those words. Per group:
-        // sum_d 128^d (L_d + H_d / 16 - 8 S_d) = sum_d (16 L_d + H_d) 128^d / 16 - C, with C = 8 sum_d 128^d S_d of the
+        // INT4, integer MMA against x as four int8 digit planes (balanced base 256); lane group g reads plane g & 3,
+        // so MMA column d carries digit d (columns 4-7 repeat them and are never read). One LOP3 per word and nibble
+        // half: low nibbles go in as u8 n (chain L), high nibbles unshifted as u8 16 n (chain H), each mma.sync taking
+        // two words of one half against the matching even / odd x of those words. Per group:
+        // sum_d 256^d (L_d + H_d / 16 - 8 S_d) = sum_d (16 L_d + H_d) 256^d / 16 - C, with C = 8 sum_d 256^d S_d of the
         // lane's digits staged per group (lanes c = 0 / 1 hold digits 0-1 / 2-3; c = 2, 3 hold unused columns).
-        // 16 L + H stays below 2^21, so every product with 128^d / 16 is an exact float.
+        // 16 L + H stays below 2^22, so every product with 256^d / 16 is an exact float.
         const int grp = (int)(threadIdx.x & 31) >> 2;
         const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp & 3) * xps + (size_t)gs * 128 + 32 * c;
-        const float flo = c == 0 ? 0.0625f : (c == 1 ? 1024.f : 0.f);
-        const float fhi = c == 0 ? 8.f : (c == 1 ? 131072.f : 0.f);
+        const float flo = c == 0 ? 0.0625f : (c == 1 ? 4096.f : 0.f);          // 256^d / 16
+        const float fhi = c == 0 ? 16.f : (c == 1 ? 1048576.f : 0.f);
 #pragma unroll
         for (int u = 0; u < NU; ++u) {
             const uint4 xa = *reinterpret_cast<const uint4*>(xp + 128 * u);
@@ -602,15 +630,19 @@ __device__ __forceinline__ bool tp_wait_counts(const unsigned int* blk, int base
 // ended): returns the calls this rank has completed, e. CTA 0 tells every rank that this rank has started call e + 1,
 // which orders its readers of call e's y (earlier in its stream) before any peer's stores of this call; then the CTA
 // waits (bounded, error 8) until every other rank has started call e + 1 before it stores into their y.
+// Every CTA counts itself in on [kTpReaders] after reading the epoch (in both forms, so the count stays (calls) x
+// CTAs); in the deferred form tp_leave's CTA 0 advances the epoch only once every CTA of the call has read it.
 __device__ __forceinline__ unsigned int tp_enter(const Params& p, int lane) {
-    const unsigned int* mine = p.tp_flag[p.tp_rank];
-    const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(mine + kTpEpoch);
+    unsigned int* mine = p.tp_flag[p.tp_rank];
+    unsigned int e = 0;
     if (lane == 0) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(e) : "l"(mine + kTpEpoch) : "memory");
+        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" :: "l"(mine + kTpReaders) : "memory");
         if (blockIdx.x == 0)
             for (int r = 0; r < p.tp_world; ++r) red_add_sys(p.tp_flag[r] + kTpReady + p.tp_rank, 1u);
         tp_wait_counts(mine, kTpReady, p.tp_world, p.tp_rank, e + 1u, 8);
     }
-    __syncwarp();
+    e = __shfl_sync(0xffffffffu, e, 0);
     return e;
 }
 // End of a TP call in one CTA's epilogue warp: every lane's stores into the ranks' y are released (warp barrier, then
@@ -618,6 +650,23 @@ __device__ __forceinline__ unsigned int tp_enter(const Params& p, int lane) {
 // (bounded, error 6) until all CTAs of every rank have counted in on this rank, and advances the epoch: the grid ends
 // only when this rank's y is complete.
 __device__ __forceinline__ void tp_leave(const Params& p, int lane, unsigned int e) {
+    if (p.tp_defer) {                                    // published by the next paia_gemv_tp_exchange
+        if (blockIdx.x == 0 && lane == 0) {
+            unsigned int* mine = p.tp_flag[p.tp_rank];
+            const uint64_t t0 = global_ns();
+            unsigned int v;
+            for (;;) {
+                asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + kTpReaders) : "memory");
+                if ((int)(v - (e + 1u) * gridDim.x) >= 0) break;
+                const uint64_t dt = global_ns() - t0;
+                if (dt > kAbortCheckNs && tma_aborted()) break;
+                if (dt > 1000000000ull) { atomicCAS(&g_tma_error, 0, 9); break; }
+                __nanosleep(64);
+            }
+            *reinterpret_cast<volatile unsigned int*>(mine + kTpEpoch) = e + 1u;
+        }
+        return;
+    }
     __syncwarp();
     if (lane == 0) {
         asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -628,6 +677,23 @@ __device__ __forceinline__ void tp_leave(const Params& p, int lane, unsigned int
             *reinterpret_cast<volatile unsigned int*>(mine + kTpEpoch) = e + 1u;
         }
     }
+}
+
+// The exchange after deferred TP calls (one thread): a system-scope fence makes every store this rank's earlier
+// kernels made (stream order: they have completed) visible system-wide, then the rank counts itself in on every rank's
+// exchange block and waits (bounded, error 6) until every rank has done the same for this exchange.
+struct TpExchangeArgs {
+    unsigned int* flag[8];
+    int world, rank;
+};
+__global__ void tp_exchange_kernel(const __grid_constant__ TpExchangeArgs a) {
+    if (threadIdx.x != 0) return;
+    asm volatile("fence.sc.sys;" ::: "memory");
+    for (int r = 0; r < a.world; ++r) red_add_sys(a.flag[r] + kTpArrive + a.rank, 1u);
+    unsigned int* mine = a.flag[a.rank];
+    const unsigned int e = *reinterpret_cast<volatile unsigned int*>(mine + kTpEpoch);
+    tp_wait_counts(mine, kTpArrive, a.world, -1, e + 1u, 6);
+    *reinterpret_cast<volatile unsigned int*>(mine + kTpEpoch) = e + 1u;
 }
 
 // BAT: batched x (p.xm rows, 1..8): x row m rides in MMA column m (lanes of group g read x row g), every D element
@@ -679,12 +745,14 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         // Streams every op's stages back to back: op j + 1's weights never wait for op j's x.
         const int pre = (p.pre > 0 && p.pre < ST) ? p.pre : -1;    // -1: never wait
         const uint64_t wpol = l2_evict_first();
+        // tiled tensor copies land at 128-byte aligned stage addresses (stage sizes are multiples of 128)
+        const bool tensor = p.tmap_ok && p.nops == 0 && (smem_addr(ring) & 127u) == 0;
         int s = 0, g = 0;                                     // ring slot, stage count over all ops
         uint32_t ph = 0;                                      // parity of the slot's previous release
         for (int jo = 0; jo < nops; ++jo) {
             const GemvOp op = tma_op(p, jo);
             const int NCH = op.nch, KC = op.kc, RS = op.rs, CS = KC >> 6;
-            const bool dense = tma_blocked(NCH, KC, RS);     // short whole rows: one copy per 8-row block
+            const bool dense = !p.tlayout && tma_blocked(NCH, KC, RS);   // short whole rows: one copy per 8-row block
             const int S = (op.nchunk + 3) >> 2;
             const size_t rowbytes = (size_t)op.nchunk * 16;
             const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
@@ -711,7 +779,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     if (g == pre) mbar_wait(xready, 0, 5);
                     if (g >= ST) mbar_wait(&empty[s], ph, 1);
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before copies
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)nrows * bytes + (F == kINT4A ? 2 : 1) * mbytes);
+                    const uint32_t wbytes = (tensor && nrows == 16) ? 16u * (uint32_t)RS : (uint32_t)nrows * bytes;
+                    mbar_arrive_expect_tx(&full[s], wbytes + (F == kINT4A ? 2 : 1) * mbytes);
                     if (meta_bulk) {
                         uint8_t* mdst = meta + (size_t)s * MB + 112;
                         const size_t moff = (size_t)r0 * op.groups * 2;
@@ -729,6 +798,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                         bulk_copy_g2s_ef(sdst + (size_t)lane * (8 * RS + 64), op.W + (size_t)(r0 + 8 * lane) * rowbytes,
                                          (uint32_t)(nb * rowbytes), &full[s], wpol);
                     }
+                } else if (tensor && nrows == 16) {           // a full tile's stage: one tiled copy of 16 rows
+                    if (lane == 0) tensor_copy_g2s_ef(sdst, &p.tmap_w, (j * KC) >> 6, r0, &full[s], wpol);
                 } else if (lane < nrows) {
                     bulk_copy_g2s_ef(sdst + (size_t)lane * RS,
                                      op.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s], wpol);
@@ -894,7 +965,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             consumer_barrier(1, NC * 32);
         }
         const int NCH = op.nch, RS = op.rs, CS = op.kc >> 6;
-        const bool blk = tma_blocked(NCH, op.kc, RS);
+        const bool blk = !p.tlayout && tma_blocked(NCH, op.kc, RS);
         const int m0 = tma_tile_row(g, blk), m1 = tma_tile_row(g + 8, blk);   // tile rows of MMA rows g, g + 8
         const int S = (op.nchunk + 3) >> 2;                   // 64-byte steps per row
         const int SF = op.nchunk >> 2;                        // steps whose four 16-byte chunks are all in the row
@@ -983,9 +1054,10 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 for (; sl < sfull; ++sl)
                     tma_steps<F, DEC, 1, false>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
                                                 op.nchunk, xps);
-                for (; sl < sb0; ++sl)                        // the ragged last step of the row
-                    tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl, c,
-                                               op.nchunk, xps);
+                if constexpr (!I4)                            // INT4 rows are whole 64-byte steps (K % 128 == 0)
+                    for (; sl < sb0; ++sl)                    // the ragged last step of the row
+                        tma_steps<F, DEC, 1, true>(A, acc0, acc1, r0p, r1p, xl, gsum, sc0, sc1, zr0, zr1, sl, gb + sl,
+                                                   c, op.nchunk, xps);
             }
 
             if (last) {

@@ -94,6 +94,16 @@ const Variant* tma_instances(int fmt, int math, int* n) {
 }
 #undef PB2_N
 
+int launch_tp_exchange(unsigned int* const* flag_all, int world, int rank, cudaStream_t st) {
+    TpExchangeArgs a{};
+    for (int r = 0; r < world; ++r) a.flag[r] = flag_all[r];
+    a.world = world;
+    a.rank = rank;
+    tp_exchange_kernel<<<1, 32, 0, st>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : (int)e;
+}
+
 // Error word of the bounded waits (1 producer gave up on a free stage, 2 consumer on a full stage, 3 epilogue on a
 // tile's partials, 4 consumer on a free partial buffer, 5 producer on the staged x, 6 tensor-parallel arrivals of
 // every rank's CTAs, 7 consumer on the previous op of a layer launch, 8 tensor-parallel start of the other ranks).

@@ -82,6 +82,10 @@ class GemvLib:
         lib.paia_gemv_tp.argtypes = [I, P, P, P, P, P, ctypes.POINTER(P), ctypes.POINTER(P), I, I, I, I, P]
         lib.paia_gemv_tp_ctas.restype = I
         lib.paia_gemv_tp_ctas.argtypes = [I, I, I]
+        lib.paia_gemv_tp_deferred.restype = I
+        lib.paia_gemv_tp_deferred.argtypes = [I, P, P, P, P, P, ctypes.POINTER(P), ctypes.POINTER(P), I, I, I, I, P]
+        lib.paia_gemv_tp_exchange.restype = I
+        lib.paia_gemv_tp_exchange.argtypes = [ctypes.POINTER(P), I, I, P]
         lib.paia_gemv_tp_alloc.restype = I
         lib.paia_gemv_tp_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(P)]
         lib.paia_gemv_tp_free.restype = I
@@ -226,7 +230,8 @@ class GemvLib:
     def launch_ex(self, kind, R, U, W, math, pdl, ks, ctas_per_sm, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr,
                   y_ptr, N, K, stream=None):
         """Any compiled kernel instance (tuning and comparisons): math 0/1 CUDA-core, 2-4 register-fed MMA, 5-8
-        TMA-fed MMA (R = ring stages, 0 = auto; ks = shared-memory share | stages-before-x << 8)."""
+        TMA-fed MMA (R = ring stages, 0 = auto; ks = shared-memory share | stages-before-x << 8 | tiled tensor copies
+        << 16)."""
         self._check(self._lib.paia_gemv_launch_ex(_KINDS[kind], R, U, W, math, pdl, ks, ctas_per_sm, Wq_ptr,
                                                   scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K,
                                                   self._st(stream)), "paia_gemv_launch_ex")
@@ -236,6 +241,15 @@ class GemvLib:
            stream=None):
         self._check(self._lib.paia_gemv_tp(_KINDS[kind], Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptrs,
                                            flag_ptrs, world, rank, N_local, K, self._st(stream)), "paia_gemv_tp")
+
+    def tp_deferred(self, kind, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptrs, flag_ptrs, world, rank,
+                    N_local, K, stream=None):
+        self._check(self._lib.paia_gemv_tp_deferred(_KINDS[kind], Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr,
+                                                    y_ptrs, flag_ptrs, world, rank, N_local, K, self._st(stream)),
+                    "paia_gemv_tp_deferred")
+
+    def tp_exchange(self, xflag_ptrs, world, rank, stream=None):
+        self._check(self._lib.paia_gemv_tp_exchange(xflag_ptrs, world, rank, self._st(stream)), "paia_gemv_tp_exchange")
 
     def tp_ctas(self, kind, N_local, K):
         n = self._lib.paia_gemv_tp_ctas(_KINDS[kind], N_local, K)

@@ -48,16 +48,18 @@ def _device_view(ptr, n, typestr, device):
     return torch.as_tensor(_CudaArray(ptr, n, typestr), device=device)
 
 
-# Counter block of one rank (uint32 words; kTpEpoch / kTpArrive / kTpReady in the kernel): calls completed here,
-# CTAs of each source rank done storing here, calls each source rank has started.
-COUNTER_WORDS, EPOCH, ARRIVE, READY = 32, 0, 8, 16
+# Counter block of one rank (uint32 words; kTpEpoch / kTpReaders / kTpArrive / kTpReady in the kernel): calls
+# completed here, CTAs here that have read the call count, CTAs of each source rank done storing here, calls each
+# source rank has started.
+COUNTER_WORDS, EPOCH, READERS, ARRIVE, READY = 32, 0, 4, 8, 16
 
 
 def expected_counts(epoch, world, ctas):
-    """A rank's counter block after `epoch` completed calls (uint32, wraps): the epoch, ctas * epoch arrivals from
-    every rank and epoch starts of every rank."""
+    """A rank's counter block after `epoch` completed complete-form calls (uint32, wraps): the epoch, ctas * epoch
+    readers, ctas * epoch arrivals from every rank and epoch starts of every rank."""
     blk = [0] * COUNTER_WORDS
     blk[EPOCH] = epoch & 0xFFFFFFFF
+    blk[READERS] = (epoch * ctas) & 0xFFFFFFFF
     for r in range(world):
         blk[ARRIVE + r] = (epoch * ctas) & 0xFFFFFFFF
         blk[READY + r] = epoch & 0xFFFFFFFF
@@ -130,6 +132,52 @@ class TpBuffers:
         self._y_mem = self._f_mem = None
 
 
+class TpExchange:
+    """The exchange block of every rank for deferred TP calls (paia_gemv_tp_deferred / paia_gemv_tp_exchange): this
+    rank's block (the library's own allocation) and every peer's mapped in. `run()` publishes this rank's deferred
+    stores and waits for every rank's; after it, the y of every deferred call issued before it is complete."""
+
+    def __init__(self, lib, device, group=None):
+        import torch
+        import torch.distributed as dist
+        self.lib, self.group = lib, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self._mem = lib.tp_alloc(4 * COUNTER_WORDS)
+        self.flag = _device_view(self._mem, COUNTER_WORDS, "<i4", device)
+        torch.cuda.synchronize(device)
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, lib.ipc_handle(self._mem), group=group)
+        self._opened = []
+        ptrs = []
+        for r, h in enumerate(gathered):
+            if r == self.rank:
+                ptrs.append(self._mem)
+            else:
+                q = lib.ipc_open(h)
+                self._opened.append(q)
+                ptrs.append(q)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)
+
+    def run(self, stream=None):
+        self.lib.tp_exchange(self.ptrs, self.world, self.rank, stream)
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        if self._mem is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for q in self._opened:
+            self.lib.ipc_close(q)
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.lib.tp_free(self._mem)
+        self._mem = None
+
+
 class ShardedGemv:
     """One rank's shard of a row-sharded GEMV. `Wq`, `s`, `z`, `bias` are this rank's rows (device tensors, formats as
     the per-format C-ABI calls); `N` is the full row count. `buffers`: a TpBuffers for N to share (else its own)."""
@@ -162,6 +210,14 @@ class ShardedGemv:
     def _ptrs(self):
         p = lambda t: t.data_ptr() if t is not None else None       # noqa: E731
         return p(self.Wq), p(self.s), p(self.z), p(self.bias)
+
+    def deferred(self, x, stream=None):
+        """The deferred form: this rank's outputs go into every rank's y, complete only after the next
+        TpExchange.run() on every rank (at most one deferred call per buffer set between two exchanges)."""
+        W, s, z, b = self._ptrs()
+        self.lib.tp_deferred(self.kind, W, s, z, x.data_ptr(), b, self.buf.y_ptrs, self.buf.f_ptrs, self.world,
+                             self.rank, self.N_local, self.K, stream)
+        return self.y
 
     def fused(self, x, stream=None):
         """y on every rank through the peer-store epilogue; returns this rank's full y, complete in stream order once

@@ -467,3 +467,20 @@ def test_fp8_tma_every_code_exact(L, math):
         assert ops.call_ex(L, ring, U, NC, math, 1, share, 0) == 0
         torch.cuda.synchronize()
         assert np.array_equal(O.bf16_to_f32(bits(ops.y)), want), (math, ring, U, NC, share)
+
+
+@pytest.mark.parametrize("kind,math", [("bf16", 5), ("fp8", 8), ("int4", 7), ("int4_asym", 7)])
+def test_tma_tensor_copies_equal_row_copies(L, kind, math):
+    """Full tiles as one tiled tensor copy per stage (paia_gemv_launch_ex, ks bit 16) give the same bits as the
+    per-row bulk copies: whole rows, chunked rows and a partial last tile per CTA."""
+    for (N, K) in ((4096, 4096), (300, 14336), (1000, 3584), (37, 18944)):
+        ops = make(kind, N, K, seed=N + 11 * K, with_bias=True)
+        outs = []
+        for ks in (0, 1 << 16):
+            ops.nan_fill()
+            assert ops.call_ex(L, 0, 2, 8, math, 1, ks, 0, with_bias=True) == 0
+            torch.cuda.synchronize()
+            outs.append(bits(ops.y).copy())
+        assert np.array_equal(outs[0], outs[1]), (kind, N, K)
+        check(ops, outs[1], ops.oracle(with_bias=True)[0], f"tensor copies {kind} {N}x{K}")
+    assert L.device_error(1) == 0

@@ -328,33 +328,48 @@ def tma_stage_bytes(rs, blocked):
     return (16 * rs + (64 if blocked else 0) + 127) // 128 * 128
 
 
-def tma_op_geometry(nchunk, kcs):
-    """Mirror of tma_op_geometry: (nch, kc, rs) of a row of nchunk 16-byte chunks in a slot of kcs bytes per row."""
+def tma_op_geometry(nchunk, kcs, tensor=False):
+    """Mirror of tma_op_geometry: (nch, kc, rs) of a row of nchunk 16-byte chunks in a slot of kcs bytes per row;
+    tensor: the layout of the tiled tensor copy (never blocked, chunks of an odd piece count where one fits)."""
     rb = nchunk * 16
     c, n = rb, 1
     if rb > kcs:
         n = (rb + kcs - 1) // kcs
         c = ((rb + n - 1) // n + 63) // 64 * 64
-    if n == 1 and rb % 64 == 0 and rb < BLOCK_ROW:
+        if tensor:
+            for m in range(n, n + 4):
+                cm = ((rb + m - 1) // m + 63) // 64 * 64
+                if (cm // 64) % 2 == 0:
+                    cm += 64
+                if cm <= kcs and (rb + cm - 1) // cm == m:
+                    n, c = m, cm
+                    break
+    if not tensor and n == 1 and rb % 64 == 0 and rb < BLOCK_ROW:
         return n, c, rb
     c64 = (c + 63) // 64 * 64
     return n, c, c64 + 64 if c64 % 128 == 0 else c64
 
 
-def tma_apply_slot(fmt, K, rowbytes, kcs, ops):
+def tma_apply_slot(fmt, K, rowbytes, kcs, ops, tensor=False):
     """Mirror of tma_apply_slot: (kc, nch, rs, st_bytes, mr, geos) for a slot of kcs bytes per row."""
     if not ops:
         n = (rowbytes + kcs - 1) // kcs
-        kb = ((rowbytes + n - 1) // n + 63) // 64 * 64
-        nch, kc, rs = tma_op_geometry(rowbytes // 16, kb)
-        return kc, nch, rs, tma_stage_bytes(rs, tma_blocked(nch, kc, rs)), tma_meta_row(kb // 64, nch > 1), None
+        kb = kcs if tensor else ((rowbytes + n - 1) // n + 63) // 64 * 64
+        nch, kc, rs = tma_op_geometry(rowbytes // 16, kb, tensor)
+        blocked = not tensor and tma_blocked(nch, kc, rs)
+        return kc, nch, rs, tma_stage_bytes(rs, blocked), tma_meta_row(kb // 64, nch > 1), None
     geos = [tma_op_geometry(ROWBYTES[fmt](k) // 16, kcs) for _, k in ops]
     st = max(tma_stage_bytes(g[2], tma_blocked(*g)) for g in geos)
     mr = tma_meta_row(kcs // 64, any(g[0] > 1 for g in geos))
     return kcs, min(g[0] for g in geos), max(g[2] for g in geos), st, mr, geos
 
 
-def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0):
+def tma_tensor(fmt, K, ops=None, xm=0, tensor_on=False):
+    """Whether a launch uses the tiled-tensor stage layout (on request: a single GEMV of whole 64-byte row pieces)."""
+    return bool(tensor_on) and not ops and not xm and ROWBYTES[fmt](K) % 64 == 0
+
+
+def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0, tensor_on=False):
     """Mirror of tma_prep<F, NC>: (kc, nch, rs, st_bytes, ring, smem) or None when the shape cannot be staged.
     Layer mode (`ops`: a list of (N, K)): K is the largest K, one slot size (kc = the slot's bytes per row) for all
     ops, nch the smallest op NCH, rs the largest op row stride, and a seventh element, the list of per-op
@@ -364,12 +379,13 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0):
     rowbytes = max(ROWBYTES[fmt](k) for _, k in ops) if ops else ROWBYTES[fmt](K)
     if ring == 1 or ring > 16:
         return None
+    tensor = tma_tensor(fmt, K, ops, xm, tensor_on)
     top = min((rowbytes + 63) // 64 * 64, 4096)
     kmin = min(top, 2048) if xm else 64
     geo = None
     for rmin in ([ring] if ring >= 2 else ([3] if xm else [3, 2])):
         for kcs in range(top, kmin - 1, -64):
-            kc, nch, rs, st, mr, geos = tma_apply_slot(fmt, K, rowbytes, kcs, ops)
+            kc, nch, rs, st, mr, geos = tma_apply_slot(fmt, K, rowbytes, kcs, ops, tensor)
             if tma_smem_bytes(fmt, NC, K, rmin, nch, mr, st, dec, xm) <= cap:
                 geo = (kc, nch, rs, st, mr, geos)
                 break
@@ -380,7 +396,7 @@ def tma_prep(fmt, NC, K, ring=0, cap=SMEM_CAP, dec=0, ops=None, xm=0):
     if fmt == "fp8" and dec == 3 and not xm and ring == 0 and not ops and geo[1] > 1:
         # chunked e4m3 rows: 4 stages of pieces >= 2.5 KB when they fit (kTmaMinPiece4)
         for kcs in range(top, 2560 - 1, -64):
-            cand = tma_apply_slot(fmt, K, rowbytes, kcs, ops)
+            cand = tma_apply_slot(fmt, K, rowbytes, kcs, ops, tensor)
             if tma_smem_bytes(fmt, NC, K, 4, cand[1], cand[4], cand[3], dec, xm) <= cap:
                 geo = cand
                 break
@@ -430,7 +446,7 @@ def meta_copy_u16(mod, T, e0, n, slot, lanes=32):
         assert got.get(off + e - e0) == e, (mod, T, e0, n, e)
 
 
-def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1, dec=0):
+def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1, dec=0, tensor_on=False):
     """Replay of gemv_tma_kernel: per CTA the producer streams T x NCH stages through a ring of ST stages (two block
     copies per whole-row stage, else one copy per valid row, KC bytes except the ragged last chunk) while the
     consumers split each stage's 64-byte steps into NC equal ranges of <= U-step iterations. Checks copies in bounds
@@ -438,20 +454,31 @@ def replay_tma(fmt, N, K, NC, ring, U, sms=148, per_sm=1, share=1, dec=0):
     and group, bias) in range, every output stored once, conflict-free fragment loads, and that the full/empty
     mbarrier protocol always makes progress."""
     cap = share_cap(share)
-    geo = tma_prep(fmt, NC, K, ring, cap, dec)
+    geo = tma_prep(fmt, NC, K, ring, cap, dec, tensor_on=tensor_on)
     assert geo is not None, (fmt, K, NC, ring, share)
     KC, NCH, RS, ST_BYTES, ST, smem = geo
     G = grid(N, sms, per_sm)
-    nsts = replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G, (KC + 63) // 64)
+    tensor = tma_tensor(fmt, K, tensor_on=tensor_on)
+    nsts = replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G, slot_steps(fmt, K, KC, tensor),
+                         tensor=tensor)
     for nst in nsts:
         replay_ring(nst, ST, NC, [i // NCH for i in range(nst)], tma_part_bufs(ST, NCH))
 
 
-def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G, CS_SLOT, CHUNKED=False):
+def slot_steps(fmt, K, KC, tensor):
+    """64-byte steps of the stage slot the metadata ring is sized for: the chunk, or with the tensor layout the slot
+    the geometry search stopped at (at least the chunk; the mirror takes the chunk, the smallest slot it allows)."""
+    return (KC + 63) // 64
+
+
+def replay_tma_op(fmt, N, K, NC, U, KC, NCH, RS, ST_BYTES, ST, smem, cap, G, CS_SLOT, CHUNKED=False, tensor=False):
     """Stage-level checks of one GEMV streamed with geometry (KC, NCH, RS) in stage slots of ST_BYTES (metadata slots
-    for CS_SLOT steps per row) by G CTAs; returns the number of stages of every CTA."""
+    for CS_SLOT steps per row) by G CTAs; returns the number of stages of every CTA. tensor: the stage layout of the
+    tiled tensor copy (full tiles: one 16-row box of RS bytes per row, RS / 64 pieces <= 256, 128-byte aligned)."""
     assert smem <= cap and RS % 64 == 0 and ST_BYTES % 128 == 0 and 2 <= ST <= 16
-    blocked = tma_blocked(NCH, KC, RS)
+    blocked = not tensor and tma_blocked(NCH, KC, RS)
+    if tensor:
+        assert RS // 64 <= 256 and 16 * RS <= ST_BYTES and (RS // 64) % 2 == 1 and KC % 64 == 0
     assert tma_row_off(15, RS, blocked) + RS <= ST_BYTES
     check_banks(RS, blocked)
     CS = KC // 64
@@ -714,3 +741,12 @@ def test_batched_geometry(fmt):
         assert sum(g) == 16 and max(g) >= 2, g
     kc, nch, rs, st, ring, smem = tma_prep(fmt, 8, 4096, 0, SMEM_CAP, 0, xm=8)
     replay_tma_op(fmt, 300, 4096, 8, 2, kc, nch, rs, st, ring, smem, SMEM_CAP, 7, (kc + 63) // 64)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int4", "int4_asym"])
+def test_tensor_copy_layout_replays(fmt):
+    """The stage layout of the optional tiled tensor copies (never blocked, odd piece counts): whole and chunked rows
+    replay cleanly, fragment loads stay conflict-free, and a full tile's box (16 rows x RS) fits its stage."""
+    dec = 2 if fmt.startswith("int4") else (3 if fmt == "fp8" else 0)
+    for N, K in ((4096, 4096), (300, 14336), (1000, 3584), (37, 18944)):
+        replay_tma(fmt, N, K, 8, 0, 2, sms=148 if N > 1000 else 7, dec=dec, tensor_on=True)

@@ -84,6 +84,27 @@ def test_tp_waits_give_up_with_an_error_status(L, missing):
     check(ops, bits(ops.y), ops.oracle()[0], "fp8 after a timed-out wait")
 
 
+def test_tp_exchange_gives_up_with_an_error_status(L):
+    """The exchange kernel with a second rank that never exchanges (both blocks local on one GPU): its wait gives up
+    after ~1 s with code 6, and the GPU keeps working."""
+    import time
+    from paia_gemv import tp
+    L.device_error(1)
+    blks = [torch.zeros(tp.COUNTER_WORDS, dtype=torch.int32, device="cuda") for _ in range(2)]
+    P = ctypes.c_void_p
+    t0 = time.perf_counter()
+    L.tp_exchange((P * 2)(blks[0].data_ptr(), blks[1].data_ptr()), 2, 0)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    assert L.device_error(1) == 6 and 0.9 < dt < 6.0, dt
+    assert blks[0][tp.ARRIVE].item() == 1 and blks[1][tp.ARRIVE].item() == 1   # counted in on both blocks
+    ops = make("fp8", 300, 1024, seed=3)
+    ops.nan_fill()
+    ops.call(L, 0)
+    torch.cuda.synchronize()
+    check(ops, bits(ops.y), ops.oracle()[0], "fp8 after a timed-out exchange")
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -129,6 +150,27 @@ def _two_rank_worker(rank, world, port, kind, result):
         torch.cuda.synchronize()
         err = L.device_error(1)
         ok = err == 0 and all(np.array_equal(bits(o), want[i % 2]) for i, o in enumerate(outs))
+    if ok:
+        # deferred form: two ops per step into their own buffers, one exchange per step, rank 1 behind; after each
+        # exchange both outputs are complete and equal to the complete-form results
+        ex = tp.TpExchange(L, torch.device("cuda", rank))
+        g1 = g                                          # a buffer set may switch forms between calls
+        g2 = tp.ShardedGemv(L, kind, sl(full.W), sl(full.s), sl(full.z), None, N, K)
+        outs = []
+        for i in range(20):
+            if rank == 1:
+                torch.cuda._sleep(100000)
+            xa, xb = (full.x, x2) if i % 2 == 0 else (x2, full.x)
+            ya = g1.deferred(xa)
+            yb = g2.deferred(xb)
+            ex.run()
+            outs.append((ya.clone(), yb.clone(), i % 2))
+        torch.cuda.synchronize()
+        err = L.device_error(1)
+        ok = err == 0 and all(np.array_equal(bits(a), want[k]) and np.array_equal(bits(b), want[1 - k])
+                              for a, b, k in outs)
+        g2.close()
+        ex.close()
     g.close()
     dist.destroy_process_group()
     result.put((rank, bool(ok), err, rel))
