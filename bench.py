@@ -1293,6 +1293,32 @@ def run_tp(args, rank, world, local_rank):
     return 0
 
 
+def run_decode_loop(args):
+    """Tokens per second of the minimal decode step (paia_gemv.decode): Llama-3.1-8B and Qwen2.5-7B with synthetic
+    weights in every format, a 1024-position KV cache, the whole token (GEMVs, norms, RoPE, attention, SiLU x up,
+    residuals, lm_head, argmax) as one CUDA graph; next to it the GEMVs alone (decode_token, the same weights bytes)."""
+    import torch
+    from paia_gemv import decode, load_lib
+    torch.cuda.set_device(0)
+    lib = load_lib()
+    peak, _ = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    for model in ("llama31_8b", "qwen25_7b"):
+        for kind in args.kinds.split(","):
+            m = decode.DecodeModel(lib, model, kind, ctx=1024)
+            us, ids = decode.time_tokens(m, tokens=20)
+            wb = m.weight_bytes()
+            del m
+            torch.cuda.empty_cache()
+            gemv_only = decode_token(lib, kind, model, g, load_tuned(), peak, "per_op", reps=5)
+            print(json.dumps({"model": model, "kind": kind, "us_per_token": round(us, 1),
+                              "tokens_per_s": round(1e6 / us, 1), "weight_GB": round(wb / 1e9, 3),
+                              "GBps_weights": round(wb / us / 1e3, 1),
+                              "gemv_only_us_per_token": gemv_only["decode_us_per_token"], "ctx": 1024,
+                              "last_token": ids[-1]}), flush=True)
+    return 0
+
+
 def run_tune(args):
     """Per-shape variant choice for B200 written to paia-project_b200/tuned/b200.json in the reference's tuned-table
     schema (src/tools/dev_sweep_bf16.py:90-99: per N x K the best (R, U, W, S, H) with its us and GB/s and the top 5 with
@@ -1407,6 +1433,8 @@ def main():
     ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
     ap.add_argument("--launches", type=int, default=4)
     ap.add_argument("--tune", action="store_true", help="per-shape variant sweep -> paia-project_b200/tuned/b200.json")
+    ap.add_argument("--decode-loop", action="store_true",
+                    help="tokens/s of the minimal decode step (GEMVs + norms, RoPE, attention, sampling)")
     ap.add_argument("--tune-all", action="store_true", help="with --tune: every tuple on every shape")
     ap.add_argument("--batched", action="store_true", help="M > 1 activation rows (paia_gemv_batched)")
     ap.add_argument("--copy-sweep", action="store_true",
@@ -1427,6 +1455,8 @@ def main():
         return run_sweep(args)
     if args.tune:
         return run_tune(args)
+    if args.decode_loop:
+        return run_decode_loop(args)
     if args.one:
         return run_one(args)
     if args.families:

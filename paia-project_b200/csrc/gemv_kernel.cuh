@@ -62,7 +62,7 @@ struct GemvOp {
 };
 constexpr int kMaxOps = 6;             // ops carried in the kernel parameters
 // Tensor-parallel counter block of one rank (uint32 words): epoch, then per-source arrival and ready counts.
-constexpr int kTpEpoch = 0, kTpReaders = 4, kTpArrive = 8, kTpReady = 16, kTpCounterWords = 32;
+constexpr int kTpEpoch = 0, kTpReaders = 4, kTpComplete = 5, kTpArrive = 8, kTpReady = 16, kTpCounterWords = 32;
 constexpr int kMaxPlanOps = 4096;       // ops of a plan (device-memory op table)
 
 struct Params {

@@ -672,8 +672,12 @@ __device__ __forceinline__ void tp_leave(const Params& p, int lane, unsigned int
         asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int r = 0; r < p.tp_world; ++r) red_add_sys(p.tp_flag[r] + kTpArrive + p.tp_rank, 1u);
         if (blockIdx.x == 0) {
+            // arrivals count complete-form calls only ([kTpComplete], touched by CTA 0 alone), so a buffer set may
+            // also take deferred calls, which count none
             unsigned int* mine = p.tp_flag[p.tp_rank];
-            tp_wait_counts(mine, kTpArrive, p.tp_world, -1, (e + 1u) * gridDim.x, 6);
+            const unsigned int cc = *reinterpret_cast<volatile unsigned int*>(mine + kTpComplete);
+            tp_wait_counts(mine, kTpArrive, p.tp_world, -1, (cc + 1u) * gridDim.x, 6);
+            *reinterpret_cast<volatile unsigned int*>(mine + kTpComplete) = cc + 1u;
             *reinterpret_cast<volatile unsigned int*>(mine + kTpEpoch) = e + 1u;
         }
     }
@@ -749,7 +753,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const bool tensor = p.tmap_ok && p.nops == 0 && (smem_addr(ring) & 127u) == 0;
         int s = 0, g = 0;                                     // ring slot, stage count over all ops
         uint32_t ph = 0;                                      // parity of the slot's previous release
-        for (int jo = 0; jo < nops; ++jo) {
+        bool live = true;                                     // false once a wait gave up: issue nothing more
+        for (int jo = 0; jo < nops && live; ++jo) {
             const GemvOp op = tma_op(p, jo);
             const int NCH = op.nch, KC = op.kc, RS = op.rs, CS = KC >> 6;
             const bool dense = !p.tlayout && tma_blocked(NCH, KC, RS);   // short whole rows: one copy per 8-row block
@@ -773,11 +778,18 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 const int nsteps = last ? S - j * CS : CS;
                 const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
                 const uint32_t mbytes = meta_bulk ? (uint32_t)(2 * nrows * op.groups) : 0u;   // per metadata array
+                // x is read right after the dependency wait: streaming only `pre` stages until it is staged keeps the
+                // x loads from queueing behind a whole ring of this SM's copies. A wait that gives up stops the
+                // producer: refilling a slot whose consumers never released it would arrive on a barrier phase more
+                // often than it expects.
+                bool ok = true;
                 if (lane == 0) {
-                    // x is read right after the dependency wait: streaming only `pre` stages until it is staged
-                    // keeps the x loads from queueing behind a whole ring of this SM's copies
-                    if (g == pre) mbar_wait(xready, 0, 5);
-                    if (g >= ST) mbar_wait(&empty[s], ph, 1);
+                    if (g == pre) ok = mbar_wait(xready, 0, 5);
+                    if (ok && g >= ST) ok = mbar_wait(&empty[s], ph, 1);
+                }
+                live = __shfl_sync(0xffffffffu, ok, 0);
+                if (!live) break;
+                if (lane == 0) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before copies
                     const uint32_t wbytes = (tensor && nrows == 16) ? 16u * (uint32_t)RS : (uint32_t)nrows * bytes;
                     mbar_arrive_expect_tx(&full[s], wbytes + (F == kINT4A ? 2 : 1) * mbytes);
@@ -862,6 +874,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const unsigned int tp_e = p.tp_world > 0 ? tp_enter(p, lane) : 0u;
         int b = 0;
         uint32_t bph = 0;
+        bool live = true;                                     // false once a wait gave up: no reads, no arrivals
         for (int jo = 0; jo < nops; ++jo) {
             const GemvOp op = tma_op(p, jo);
             const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
@@ -876,8 +889,9 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     if constexpr (F == kFP8) rs = ld_f32(reinterpret_cast<const float*>(op.s) + row);
                     if (op.bias) rbias = __uint_as_float((uint32_t)ld_u16(op.bias + row) << 16);
                 }
-                mbar_wait(&tdone[b], bph, 3);
-                if constexpr (BAT) {
+                live = __all_sync(0xffffffffu, live && mbar_wait(&tdone[b], bph, 3));
+                if (!live) {
+                } else if constexpr (BAT) {
                     // 16 rows x XM x rows: lane pairs (row r, x row m); row scale first, then x row m's scale
                     const float* buf = part + (size_t)b * NC * 16 * 8;
                     for (int idx = lane; idx < 16 * XM; idx += 32) {
@@ -914,7 +928,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     }
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&pfree[b]);
+                if (live && lane == 0) mbar_arrive(&pfree[b]);
                 if (++b == NB) { b = 0; bph ^= 1u; }
             }
             if (p.nops > 0) {
@@ -952,6 +966,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     float acc0 = 0.f, acc1 = 0.f;
     float acc4[4] = {0.f, 0.f, 0.f, 0.f};                     // batched INT4: rows g, g + 8 x columns 2c, 2c + 1
     int s = 0, b = 0, tg = 0;                                 // ring slot, partial buffer, tiles over all ops
+    bool live = true;                                         // false once one of this warp's waits gave up
     uint32_t ph = 0, bph = 0;
     for (int jo = 0; jo < nops; ++jo) {
         const GemvOp op = tma_op(p, jo);
@@ -1006,7 +1021,9 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         for (int i = 0; i < nst; ++i) {
             const int r0 = rb + 16 * t;
             const bool last = j == NCH - 1;
-            mbar_wait(&full[s], ph, 2);
+            // once a wait gave up the warp stays in step with the loop (and with the named barriers of layer mode)
+            // but reads no stage and arrives on no barrier: no phase gets more arrivals than it expects
+            live = __all_sync(0xffffffffu, live && mbar_wait(&full[s], ph, 2));
             const int nsteps = last ? S - j * CS : CS;
             const int sa0 = warp * nsteps / NC, sb0 = (warp + 1) * nsteps / NC;
             const uint8_t* st = ring + (size_t)s * p.st_bytes;
@@ -1037,7 +1054,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             }
             const int gb = j * CS;                            // global step of stage-local step 0
             const int sfull = SF - gb < sb0 ? SF - gb : sb0;  // steps below sfull are whole
-            int sl = sa0;
+            int sl = live ? sa0 : sb0;                        // a warp that gave up skips the stage's steps
             if constexpr (BAT && I4) {
 #pragma unroll 1
                 for (; sl + U <= sfull; sl += U)
@@ -1098,10 +1115,12 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     }
                     A.zero();
                 }
-                if (tg >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile tg - NB
+                if (live && tg >= NB)                          // the epilogue warp has read tile tg - NB
+                    live = __all_sync(0xffffffffu, mbar_wait(&pfree[b], bph ^ 1u, 4));
                 ++tg;
                 float* buf = part + (size_t)b * NC * 16 * PC;
-                if constexpr (BAT) {
+                if (!live) {
+                } else if constexpr (BAT) {
                     float* r0b = buf + (warp * 16 + m0) * 8 + 2 * c;
                     float* r1b = buf + (warp * 16 + m1) * 8 + 2 * c;
                     r0b[0] = sb[0]; r0b[1] = sb[1]; r1b[0] = sb[2]; r1b[1] = sb[3];
@@ -1109,11 +1128,11 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     buf[warp * 16 + m0] = s0; buf[warp * 16 + m1] = s1;
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tdone[b]);         // release: this warp's partials of the tile
+                if (live && lane == 0) mbar_arrive(&tdone[b]); // release: this warp's partials of the tile
                 if (++b == NB) { b = 0; bph ^= 1u; }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (live && lane == 0) mbar_arrive(&empty[s]);
             if (++s == ST) { s = 0; ph ^= 1u; }
             if (++j == NCH) { j = 0; ++t; }
         }

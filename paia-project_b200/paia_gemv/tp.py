@@ -48,10 +48,10 @@ def _device_view(ptr, n, typestr, device):
     return torch.as_tensor(_CudaArray(ptr, n, typestr), device=device)
 
 
-# Counter block of one rank (uint32 words; kTpEpoch / kTpReaders / kTpArrive / kTpReady in the kernel): calls
-# completed here, CTAs here that have read the call count, CTAs of each source rank done storing here, calls each
-# source rank has started.
-COUNTER_WORDS, EPOCH, READERS, ARRIVE, READY = 32, 0, 4, 8, 16
+# Counter block of one rank (uint32 words; kTpEpoch / kTpReaders / kTpComplete / kTpArrive / kTpReady in the kernel):
+# calls completed here, CTAs here that have read the call count, complete-form calls, CTAs of each source rank done
+# storing here (complete form), calls each source rank has started.
+COUNTER_WORDS, EPOCH, READERS, COMPLETE, ARRIVE, READY = 32, 0, 4, 5, 8, 16
 
 
 def expected_counts(epoch, world, ctas):
@@ -60,6 +60,7 @@ def expected_counts(epoch, world, ctas):
     blk = [0] * COUNTER_WORDS
     blk[EPOCH] = epoch & 0xFFFFFFFF
     blk[READERS] = (epoch * ctas) & 0xFFFFFFFF
+    blk[COMPLETE] = epoch & 0xFFFFFFFF
     for r in range(world):
         blk[ARRIVE + r] = (epoch * ctas) & 0xFFFFFFFF
         blk[READY + r] = epoch & 0xFFFFFFFF

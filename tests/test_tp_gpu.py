@@ -54,6 +54,33 @@ def test_tp_world1_matches_tma_instance(L, kind):
     check(ops, bits(y), ops.oracle(with_bias=True)[0], f"tp world 1 {kind}")
 
 
+def test_tp_world1_forms_interleave(L):
+    """One buffer set taking complete-form calls, deferred calls with an exchange (world 1: the rank counts itself
+    in), then complete-form calls again: every result equals the TMA instance and no wait gives up."""
+    from paia_gemv import tp
+    N, K = 1000, 4096
+    ops = make("fp8", N, K, seed=23)
+    ref = torch.full((N,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    L.launch_ex("fp8", 0, 2, 8, 8, 1, 0, 0, _ptr(ops.W), _ptr(ops.s), None, _ptr(ops.x), None, ref.data_ptr(), N, K)
+    y = torch.full((N,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    flag = torch.zeros(tp.COUNTER_WORDS, dtype=torch.int32, device="cuda")
+    xblk = torch.zeros(tp.COUNTER_WORDS, dtype=torch.int32, device="cuda")
+    P = ctypes.c_void_p
+    yp, fp, xp = (P * 1)(y.data_ptr()), (P * 1)(flag.data_ptr()), (P * 1)(xblk.data_ptr())
+    L.device_error(1)
+    for form in ("complete", "complete", "deferred", "deferred", "complete", "deferred", "complete"):
+        y.fill_(float("nan"))
+        if form == "complete":
+            L.tp("fp8", _ptr(ops.W), _ptr(ops.s), None, _ptr(ops.x), None, yp, fp, 1, 0, N, K)
+        else:
+            L.tp_deferred("fp8", _ptr(ops.W), _ptr(ops.s), None, _ptr(ops.x), None, yp, fp, 1, 0, N, K)
+            L.tp_exchange(xp, 1, 0)
+        torch.cuda.synchronize()
+        assert L.device_error(1) == 0, form
+        assert np.array_equal(bits(y), bits(ref)), form
+    assert flag[tp.EPOCH].item() == 7 and flag[tp.COMPLETE].item() == 4 and xblk[tp.EPOCH].item() == 3
+
+
 @pytest.mark.parametrize("missing", ["start", "arrivals"])
 def test_tp_waits_give_up_with_an_error_status(L, missing):
     """World 2 on one GPU with both counter blocks local and no second rank: nothing ever counts rank 1 in. With its
