@@ -152,6 +152,17 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
                         const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
                         void* stream);
 
+/* No reference kernel (survey row f3, the QKV neighbour of the decode GEMV): y = RoPE(W x + bias) for a fused QKV
+ * projection, the rotary embedding applied in the epilogue. Rows [0, rope_rows) are the q and k heads (head_dim rows
+ * each) in pair-interleaved order - row 2i + h of a head holds dimension i + h head_dim / 2 (rope_pair_rows in
+ * paia_gemv.quant permutes W, its scales / zeros and the bias once) - and rows past rope_rows (v) are as usual. The
+ * epilogue rotates pair i of each head by pos * theta^(-2i / head_dim) (the rotate-half form) and stores every
+ * dimension of every head at its natural row, so y is in the usual order. Same checks and codes as the per-format
+ * calls; -2 also for odd N or head_dim, rope_rows not a multiple of head_dim, theta <= 0, pos < 0, or a shape the
+ * TMA-fed kernel cannot stage. */
+int paia_gemv_rope(int kind, const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                   void* y, int N, int K, int rope_rows, int head_dim, float pos, float theta, void* stream);
+
 /* Batched x (M >= 1 activation rows; the reference kernels are M = 1 only, src/README.md:118):
  * Y[M, N] = X[M, K] . dequant(W)^T (+ bias on every row), x and y bf16 row-major (row m at x + m K, y + m N), same
  * weight formats, pointer rules and codes as the per-format calls (kind 0 bf16, 1 fp8, 2 int4, 3 int4_asym; scales /

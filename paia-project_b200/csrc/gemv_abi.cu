@@ -8,6 +8,7 @@
 // (CUDA-graph capturable). Its only static state is a per-device cache of SM counts and occupancies.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -314,6 +315,22 @@ const Variant* tp_instance(int fmt, const Params& p, Variant* out) {
     return nullptr;
 }
 
+// The rotary-epilogue instance of the same decodes, in the same order (the first one whose plan fits).
+const Variant* rope_instance(int fmt, const Params& p, Variant* out) {
+    static const int maths[4][2] = {{5, 0}, {8, 5}, {7, 5}, {7, 5}};
+    for (int k = 0; k < 2; ++k) {
+        const int math = maths[fmt][k];
+        if (!math) break;
+        const Variant* inst = tma_rope(fmt, math);
+        if (!inst) continue;
+        long long G = 0;
+        *out = *inst;
+        const LaunchOpts o{0, 0};
+        if (launch_variant(*out, p, o, nullptr, &G) == 0) return out;
+    }
+    return nullptr;
+}
+
 }  // namespace pb2tp
 
 
@@ -577,6 +594,37 @@ int paia_gemv_tp_ctas(int kind, int N_local, int K) {
     const LaunchOpts o{0, 0};
     if (launch_variant(v, p, o, nullptr, &G)) return -2;
     return (int)G;
+}
+
+// ------------------------------------------------------------------ rotary embedding fused into the epilogue
+
+int paia_gemv_rope(int kind, const void* Wq, const void* scales, const void* zeros, const void* x, const void* bias,
+                   void* y, int N, int K, int rope_rows, int head_dim, float pos, float theta, void* stream) {
+    if (kind < 0 || kind > 3) return -2;
+    const int rc = check_args(kind, Wq, scales, zeros, x, bias, y, N, K);
+    if (rc) return rc;
+    if ((N & 1) || head_dim < 2 || (head_dim & 1) || rope_rows < 0 || rope_rows > N || rope_rows % head_dim ||
+        !(theta > 0.f) || !(pos >= 0.f))
+        return -2;
+    Params p{};
+    p.W = static_cast<const uint8_t*>(Wq);
+    p.s = scales;
+    p.z = zeros;
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.bias = static_cast<const __nv_bfloat16*>(bias);
+    p.y = static_cast<__nv_bfloat16*>(y);
+    p.N = N;
+    p.K = K;
+    p.nchunk = row_bytes(kind, K) / 16;
+    p.groups = K / 128;
+    p.rope_rows = rope_rows;
+    p.rope_hd = head_dim;
+    p.rope_pos = pos;
+    p.rope_log2_theta = log2f(theta);
+    Variant v;
+    if (!pb2tp::rope_instance(kind, p, &v)) return -2;        // the rotary instance of the format's default decode
+    const LaunchOpts o{0, 0};
+    return launch_variant(v, p, o, static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------------ batched x (M > 1)

@@ -101,6 +101,12 @@ struct Params {
     // and waits later. Every CTA counts itself in on [kTpReaders] once it has read the epoch, and in this form CTA 0
     // advances the epoch only after all of them have.
     int tp_world, tp_off, tp_rank, tp_defer;
+    // Rotary embedding fused into the epilogue (single GEMV, rope_rows > 0): rows [0, rope_rows) are q and k heads of
+    // rope_hd rows each, stored pair-interleaved (row 2i + h of a head holds dimension i + h rope_hd / 2); the epilogue
+    // rotates each pair by pos * theta^(-2i / rope_hd) and stores dimension d of the head at its natural place. CTA
+    // row ranges then start on even rows, so a pair never straddles two tiles.
+    int rope_rows, rope_hd;
+    float rope_pos, rope_log2_theta;
     __nv_bfloat16* tp_y[8];
     unsigned int* tp_flag[8];
     // Layer mode (TMA kernels; nops = 0: off, the single GEMV above). One persistent cooperative launch runs ops

@@ -160,6 +160,7 @@ const Variant* find_instance(int fmt, int R, int U, int W, int math);
 const Variant* mma_instances(int fmt, int math, int* n);
 const Variant* tma_instances(int fmt, int math, int* n);
 const Variant* tma_public(int fmt, int* n);                  // the TMA variants appended to each format's table
+const Variant* tma_rope(int fmt, int math);                 // the rotary-epilogue instance of (format, math)
 int tma_device_error(int clear);
 int launch_tp_exchange(unsigned int* const* flag_all, int world, int rank, cudaStream_t st);
 

@@ -34,8 +34,14 @@
 //             of op j - 1 (a per-op completion counter) before they stage x of op j.
 //   waits     every wait gives up after ~2 s (%globaltimer), records an error code that paia_gemv_device_error()
 //             reports, and carries on without waiting, so a fault can never hang the GPU; once one wait has given
-//             up, every wait that has run for 1 ms gives up at once, and the producer keeps the CTA alive 200 us for
-//             its copies in flight before it exits.
+//             up, every wait that has run for 1 ms gives up at once. Only the byte-counted `full` barriers can be
+//             broken by a warp out of step (one more arrival on a phase whose bytes are in flight); a consumer warp
+//             releases a slot only after it saw the slot's `full` phase complete, so the producer re-arms only
+//             phases that completed, and stops arriving at its first failed wait (keeping the CTA alive 200 us for
+//             its copies in flight). The other barriers count arrivals only, which a warp out of step cannot
+//             break; its results are garbage and the error code says so.
+//   rope      an instance with ROPE = true rotates q / k row pairs in the epilogue (paia_gemv_rope); the other
+//             instances carry no rotary code.
 //   tp        row-sharded tensor parallelism: the epilogue stores every output into every rank's y over NVLink; the
 //             ranks count calls started and CTAs finished in each other's counter blocks, and CTA 0 waits until every
 //             rank's CTAs are done, so a rank's y is complete when its grid ends (tp_enter / tp_leave).
@@ -570,6 +576,12 @@ __device__ __forceinline__ void tma_steps_i4_bat(float (&acc)[4], const uint8_t*
     }
 }
 
+// First row of CTA c (c = gridDim.x: N): equal shares; even rows when the rotary epilogue pairs adjacent rows.
+__device__ __forceinline__ int tma_row_begin(const Params& p, int N, unsigned int c) {
+    const int r = (int)((long long)c * N / gridDim.x);
+    return (p.rope_rows > 0 && c < gridDim.x) ? (r & ~1) : r;
+}
+
 // Op j of the launch: the single GEMV of Params (nops == 0) or the layer list.
 __device__ __forceinline__ GemvOp tma_op(const Params& p, int j) {
     if (p.op_table) return p.op_table[j];
@@ -703,7 +715,7 @@ __global__ void tp_exchange_kernel(const __grid_constant__ TpExchangeArgs a) {
 // BAT: batched x (p.xm rows, 1..8): x row m rides in MMA column m (lanes of group g read x row g), every D element
 // is a (weight row, x row) output, partial buffers hold 16 rows x 8 columns per warp, and y row m is written at
 // y + m ldy. Decodes with a per-column fold only: BF16, FP8 DEC 0 (cvt to f16, x scaled per row), INT4 DEC 0.
-template <int F, int NC, int U, int DEC = 0, bool BAT = false>
+template <int F, int NC, int U, int DEC = 0, bool BAT = false, bool ROPE = false>
 __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid_constant__ Params p) {
     constexpr bool I4 = (F == kINT4 || F == kINT4A);
     static_assert(!BAT || DEC == 0, "batched x uses the per-column decodes");
@@ -736,8 +748,9 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     if (tid == 0) {
-        // full: the producer's expect_tx arrival, 32 lanes' cp.async arrivals and its closing arrival
-        for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 34); mbar_init(&empty[s], NC); }
+        // full: INT4 the producer's expect_tx arrival, 32 lanes' cp.async arrivals (metadata) and its closing
+        // arrival; BF16 / FP8 (bulk copies only) the expect_tx arrival alone
+        for (int s = 0; s < ST; ++s) { mbar_init(&full[s], I4 ? 34 : 1); mbar_init(&empty[s], NC); }
         for (int b = 0; b < NB; ++b) { mbar_init(&tdone[b], NC); mbar_init(&pfree[b], 1); }
         mbar_init(xready, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -753,15 +766,24 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const bool tensor = p.tmap_ok && p.nops == 0 && (smem_addr(ring) & 127u) == 0;
         int s = 0, g = 0;                                     // ring slot, stage count over all ops
         uint32_t ph = 0;                                      // parity of the slot's previous release
-        bool live = true;                                     // false once a wait gave up: issue nothing more
-        for (int jo = 0; jo < nops && live; ++jo) {
+        // Lane 0's slot waits decide whether the warp still refills: a consumer warp releases a slot only after its
+        // own wait saw the slot's `full` phase complete, so a successful `empty` wait proves that phase complete
+        // and re-arming it is safe. Once an `empty` wait gives up, that is no longer known (a `full` phase can sit
+        // at zero pending arrivals while its bytes are in flight, and one more arrival would take the count below
+        // zero), so lane 0 arrives on nothing more, and the other lanes stop at the next point where they learn
+        // it: INT4 before their metadata arrivals of the same stage, BF16 / FP8 (no arrivals but lane 0's) one
+        // stage later, off the copy-issue path, so at most one stage's bytes land on a phase lane 0 did not arm (its
+        // transaction count stays within range). Every other barrier counts arrivals only, which a warp put out of
+        // step by a failed wait cannot break.
+        bool live = true;
+        for (int jo = 0; jo < nops; ++jo) {
             const GemvOp op = tma_op(p, jo);
             const int NCH = op.nch, KC = op.kc, RS = op.rs, CS = KC >> 6;
             const bool dense = !p.tlayout && tma_blocked(NCH, KC, RS);   // short whole rows: one copy per 8-row block
             const int S = (op.nchunk + 3) >> 2;
             const size_t rowbytes = (size_t)op.nchunk * 16;
-            const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
-            const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
+            const int rb = tma_row_begin(p, op.N, blockIdx.x);
+            const int re = tma_row_begin(p, op.N, blockIdx.x + 1);
             const int nst = ((re - rb + 15) >> 4) * NCH;
             const long long NG = (long long)op.N * op.groups;
             // INT4 whole-row stages whose scale (zero) runs start and end on 16-byte boundaries: one bulk copy per
@@ -779,17 +801,12 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
                 const uint32_t mbytes = meta_bulk ? (uint32_t)(2 * nrows * op.groups) : 0u;   // per metadata array
                 // x is read right after the dependency wait: streaming only `pre` stages until it is staged keeps the
-                // x loads from queueing behind a whole ring of this SM's copies. A wait that gives up stops the
-                // producer: refilling a slot whose consumers never released it would arrive on a barrier phase more
-                // often than it expects.
-                bool ok = true;
-                if (lane == 0) {
-                    if (g == pre) ok = mbar_wait(xready, 0, 5);
-                    if (ok && g >= ST) ok = mbar_wait(&empty[s], ph, 1);
+                // x loads from queueing behind a whole ring of this SM's copies.
+                if (lane == 0 && live) {
+                    if (g == pre) mbar_wait(xready, 0, 5);
+                    if (g >= ST) live = mbar_wait(&empty[s], ph, 1);
                 }
-                live = __shfl_sync(0xffffffffu, ok, 0);
-                if (!live) break;
-                if (lane == 0) {
+                if (lane == 0 && live) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before copies
                     const uint32_t wbytes = (tensor && nrows == 16) ? 16u * (uint32_t)RS : (uint32_t)nrows * bytes;
                     mbar_arrive_expect_tx(&full[s], wbytes + (F == kINT4A ? 2 : 1) * mbytes);
@@ -804,7 +821,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 }
                 __syncwarp();                                 // the slot is free and its byte count announced
                 uint8_t* sdst = ring + (size_t)s * p.st_bytes;
-                if (dense) {                                  // rows 8b .. 8b + 7 of the tile: one copy per block
+                if (!live) {
+                } else if (dense) {                                  // rows 8b .. 8b + 7 of the tile: one copy per block
                     if (lane < 2 && nrows > 8 * lane) {
                         const int nb = nrows - 8 * lane < 8 ? nrows - 8 * lane : 8;
                         bulk_copy_g2s_ef(sdst + (size_t)lane * (8 * RS + 64), op.W + (size_t)(r0 + 8 * lane) * rowbytes,
@@ -817,7 +835,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                                      op.W + (size_t)(r0 + lane) * rowbytes + (size_t)j * KC, bytes, &full[s], wpol);
                 }
                 uint8_t* ms = meta + (size_t)s * MB;
-                if constexpr (I4) {
+                if (!live) {
+                } else if constexpr (I4) {
                     uint16_t* msc = reinterpret_cast<uint16_t*>(ms + 112);
                     const uint16_t* sa = reinterpret_cast<const uint16_t*>(op.s);
                     const uint16_t* za = reinterpret_cast<const uint16_t*>(op.z);
@@ -848,9 +867,12 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                         }
                     }
                 }
-                cp_async_arrive(&full[s]);
-                __syncwarp();                                 // plain-load halves stored before the closing arrival
-                if (lane == 0) mbar_arrive(&full[s]);
+                live = __shfl_sync(0xffffffffu, live, 0);     // lane 0's status (see above)
+                if constexpr (I4) {
+                    if (live) cp_async_arrive(&full[s]);
+                    __syncwarp();                             // plain-load halves stored before the closing arrival
+                    if (lane == 0 && live) mbar_arrive(&full[s]);
+                }
                 if (++s == ST) { s = 0; if (g >= ST) ph ^= 1u; }    // waits from the second pass on: parity 0, 1, 0, ...
                 if (++j == NCH) { j = 0; ++t; }
             }
@@ -874,11 +896,10 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const unsigned int tp_e = p.tp_world > 0 ? tp_enter(p, lane) : 0u;
         int b = 0;
         uint32_t bph = 0;
-        bool live = true;                                     // false once a wait gave up: no reads, no arrivals
         for (int jo = 0; jo < nops; ++jo) {
             const GemvOp op = tma_op(p, jo);
-            const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
-            const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
+            const int rb = tma_row_begin(p, op.N, blockIdx.x);
+            const int re = tma_row_begin(p, op.N, blockIdx.x + 1);
             const int T = (re - rb + 15) >> 4;
             const float* xsc = xscale + 4 * (jo & 1);
             for (int t = 0; t < T; ++t) {
@@ -889,9 +910,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     if constexpr (F == kFP8) rs = ld_f32(reinterpret_cast<const float*>(op.s) + row);
                     if (op.bias) rbias = __uint_as_float((uint32_t)ld_u16(op.bias + row) << 16);
                 }
-                live = __all_sync(0xffffffffu, live && mbar_wait(&tdone[b], bph, 3));
-                if (!live) {
-                } else if constexpr (BAT) {
+                mbar_wait(&tdone[b], bph, 3);
+                if constexpr (BAT) {
                     // 16 rows x XM x rows: lane pairs (row r, x row m); row scale first, then x row m's scale
                     const float* buf = part + (size_t)b * NC * 16 * 8;
                     for (int idx = lane; idx < 16 * XM; idx += 32) {
@@ -907,28 +927,45 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                             op.y[(size_t)m * p.ldy + rowb] = __float2bfloat16_rn(out);
                         }
                     }
-                } else if (mine) {
-                    const float* buf = part + (size_t)b * NC * 16;
-                    float total = 0.f;
+                } else {
+                    float val = 0.f;
+                    if (mine) {
+                        const float* buf = part + (size_t)b * NC * 16;
+                        float total = 0.f;
 #pragma unroll
-                    for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
-                    // row scale first, then the x scale (products that only the row scale keeps finite stay finite)
-                    float out = total;
-                    if constexpr (F == kFP8)                  // row scale, then 2^e (a normal power of two)
-                        out = out * rs * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
-                    if constexpr (I4 && DEC == 1)             // x was staged as x * 2^-e
-                        out = out * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
-                    if constexpr (I4 && DEC == 2)             // x was staged as integers x * 2^s
-                        out = out * xsc[1];
-                    const __nv_bfloat16 v = __float2bfloat16_rn(out + rbias);
-                    if (p.tp_world == 0) {
-                        op.y[row] = v;
-                    } else {
-                        for (int r = 0; r < p.tp_world; ++r) p.tp_y[r][p.tp_off + row] = v;   // peer stores
+                        for (int w = 0; w < NC; ++w) total += buf[w * 16 + lane];
+                        // row scale first, then the x scale (products only the row scale keeps finite stay finite)
+                        float out = total;
+                        if constexpr (F == kFP8)              // row scale, then 2^e (a normal power of two)
+                            out = out * rs * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
+                        if constexpr (I4 && DEC == 1)         // x was staged as x * 2^-e
+                            out = out * __uint_as_float((uint32_t)(__float_as_int(xsc[0]) + 127) << 23);
+                        if constexpr (I4 && DEC == 2)         // x was staged as integers x * 2^s
+                            out = out * xsc[1];
+                        val = out + rbias;
+                    }
+                    int orow = row;
+                    if constexpr (ROPE) {                     // rotary pairs sit in adjacent lanes (even tile starts)
+                        const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+                        if (mine && row < p.rope_rows) {
+                            const int hd = p.rope_hd, jh = row % hd, i = jh >> 1;
+                            float sn, cs;
+                            sincosf(p.rope_pos * exp2f(-(float)(2 * i) / (float)hd * p.rope_log2_theta), &sn, &cs);
+                            val = (jh & 1) ? fmaf(val, cs, partner * sn) : fmaf(val, cs, -(partner * sn));
+                            orow = row - jh + i + (jh & 1) * (hd >> 1);
+                        }
+                    }
+                    if (mine) {
+                        const __nv_bfloat16 v = __float2bfloat16_rn(val);
+                        if (p.tp_world == 0) {
+                            op.y[orow] = v;
+                        } else {
+                            for (int r = 0; r < p.tp_world; ++r) p.tp_y[r][p.tp_off + row] = v;   // peer stores
+                        }
                     }
                 }
                 __syncwarp();
-                if (live && lane == 0) mbar_arrive(&pfree[b]);
+                if (lane == 0) mbar_arrive(&pfree[b]);
                 if (++b == NB) { b = 0; bph ^= 1u; }
             }
             if (p.nops > 0) {
@@ -966,8 +1003,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     float acc0 = 0.f, acc1 = 0.f;
     float acc4[4] = {0.f, 0.f, 0.f, 0.f};                     // batched INT4: rows g, g + 8 x columns 2c, 2c + 1
     int s = 0, b = 0, tg = 0;                                 // ring slot, partial buffer, tiles over all ops
-    bool live = true;                                         // false once one of this warp's waits gave up
     uint32_t ph = 0, bph = 0;
+    bool seen = true;                                         // every `full` wait of this lane saw its phase complete
     for (int jo = 0; jo < nops; ++jo) {
         const GemvOp op = tma_op(p, jo);
         if (jo == 0) {
@@ -986,8 +1023,8 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const int SF = op.nchunk >> 2;                        // steps whose four 16-byte chunks are all in the row
         const int Kp = tma_kx<F>(op.K);
         const int xps = x_plane_stride<F, DEC>(Kp);           // byte planes of x (FP8 DEC 3, INT4 DEC 2)
-        const int rb = (int)((long long)blockIdx.x * op.N / gridDim.x);
-        const int re = (int)((long long)(blockIdx.x + 1) * op.N / gridDim.x);
+        const int rb = tma_row_begin(p, op.N, blockIdx.x);
+        const int re = tma_row_begin(p, op.N, blockIdx.x + 1);
         const int nst = ((re - rb + 15) >> 4) * NCH;
         if (nst > 0) {                                        // CTA-uniform: a CTA without rows of the op skips x
             if constexpr (BAT) {
@@ -1021,9 +1058,10 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         for (int i = 0; i < nst; ++i) {
             const int r0 = rb + 16 * t;
             const bool last = j == NCH - 1;
-            // once a wait gave up the warp stays in step with the loop (and with the named barriers of layer mode)
-            // but reads no stage and arrives on no barrier: no phase gets more arrivals than it expects
-            live = __all_sync(0xffffffffu, live && mbar_wait(&full[s], ph, 2));
+            // a wait that gave up leaves the warp out of step but in the loop (and in the named barriers of layer
+            // mode), reading stages that may be in flight; its lane 0 then releases no slot, so the producer never
+            // re-arms a `full` phase it cannot prove complete. Lane-local: no vote on the stage loop's path.
+            seen = seen && mbar_wait(&full[s], ph, 2);
             const int nsteps = last ? S - j * CS : CS;
             const int sa0 = warp * nsteps / NC, sb0 = (warp + 1) * nsteps / NC;
             const uint8_t* st = ring + (size_t)s * p.st_bytes;
@@ -1054,7 +1092,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
             }
             const int gb = j * CS;                            // global step of stage-local step 0
             const int sfull = SF - gb < sb0 ? SF - gb : sb0;  // steps below sfull are whole
-            int sl = live ? sa0 : sb0;                        // a warp that gave up skips the stage's steps
+            int sl = sa0;
             if constexpr (BAT && I4) {
 #pragma unroll 1
                 for (; sl + U <= sfull; sl += U)
@@ -1115,12 +1153,10 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     }
                     A.zero();
                 }
-                if (live && tg >= NB)                          // the epilogue warp has read tile tg - NB
-                    live = __all_sync(0xffffffffu, mbar_wait(&pfree[b], bph ^ 1u, 4));
+                if (tg >= NB) mbar_wait(&pfree[b], bph ^ 1u, 4);   // the epilogue warp has read tile tg - NB
                 ++tg;
                 float* buf = part + (size_t)b * NC * 16 * PC;
-                if (!live) {
-                } else if constexpr (BAT) {
+                if constexpr (BAT) {
                     float* r0b = buf + (warp * 16 + m0) * 8 + 2 * c;
                     float* r1b = buf + (warp * 16 + m1) * 8 + 2 * c;
                     r0b[0] = sb[0]; r0b[1] = sb[1]; r1b[0] = sb[2]; r1b[1] = sb[3];
@@ -1128,11 +1164,11 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                     buf[warp * 16 + m0] = s0; buf[warp * 16 + m1] = s1;
                 }
                 __syncwarp();
-                if (live && lane == 0) mbar_arrive(&tdone[b]); // release: this warp's partials of the tile
+                if (lane == 0) mbar_arrive(&tdone[b]);         // release: this warp's partials of the tile
                 if (++b == NB) { b = 0; bph ^= 1u; }
             }
             __syncwarp();
-            if (live && lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0 && seen) mbar_arrive(&empty[s]);
             if (++s == ST) { s = 0; ph ^= 1u; }
             if (++j == NCH) { j = 0; ++t; }
         }

@@ -50,7 +50,20 @@ static const Variant kPubInt4a[] = {PB2_TP_NC(kINT4A, 7, 2)};
 #undef PB2_TP_H
 #undef PB2_TP
 
+// The rotary-epilogue instances (paia_gemv_rope): W = 8, U = 2, PDL on, per format its default decode and the
+// fallback one. Only these carry the rotary code, so the other instances' epilogue stays as lean as before.
+#define PB2_ROPE(F, M, DEC) {0, 2, 8, 0, 1, M, &gemv_tma_kernel<F, 8, 2, DEC, false, true>, nullptr, &tma_prep<F, 8, DEC>},
+static const Variant kRope[] = {PB2_ROPE(kBF16, 5, 0) PB2_ROPE(kFP8, 8, 3) PB2_ROPE(kFP8, 5, 0)
+                                PB2_ROPE(kINT4, 7, 2) PB2_ROPE(kINT4, 5, 0) PB2_ROPE(kINT4A, 7, 2) PB2_ROPE(kINT4A, 5, 0)};
+static const int kRopeFmt[] = {kBF16, kFP8, kFP8, kINT4, kINT4, kINT4A, kINT4A};
+#undef PB2_ROPE
+
 #define PB2_N(t) (int)(sizeof(t) / sizeof(t[0]))
+const Variant* tma_rope(int fmt, int math) {
+    for (int i = 0; i < PB2_N(kRope); ++i)
+        if (kRopeFmt[i] == fmt && kRope[i].math == math) return &kRope[i];
+    return nullptr;
+}
 const Variant* tma_public(int fmt, int* n) {
     switch (fmt) {
         case kBF16: *n = PB2_N(kPubBf16); return kPubBf16;

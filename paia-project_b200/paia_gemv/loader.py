@@ -84,6 +84,8 @@ class GemvLib:
         lib.paia_gemv_tp_ctas.argtypes = [I, I, I]
         lib.paia_gemv_tp_deferred.restype = I
         lib.paia_gemv_tp_deferred.argtypes = [I, P, P, P, P, P, ctypes.POINTER(P), ctypes.POINTER(P), I, I, I, I, P]
+        lib.paia_gemv_rope.restype = I
+        lib.paia_gemv_rope.argtypes = [I, P, P, P, P, P, P, I, I, I, I, ctypes.c_float, ctypes.c_float, P]
         lib.paia_gemv_tp_exchange.restype = I
         lib.paia_gemv_tp_exchange.argtypes = [ctypes.POINTER(P), I, I, P]
         lib.paia_gemv_tp_alloc.restype = I
@@ -247,6 +249,14 @@ class GemvLib:
         self._check(self._lib.paia_gemv_tp_deferred(_KINDS[kind], Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr,
                                                     y_ptrs, flag_ptrs, world, rank, N_local, K, self._st(stream)),
                     "paia_gemv_tp_deferred")
+
+    def rope(self, kind, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K, rope_rows, head_dim, pos, theta,
+             stream=None):
+        """y = RoPE(W x + bias) of a fused QKV projection whose first rope_rows rows are in pair-interleaved order
+        (quant.rope_pair_rows); y comes out in the natural order."""
+        self._check(self._lib.paia_gemv_rope(_KINDS[kind], Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K,
+                                             rope_rows, head_dim, float(pos), float(theta), self._st(stream)),
+                    "paia_gemv_rope")
 
     def tp_exchange(self, xflag_ptrs, world, rank, stream=None):
         self._check(self._lib.paia_gemv_tp_exchange(xflag_ptrs, world, rank, self._st(stream)), "paia_gemv_tp_exchange")

@@ -80,3 +80,19 @@ def dequant_int4_asym(packed, scale_bf16, zero_bf16):
     s = scale_bf16.float().repeat_interleave(GROUP, dim=1)
     z = zero_bf16.float().repeat_interleave(GROUP, dim=1)
     return n * s + z
+
+
+def rope_pair_rows(t, rope_rows, head_dim):
+    """Rows of a fused QKV projection (weights, scales, zeros or bias; any format, rows first) reordered for the
+    rotary epilogue (paia_gemv_rope): within each of the rope_rows // head_dim q/k heads, new row 2i + h holds old row
+    i + h head_dim / 2 (the two halves a rotate-half RoPE pairs become adjacent); rows past rope_rows stay."""
+    import torch as _torch
+    half = head_dim // 2
+    j = _torch.arange(rope_rows, device=t.device)
+    base = j - j % head_dim
+    jh = j % head_dim
+    src = base + (jh >> 1) + (jh & 1) * half
+    out = t.clone()
+    out[:rope_rows] = t[src]
+    return out
+

@@ -484,3 +484,40 @@ def test_tma_tensor_copies_equal_row_copies(L, kind, math):
         assert np.array_equal(outs[0], outs[1]), (kind, N, K)
         check(ops, outs[1], ops.oracle(with_bias=True)[0], f"tensor copies {kind} {N}x{K}")
     assert L.device_error(1) == 0
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp8", "int4", "int4_asym"])
+def test_rope_epilogue_matches_oracle(L, kind):
+    """paia_gemv_rope: a Qwen-like fused QKV (28 q + 4 k heads of 128 rows rotated, 4 v heads not) with bias, rows
+    pair-interleaved by quant.rope_pair_rows; against the oracle's fp64 GEMV on the permuted bytes, un-permuted,
+    rotated in fp64 (rotate-half, theta 1e6) and rounded once to bf16; a position 0 call equals the plain GEMV."""
+    hd, nq, nkv = 128, 28, 4
+    N, K = (nq + 2 * nkv) * hd, 3584
+    rope_rows = (nq + nkv) * hd
+    ops = make(kind, N, K, seed=31, with_bias=True)
+    for name in ("W", "s", "z", "bias"):
+        t = getattr(ops, name)
+        if t is not None:
+            setattr(ops, name, quant.rope_pair_rows(t, rope_rows, hd).contiguous())
+    _, lin = ops.oracle(with_bias=True)                    # fp64, permuted row order
+    j = np.arange(N)
+    nat = j.copy()
+    jh = j[:rope_rows] % hd
+    nat[:rope_rows] = j[:rope_rows] - jh + (jh >> 1) + (jh & 1) * (hd // 2)
+    y_nat = np.empty(N)
+    y_nat[nat] = lin                                       # natural order: dimension d of each head at its row
+    for pos, theta in ((0.0, 1e6), (1234.0, 1e6), (77.0, 5e5)):
+        want = y_nat.copy()
+        i = np.arange(hd // 2)
+        ang = pos * theta ** (-2.0 * i / hd)
+        for h in range(rope_rows // hd):
+            a, b = y_nat[h * hd:h * hd + hd // 2], y_nat[h * hd + hd // 2:(h + 1) * hd]
+            want[h * hd:h * hd + hd // 2] = a * np.cos(ang) - b * np.sin(ang)
+            want[h * hd + hd // 2:(h + 1) * hd] = b * np.cos(ang) + a * np.sin(ang)
+        ops.nan_fill()
+        p_ = lambda t: None if t is None else t.data_ptr()                 # noqa: E731
+        L.rope(kind, p_(ops.W), p_(ops.s), p_(ops.z), ops.x.data_ptr(), ops.bias.data_ptr(), ops.y.data_ptr(), N, K,
+               rope_rows, hd, pos, theta)
+        torch.cuda.synchronize()
+        check(ops, bits(ops.y), O.f64_to_bf16(want), f"rope {kind} pos {pos}")
+    assert L.device_error(1) == 0
