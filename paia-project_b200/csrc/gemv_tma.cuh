@@ -146,8 +146,10 @@ __device__ __forceinline__ void u16_block_copy(uint16_t* dst, const uint16_t* a,
 
 constexpr int kTmaMaxRing = 16;        // ring stages at most
 constexpr int kTmaMaxParts = kTmaMaxRing + 1;   // tile-partial buffers at most
-// mbarriers: full[16], empty[16], tile_done[17], part_free[17], x_ready (67 x 8 bytes, padded to 640)
+// mbarriers: full[16], empty[16], tile_done[17], part_free[17], x_ready (67 x 8 bytes), the producer's stop flag
+// (4 bytes), padded to 640
 constexpr int kTmaBarBytes = 640;
+static_assert((2 * kTmaMaxRing + 2 * kTmaMaxParts + 1) * 8 + 4 <= kTmaBarBytes, "barrier region");
 constexpr int kTmaTailBytes = 160;     // x scale of two ops (2 x 4 floats) + x staging scratch (32 floats)
 
 // Metadata slot of a stage (bytes): INT4 scales and (INT4A) zeros at 112, 16 rows x tma_meta_row(CS) halves each
@@ -733,6 +735,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     uint64_t* tdone = empty + kTmaMaxRing;                    // tile t's NC partials are in buffer t mod NB
     uint64_t* pfree = tdone + kTmaMaxParts;                   // the epilogue warp has read buffer t mod NB
     uint64_t* xready = pfree + kTmaMaxParts;                  // the consumers have staged x (op 0)
+    volatile int* pstop = reinterpret_cast<volatile int*>(xready + 1);   // producer lane 0 stopped (BF16 / FP8)
     uint8_t* ring = smem + kTmaBarBytes;
     uint8_t* meta = ring + (size_t)ST * p.st_bytes;
     uint16_t* xs = reinterpret_cast<uint16_t*>(meta + (size_t)ST * MB);
@@ -753,6 +756,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         for (int s = 0; s < ST; ++s) { mbar_init(&full[s], I4 ? 34 : 1); mbar_init(&empty[s], NC); }
         for (int b = 0; b < NB; ++b) { mbar_init(&tdone[b], NC); mbar_init(&pfree[b], 1); }
         mbar_init(xready, 1);
+        *pstop = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -771,10 +775,10 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         // and re-arming it is safe. Once an `empty` wait gives up, that is no longer known (a `full` phase can sit
         // at zero pending arrivals while its bytes are in flight, and one more arrival would take the count below
         // zero), so lane 0 arrives on nothing more, and the other lanes stop at the next point where they learn
-        // it: INT4 before their metadata arrivals of the same stage, BF16 / FP8 (no arrivals but lane 0's) one
-        // stage later, off the copy-issue path, so at most one stage's bytes land on a phase lane 0 did not arm (its
-        // transaction count stays within range). Every other barrier counts arrivals only, which a warp put out of
-        // step by a failed wait cannot break.
+        // it: INT4 (a shuffle) before their metadata arrivals of the same stage; BF16 / FP8 (no arrivals but lane
+        // 0's) from a shared flag that they read at the end of each stage, off the copy-issue path, so at most one
+        // stage's bytes land on a phase lane 0 did not arm (its transaction count stays within range). Every other
+        // barrier counts arrivals only, which a warp put out of step by a failed wait cannot break.
         bool live = true;
         for (int jo = 0; jo < nops; ++jo) {
             const GemvOp op = tma_op(p, jo);
@@ -805,6 +809,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 if (lane == 0 && live) {
                     if (g == pre) mbar_wait(xready, 0, 5);
                     if (g >= ST) live = mbar_wait(&empty[s], ph, 1);
+                    if (!I4 && !live) *pstop = 1;
                 }
                 if (lane == 0 && live) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // consumers' reads before copies
@@ -867,11 +872,13 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                         }
                     }
                 }
-                live = __shfl_sync(0xffffffffu, live, 0);     // lane 0's status (see above)
                 if constexpr (I4) {
+                    live = __shfl_sync(0xffffffffu, live, 0); // lane 0's status (see above)
                     if (live) cp_async_arrive(&full[s]);
                     __syncwarp();                             // plain-load halves stored before the closing arrival
                     if (lane == 0 && live) mbar_arrive(&full[s]);
+                } else {
+                    if (lane != 0 && live) live = *pstop == 0;   // written before this stage's __syncwarp
                 }
                 if (++s == ST) { s = 0; if (g >= ST) ph ^= 1u; }    // waits from the second pass on: parity 0, 1, 0, ...
                 if (++j == NCH) { j = 0; ++t; }
