@@ -145,7 +145,8 @@ int paia_gemv_variant_info_ex(int kind, int v, paia_gemv_variant_ex* out);
 /* Tuning entry point (the B200 analogue of the variant sweep of src/tools/dev_sweep_bf16.py): launch any compiled
  * kernel instance (R, U, W, math) of `kind` with explicit PDL (0/1), warps per row ks (0 = auto) and CTAs per SM
  * (0 = auto). TMA-fed instances (math >= 5): R = ring stages (<= 1: as many as fit) and ks = shared-memory share
- * (bits 0-7) | stages streamed before x is staged (bits 8-15) | full tiles as one tiled tensor copy per stage
+ * (bits 0-7) | x-first knob (bits 8-15: 0 auto, k in 1..254 streams k - 1 weight stages before the producer
+ * waits for the consumers' x loads, 255 streams the whole ring first) | full tiles as one tiled tensor copy per stage
  * instead of per-row bulk copies (bit 16; slower on every decode shape measured, kept for comparison).
  * s/z/bias as in the per-format entry points (unused ones may be NULL). -1 if no such instance exists. */
 int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks, int ctas_per_sm, const void* Wq,

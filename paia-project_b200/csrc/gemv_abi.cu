@@ -821,7 +821,7 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
     p.groups = K / 128;
     LaunchOpts o{ks, ctas_per_sm};
     if (math >= 5) {                        // TMA-fed kernels: R = ring stages (<= 1: auto), ks = shared-memory share
-        o.ring = R <= 1 ? 0 : R;            // (bits 0-7), stages streamed before x is staged (bits 8-15, 0 = all),
+        o.ring = R <= 1 ? 0 : R;            // (bits 0-7), stages streamed before the x loads (bits 8-15, LaunchOpts),
         o.share = ks & 0xFF;                // tiled tensor copies of full tiles (bit 16)
         o.pre = (ks >> 8) & 0xFF;
         o.tensor_on = (ks >> 16) & 1;

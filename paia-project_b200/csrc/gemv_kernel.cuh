@@ -62,6 +62,11 @@ struct GemvOp {
 };
 constexpr int kMaxOps = 6;             // ops carried in the kernel parameters
 // Tensor-parallel counter block of one rank (uint32 words): epoch, then per-source arrival and ready counts.
+// TMA kernels: weight stages streamed before the producer waits for the consumers to issue their x loads (so the x
+// loads, on the critical path after the dependency wait, do not queue behind a whole ring of copies). Measured within
+// one build through the launch knob (the same binary, so no code-layout effects): FP8 gate_up 20.8 -> 20.3 us, qkv
+// 7.29 -> 7.15, INT4 asym lm_head 52.3 -> 51.8, o 5.7 -> 5.5; ties elsewhere.
+constexpr int kTmaPreAuto = 1;
 constexpr int kTpEpoch = 0, kTpReaders = 4, kTpComplete = 5, kTpArrive = 8, kTpReady = 16, kTpCounterWords = 32;
 constexpr int kMaxPlanOps = 4096;       // ops of a plan (device-memory op table)
 

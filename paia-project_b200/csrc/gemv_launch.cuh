@@ -31,7 +31,8 @@ struct LaunchOpts {
     int ring = 0;             // TMA kernels: ring stages (0 = as many as fit, else 2..16)
     int share = 0;            // TMA kernels: size the CTA for 1/share of the SM's shared memory (0 = 1: all of it);
                               // share 2 with one CTA per SM leaves room for the next kernel's CTA under PDL
-    int pre = 0;              // TMA kernels: stages streamed before x is staged (0 = the whole ring)
+    int pre = 0;              // TMA kernels: 0 = auto; k in 1..254: k - 1 stages streamed before the producer waits
+                              // for the consumers' x loads to be issued; 255: never wait (the whole ring first)
     int tensor_on = 0;        // TMA kernels: 1 = tiled tensor copies of full tiles (comparisons; slower, off by default)
 };
 
@@ -77,7 +78,7 @@ inline int plan_variant(const Variant& v, const Params& p_in, const LaunchOpts& 
         size_t cap = sm_smem_bytes() / share - (share > 1 ? 1024 : 0);
         if (cap > max_dyn_smem()) cap = max_dyn_smem();
         p.ring = o.ring;
-        p.pre = o.pre;
+        p.pre = o.pre == 0 ? kTmaPreAuto : (o.pre >= 255 ? -1 : o.pre - 1);
         p.tensor_on = o.tensor_on;
         smem = v.prep(p, cap);
     } else {

@@ -162,13 +162,21 @@ __device__ __forceinline__ uint4 x_block(const uint4* x4, int nx, int i) {
     return ld_x16(x4 + i);
 }
 
+// Called once by every thread as soon as its first round of x loads is issued (before their values are used): the
+// TMA kernel's producer holds most of its weight copies until then, so the x loads do not queue behind them.
+struct NoHook {
+    __device__ __forceinline__ void operator()() const {}
+};
+
 // R blocks per thread per round (R loads in flight); CACHE 1 keeps the first round's blocks in c[0 .. R), CACHE 2 takes
 // them from there. The map is taken by value: a stateful map (a cursor over its runs) restarts on every pass, and
 // sees q in increasing order within a thread.
-template <bool ACT, int CACHE, int R, typename Fn, typename Map>
-__device__ __forceinline__ void x_blocks_t(const XSrc& p, int tid, int nthr, int n0, Fn& fn, uint4* c, Map map) {
+template <bool ACT, int CACHE, int R, typename Fn, typename Map, typename Hook>
+__device__ __forceinline__ void x_blocks_t(const XSrc& p, int tid, int nthr, int n0, Fn& fn, uint4* c, Map map,
+                                           const Hook& hook) {
     const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
     const int nx = p.K / 8, n = map.count(n0);
+    if (tid >= n) hook();                                 // no blocks for this thread
     for (int i0 = tid, r = 0; i0 < n; i0 += R * nthr, ++r) {
         uint4 v[R];
         int ii[R];
@@ -180,24 +188,27 @@ __device__ __forceinline__ void x_blocks_t(const XSrc& p, int tid, int nthr, int
             else v[k] = ii[k] < nx ? x_block<ACT>(x4, nx, ii[k]) : make_uint4(0u, 0u, 0u, 0u);
             if (CACHE == 1 && r == 0) c[k] = v[k];
         }
+        if (r == 0) hook();
 #pragma unroll
         for (int k = 0; k < R; ++k)
             if (i0 + k * nthr < n) fn(ii[k], v[k]);
     }
 }
-template <int CACHE = 0, int R = 4, typename Fn, typename Map = XAll>
+template <int CACHE = 0, int R = 4, typename Fn, typename Map = XAll, typename Hook = NoHook>
 __device__ __forceinline__ void x_blocks(const XSrc& p, int tid, int nthr, int n0, Fn fn, uint4* c = nullptr,
-                                         Map map = Map()) {
-    if (p.act == kActSiluMul) x_blocks_t<true, CACHE, R>(p, tid, nthr, n0, fn, c, map);
-    else x_blocks_t<false, CACHE, R>(p, tid, nthr, n0, fn, c, map);
+                                         Map map = Map(), const Hook& hook = Hook()) {
+    if (p.act == kActSiluMul) x_blocks_t<true, CACHE, R>(p, tid, nthr, n0, fn, c, map, hook);
+    else x_blocks_t<false, CACHE, R>(p, tid, nthr, n0, fn, c, map, hook);
 }
 // As x_blocks, but every thread calls fn(i, v) in every round (i may be >= the staged length; v is then zero), so fn
 // may use warp shuffles; blocks q0 + tid of a round belong to consecutive lanes (with a Map, 16 consecutive q of a
 // 16-aligned run map to one 128-group: runs are whole groups).
-template <bool ACT, int CACHE, int R, typename Fn, typename Map>
-__device__ __forceinline__ void x_blocks_all_t(const XSrc& p, int tid, int nthr, int n0, Fn& fn, uint4* c, Map map) {
+template <bool ACT, int CACHE, int R, typename Fn, typename Map, typename Hook>
+__device__ __forceinline__ void x_blocks_all_t(const XSrc& p, int tid, int nthr, int n0, Fn& fn, uint4* c, Map map,
+                                               const Hook& hook) {
     const uint4* x4 = reinterpret_cast<const uint4*>(p.x);
     const int nx = p.K / 8, n = map.count(n0);
+    if (n <= 0) hook();
     for (int i0 = 0, r = 0; i0 < n; i0 += R * nthr, ++r) {
         uint4 v[R];
         int ii[R];
@@ -209,16 +220,17 @@ __device__ __forceinline__ void x_blocks_all_t(const XSrc& p, int tid, int nthr,
             else v[k] = ii[k] < nx ? x_block<ACT>(x4, nx, ii[k]) : make_uint4(0u, 0u, 0u, 0u);
             if (CACHE == 1 && r == 0) c[k] = v[k];
         }
+        if (r == 0) hook();
 #pragma unroll
         for (int k = 0; k < R; ++k)
             if (i0 + k * nthr < n) fn(ii[k], v[k]);
     }
 }
-template <int CACHE = 0, int R = 4, typename Fn, typename Map = XAll>
+template <int CACHE = 0, int R = 4, typename Fn, typename Map = XAll, typename Hook = NoHook>
 __device__ __forceinline__ void x_blocks_all(const XSrc& p, int tid, int nthr, int n0, Fn fn, uint4* c = nullptr,
-                                             Map map = Map()) {
-    if (p.act == kActSiluMul) x_blocks_all_t<true, CACHE, R>(p, tid, nthr, n0, fn, c, map);
-    else x_blocks_all_t<false, CACHE, R>(p, tid, nthr, n0, fn, c, map);
+                                             Map map = Map(), const Hook& hook = Hook()) {
+    if (p.act == kActSiluMul) x_blocks_all_t<true, CACHE, R>(p, tid, nthr, n0, fn, c, map, hook);
+    else x_blocks_all_t<false, CACHE, R>(p, tid, nthr, n0, fn, c, map, hook);
 }
 
 // Stage x for the tensor-core kernels (padded with zeros to Kpad): BF16 as is; FP8 as f16 scaled by 2^-e (e from the
@@ -227,14 +239,15 @@ __device__ __forceinline__ void x_blocks_all(const XSrc& p, int tid, int nthr, i
 // Called by `nthr` threads (thread index tid); `sync` is the barrier over exactly those threads; `scratch` holds
 // nthr/32 floats. Ends with x visible to the caller only after the caller's own barrier.
 // With a Map, only the mapped blocks are staged (and the max is taken over them). XR: blocks per thread per round.
-template <int F, int DEC, int GST = 1, int XR = 4, typename Sync, typename Map = XAll>
+template <int F, int DEC, int GST = 1, int XR = 4, typename Sync, typename Map = XAll, typename Hook = NoHook>
 __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum, float* xscale, float* scratch, int tid,
-                                        int nthr, Sync sync, const Map& map = Map()) {
+                                        int nthr, Sync sync, const Map& map = Map(), const Hook& issued = Hook()) {
     // INT4 group sums are written GST words apart (the integer path needs 8 words per group)
     static_assert(!(F == kINT4 || F == kINT4A) || DEC != 2 || GST == 8, "integer INT4 staging needs 8 words per group");
     const int Kp = p.kx ? p.kx : mma_kpad<F>(p.K);
     if constexpr (F == kBF16) {
-        x_blocks<0, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) { reinterpret_cast<uint4*>(xs)[i] = v; }, nullptr, map);   // K % 8 == 0
+        x_blocks<0, XR>(p, tid, nthr, Kp / 8, [&](int i, uint4 v) { reinterpret_cast<uint4*>(xs)[i] = v; },   // K % 8 == 0
+                        nullptr, map, issued);
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     } else if constexpr (F == kFP8 && DEC == 3) {
         // v = x * 2^-e (max|x| * 2^-e in [128, 256)) as four e4m3 terms in two exponent tiers, one byte plane each
@@ -249,7 +262,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }, xc, map);
+        }, xc, map, issued);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -300,7 +313,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }, xc, map);
+        }, xc, map, issued);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -357,7 +370,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
                 bad |= ((vv[j] & 0x7F800000u) == 0x7F800000u) || ((vv[j] & 0x7F80u) == 0x7F80u);
                 m = fmaxf(m, fmaxf(fabsf(bf_lo(vv[j])), fabsf(bf_hi(vv[j]))));
             }
-        }, xc, map);
+        }, xc, map, issued);
         if (__any_sync(0xffffffffu, bad)) m = __int_as_float(0x7F800000);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -446,7 +459,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
         x_blocks<1, XR>(p, tid, nthr, p.K / 8, [&](int, uint4 v) {
             m = fmaxf(m, fmaxf(fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))),
                                fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w))))));
-        }, xc, map);
+        }, xc, map, issued);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if ((tid & 31) == 0) scratch[tid >> 5] = m;
@@ -509,7 +522,7 @@ __device__ __forceinline__ void stage_x(const XSrc& p, uint16_t* xs, float* gsum
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);   // 16-lane groups
             if (i < nb && (i & 15) == 0) gsum[GST * (i >> 4)] = sum;
-        }, nullptr, map);
+        }, nullptr, map, issued);
         if (tid == 0) { xscale[0] = __int_as_float(0); xscale[1] = 1.f; }
     }
 }

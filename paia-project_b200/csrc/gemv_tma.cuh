@@ -59,6 +59,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* m, int count) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* m) {
     asm volatile("mbarrier.arrive.shared.b64 _, [%0];" :: "r"(smem_addr(m)) : "memory");
 }
+// Relaxed: orders nothing before it (used to say "my loads are issued" without waiting for them to complete).
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* m) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" :: "r"(smem_addr(m)) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* m, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" :: "r"(smem_addr(m)), "r"(bytes) : "memory");
 }
@@ -734,7 +738,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     uint64_t* empty = full + kTmaMaxRing;
     uint64_t* tdone = empty + kTmaMaxRing;                    // tile t's NC partials are in buffer t mod NB
     uint64_t* pfree = tdone + kTmaMaxParts;                   // the epilogue warp has read buffer t mod NB
-    uint64_t* xready = pfree + kTmaMaxParts;                  // the consumers have staged x (op 0)
+    uint64_t* xready = pfree + kTmaMaxParts;                  // every consumer thread has issued its x loads (op 0)
     volatile int* pstop = reinterpret_cast<volatile int*>(xready + 1);   // producer lane 0 stopped (BF16 / FP8)
     uint8_t* ring = smem + kTmaBarBytes;
     uint8_t* meta = ring + (size_t)ST * p.st_bytes;
@@ -755,7 +759,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         // arrival; BF16 / FP8 (bulk copies only) the expect_tx arrival alone
         for (int s = 0; s < ST; ++s) { mbar_init(&full[s], I4 ? 34 : 1); mbar_init(&empty[s], NC); }
         for (int b = 0; b < NB; ++b) { mbar_init(&tdone[b], NC); mbar_init(&pfree[b], 1); }
-        mbar_init(xready, 1);
+        mbar_init(xready, NC * 32);
         *pstop = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -764,7 +768,7 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
     if (warp == NC) {
         // ------------------------------------------------------------ producer warp
         // Streams every op's stages back to back: op j + 1's weights never wait for op j's x.
-        const int pre = (p.pre > 0 && p.pre < ST) ? p.pre : -1;    // -1: never wait
+        const int pre = (p.pre >= 0 && p.pre < ST) ? p.pre : -1;   // -1: never wait
         const uint64_t wpol = l2_evict_first();
         // tiled tensor copies land at 128-byte aligned stage addresses (stage sizes are multiples of 128)
         const bool tensor = p.tmap_ok && p.nops == 0 && (smem_addr(ring) & 127u) == 0;
@@ -804,8 +808,9 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
                 const int nsteps = last ? S - j * CS : CS;
                 const uint32_t bytes = last ? (uint32_t)(rowbytes - (size_t)j * KC) : (uint32_t)KC;
                 const uint32_t mbytes = meta_bulk ? (uint32_t)(2 * nrows * op.groups) : 0u;   // per metadata array
-                // x is read right after the dependency wait: streaming only `pre` stages until it is staged keeps the
-                // x loads from queueing behind a whole ring of this SM's copies.
+                // x is read right after the dependency wait, and its loads queue behind whatever this SM has in
+                // flight: the producer streams `pre` stages, then waits until every consumer thread has issued its
+                // first x loads before it fills the rest of the ring (the weights' latency then overlaps x staging).
                 if (lane == 0 && live) {
                     if (g == pre) mbar_wait(xready, 0, 5);
                     if (g >= ST) live = mbar_wait(&empty[s], ph, 1);
@@ -1033,23 +1038,26 @@ __global__ void __launch_bounds__((NC + 2) * 32, 1) gemv_tma_kernel(const __grid
         const int rb = tma_row_begin(p, op.N, blockIdx.x);
         const int re = tma_row_begin(p, op.N, blockIdx.x + 1);
         const int nst = ((re - rb + 15) >> 4) * NCH;
+        // op 0: every consumer thread tells the producer once its first x loads are issued (or at once without rows)
+        const auto issued = [&]() { if (jo == 0) mbar_arrive_relaxed(xready); };
         if (nst > 0) {                                        // CTA-uniform: a CTA without rows of the op skips x
             if constexpr (BAT) {
                 for (int m = 0; m < XM; ++m)                  // every x row: its own region, group sums and scale
                     stage_x<F, DEC, tma_gsum_words(DEC)>(
                         XSrc{op.x + (size_t)m * p.ldx, op.K, 0, Kp},
                         reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(xs) + (size_t)m * XROW), gsum + m * GR,
-                        xscale + 4 * m, xscr, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+                        xscale + 4 * m, xscr, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); }, XAll(),
+                        [&]() { if (m == 0) issued(); });
             } else {
                 stage_x<F, DEC, tma_gsum_words(DEC)>(XSrc{op.x, op.K, op.act, Kp}, xs, gsum, xscale + 4 * (jo & 1),
-                                                     xscr, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); });
+                                                     xscr, tid, NC * 32, [&]() { consumer_barrier(1, NC * 32); },
+                                                     XAll(), issued);
             }
             consumer_barrier(1, NC * 32);
+        } else {
+            issued();
         }
-        if (jo == 0 && tid == 0) {
-            launch_dependents();
-            mbar_arrive(xready);
-        }
+        if (jo == 0 && tid == 0) launch_dependents();
         const uint16_t* sa = reinterpret_cast<const uint16_t*>(op.s);
         const uint16_t* za = reinterpret_cast<const uint16_t*>(op.z);
         // batched: lanes of group g feed MMA column g with x row g (columns past the last row repeat it, unused)

@@ -232,8 +232,8 @@ class GemvLib:
     def launch_ex(self, kind, R, U, W, math, pdl, ks, ctas_per_sm, Wq_ptr, scales_ptr, zeros_ptr, x_ptr, bias_ptr,
                   y_ptr, N, K, stream=None):
         """Any compiled kernel instance (tuning and comparisons): math 0/1 CUDA-core, 2-4 register-fed MMA, 5-8
-        TMA-fed MMA (R = ring stages, 0 = auto; ks = shared-memory share | stages-before-x << 8 | tiled tensor copies
-        << 16)."""
+        TMA-fed MMA (R = ring stages, 0 = auto; ks = shared-memory share | x-first knob << 8 (0 auto, k: k - 1 weight
+        stages before the producer waits for the x loads, 255: the whole ring first) | tiled tensor copies << 16)."""
         self._check(self._lib.paia_gemv_launch_ex(_KINDS[kind], R, U, W, math, pdl, ks, ctas_per_sm, Wq_ptr,
                                                   scales_ptr, zeros_ptr, x_ptr, bias_ptr, y_ptr, N, K,
                                                   self._st(stream)), "paia_gemv_launch_ex")
