@@ -12,8 +12,9 @@ copies of its shards so the weights stream from HBM (>= 4 x L2).
 
 value   = full weight bytes (weights + scales / zeros of all four matrices) per step x steps / device time of the K
           steps (CUDA events around a graph replay, max over ranks), GB/s. Strong scaling: the work is fixed.
-e2e     = the same metric through the public API (GemvLib methods; ShardedGemv.fused on > 1 GPU) with a pinned x
-          copied in and every full y copied out each step, in stream order.
+e2e     = the same metric through the public API (GemvLib methods; ShardedGemv.deferred + TpExchange.run on > 1 GPU)
+          with a pinned x copied in and every full y copied out each step, the copies on a second stream overlapping
+          the next step's compute (all inside the timed region).
 roofline: the dominant kernel (FP8 lm_head rows of the rank): algorithmic bytes / per-launch device time.
 cpu_baseline: the reference's CPU path (weights dequantised once, per-call chunked fp32 matmul) on the host cores.
 --impl reference: that CPU path alone, as the reference arm (rank 0 only).
@@ -732,22 +733,39 @@ def run_main(args, rank, world, local_rank):
                        "all_gather_into_tensor (NCCL) on the compute stream, eager launches, max over ranks"}
 
     # e2e through the public API with host buffers: every step x copied in from pinned memory, the four ops called
-    # eagerly through the user-facing API (GemvLib methods; ShardedGemv.fused on > 1 GPU), every op's full y copied
-    # out to pinned memory, all in stream order on one stream; CUDA events, max over ranks
+    # eagerly through the user-facing API (GemvLib methods; ShardedGemv.deferred + TpExchange.run on > 1 GPU), every
+    # op's full y copied out to pinned memory; CUDA events, max over ranks. The copies run on a second stream, as a
+    # user overlaps them: step i's outputs go to the host while step i + 1 computes (its ops write the other rotation
+    # copy's y), and x of step i + n is copied in once step i's ops have read x_dev[i mod n]. Every copy of every
+    # timed step completes inside the timed region.
     x_host = torch.empty(x.numel(), dtype=torch.bfloat16).pin_memory()
     x_host.copy_(x.cpu())
-    y_host = [torch.empty(op.N, dtype=torch.bfloat16).pin_memory() for op in ops]
+    y_host = [[torch.empty(op.N, dtype=torch.bfloat16).pin_memory() for op in ops] for _ in range(n)]
     x_dev = [torch.empty_like(x) for _ in range(n)]
+    comp, cs = torch.cuda.current_stream(), torch.cuda.Stream()
+    ev_x = [torch.cuda.Event() for _ in range(n)]          # on cs: x_dev[c] loaded (and copy c's last outputs out)
+    ev_done = [torch.cuda.Event() for _ in range(n)]       # on comp: the ops of the step that used copy c are done
+
+    def load_x(c):
+        with torch.cuda.stream(cs):
+            x_dev[c].copy_(x_host, non_blocking=True)
+            ev_x[c].record(cs)
 
     def e2e_step(i):
         c = i % n
-        x_dev[c].copy_(x_host, non_blocking=True)
+        comp.wait_event(ev_x[c])                           # x in, and the previous outputs of copy c out
         ys = [op.api_call(c, x_dev[c]) for op in ops]
         if exchange is not None:
             exchange.run()
-        for y, yh in zip(ys, y_host):
-            yh.copy_(y, non_blocking=True)
+        ev_done[c].record(comp)
+        with torch.cuda.stream(cs):
+            cs.wait_event(ev_done[c])
+            for y, yh in zip(ys, y_host[c]):
+                yh.copy_(y, non_blocking=True)
+        load_x(c)                                          # x of step i + n
 
+    for c in range(n):
+        load_x(c)
     for i in range(max(3, args.warmup // 10)):
         e2e_step(i)
     torch.cuda.synchronize()
@@ -755,13 +773,17 @@ def run_main(args, rank, world, local_rank):
         dist.barrier()
     e2e_steps = max(n, min(args.steps, 200))
     b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    b0.record()
+    b0.record(comp)
+    cs.wait_event(b0)
+    for c in range(n):
+        load_x(c)
     for i in range(e2e_steps):
         e2e_step(i)
-    b1.record()
+    comp.wait_stream(cs)
+    b1.record(comp)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks([b0.elapsed_time(b1)], world)[0]
-    if not all(bool(torch.isfinite(yh.float()).all()) for yh in y_host):
+    if not all(bool(torch.isfinite(yh.float()).all()) for yc in y_host for yh in yc):
         raise RuntimeError("e2e: non-finite output copied to the host")
     e2e_value = headline_bytes() * e2e_steps / (e2e_ms * 1e-3) / 1e9
 
@@ -820,9 +842,10 @@ def run_main(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 2,
                     "d2h_bytes_per_step": sum(op.N * 2 for op in ops), "steps": e2e_steps,
                     "how": "public API (paia_gemv.loader GemvLib methods; on > 1 GPU tp.ShardedGemv.deferred and "
-                           "TpExchange.run), eager launches; per step a pinned H2D of x, the four ops, a pinned D2H of "
-                           "every op's full y, all in order on one stream; CUDA events around all steps, max over "
-                           "ranks"},
+                           "TpExchange.run), eager launches; per step a pinned H2D of x and a pinned D2H of every op's "
+                           "full y on a copy stream (step i's outputs leave while step i + 1 computes into the other "
+                           "rotation copy's buffers), the ops on the compute stream; CUDA events around all steps "
+                           "and all their copies, max over ranks"},
             "gpu_launches": launches,
             "clocks": clocks,
             "check_rel_l2_vs_torch": round(bad[1], 7),
