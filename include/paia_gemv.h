@@ -3,7 +3,7 @@
  *
  * y[N] = dequant(W)[N,K] . x[K] (+ bias), bf16 activations and outputs, fp32 accumulation. Pointers are device
  * pointers; `stream` is a cudaStream_t (NULL = legacy default stream). Every entry point launches asynchronously on
- * `stream`, allocates nothing, never synchronises and is safe to capture in a CUDA graph.
+ * `stream`, allocates nothing and never synchronises (exceptions are noted at their declarations).
  * Return codes: 0 ok, -1 bad variant, -2 bad shape or alignment, >0 the cudaError_t of the launch.
  *
  * The entry points marked REF replace the reference's (Bejaine/PAIA-Project) symbols of the same name with identical
@@ -66,8 +66,8 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
  * and codes as paia_gemv_int4_unfused (a >0 cudaError_t also when the array's address cannot be looked up). The
  * array keeps the last call's contents; each call overwrites the N * K elements it reads, so nothing needs clearing.
  * Calls that overlap on the GPU (two streams, or two host threads) share the array and race. The first call on each
- * device looks the array's address up with a runtime call and caches it: make that first call before any stream
- * capture, and not across a cudaDeviceReset (the cached address does not survive it). */
+ * device looks the array's address up with a runtime call and caches it; the cached address does not survive a
+ * cudaDeviceReset. */
 int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
                                   void* stream);
 
