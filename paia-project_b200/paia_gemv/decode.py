@@ -1,16 +1,16 @@
 """A minimal batch-1 decode step built around the GEMV family: the layer structure of Llama-3.1-8B / Qwen2.5-7B with
 synthetic weights, every projection through this library's GEMVs, everything else on the device with torch.
 
-One token = embedding -> L x [RMSNorm -> qkv (+ bias) -> RoPE -> KV-cache write -> grouped-query attention over the
-cache -> o -> residual -> RMSNorm -> gate_up -> SiLU(gate) * up -> down -> residual] -> RMSNorm -> lm_head ->
-argmax. The cache holds `ctx` positions (the first ctx - 1 synthetic), and the token is decoded at position ctx - 1,
-so every tensor shape is fixed and a whole token captures as one CUDA graph; tokens/s = 1 / its device time. The
-reference measures decode cost per token as a sum of per-op GEMV times (paia-bench/bench/analyze_e4.py:177-196);
-this measures the token itself, GEMVs and the ops between them.
+One token = embedding -> L x [RMSNorm -> qkv (+ bias) with RoPE fused in its epilogue -> KV-cache write ->
+grouped-query attention over the cache -> o -> residual -> RMSNorm -> gate_up -> SiLU(gate) * up -> down -> residual]
+-> RMSNorm -> lm_head -> argmax. The cache holds `ctx` positions (the first ctx - 1 synthetic), and the token is decoded
+at position ctx - 1, so every tensor shape is fixed and a whole token captures as one CUDA graph; tokens/s = 1 / its
+device time. The reference measures decode cost per token as a sum of per-op GEMV times
+(paia-bench/bench/analyze_e4.py:177-196); this measures the token itself, GEMVs and the ops between them (torch:
+RMSNorm, scaled-dot-product attention, SiLU x up, residual adds).
 """
-import math
-
 import torch
+import torch.nn.functional as F
 
 from . import quant
 
@@ -24,10 +24,12 @@ MODELS = {
 
 class Projection:
     """One weight matrix [N, K] in a format, on the device, with its GEMV through the library (or, for references,
-    a torch fp32 dequantise-then-matmul of the same bytes)."""
+    a torch fp32 dequantise-then-matmul of the same bytes). rope = (rope_rows, head_dim, pos, theta): a fused QKV
+    projection whose first rope_rows rows are q / k heads, stored pair-interleaved (quant.rope_pair_rows) and rotated
+    in the GEMV's epilogue (paia_gemv_rope); its output is in the natural row order."""
 
-    def __init__(self, lib, kind, N, K, g, bias=False):
-        self.lib, self.kind, self.N, self.K = lib, kind, N, K
+    def __init__(self, lib, kind, N, K, g, bias=False, rope=None):
+        self.lib, self.kind, self.N, self.K, self.rope = lib, kind, N, K, rope
         W = torch.randn(N, K, device="cuda", generator=g).mul_(0.02)
         self.s = self.z = None
         if kind == "bf16":
@@ -40,16 +42,31 @@ class Projection:
             self.W, self.s, self.z = quant.quantize_int4_asym(W)
         del W
         self.bias = (torch.randn(N, device="cuda", generator=g) * 0.02).to(torch.bfloat16) if bias else None
+        self.natural = None
+        if rope is not None:
+            # row-wise formats: reordering the quantised rows (and their scales / zeros / bias) is reordering W
+            rows, hd = rope[0], rope[1]
+            perm = lambda t: None if t is None else quant.rope_pair_rows(t, rows, hd)   # noqa: E731
+            self.W, self.s, self.z, self.bias = perm(self.W), perm(self.s), perm(self.z), perm(self.bias)
+            j = torch.arange(N, device="cuda")
+            src = j.clone()
+            jh = j[:rows] % hd
+            src[:rows] = j[:rows] - jh + (jh >> 1) + (jh & 1) * (hd // 2)
+            self.natural = torch.empty_like(src)
+            self.natural[src] = j                                    # natural row d sits at stored row natural[d]
         table = {"bf16": lib.variants, "fp8": lib.variants_fp8, "int4": lib.variants_int4,
                  "int4_asym": lib.variants_int4_asym}[kind]
         want = {"bf16": (2, 4, 4, 0, 1), "fp8": (2, 2, 4, 0, 1)}.get(kind, (4, 2, 4, 0, 1))
         self.variant = next(v["id"] for v in table if tuple(v[k] for k in "RUWSH") == want)
 
     def __call__(self, x, y):
-        """y = W x (+ bias) through the library's default path (bf16 in and out)."""
+        """y = W x (+ bias) through the library's default path (bf16 in and out), rotated when rope is set."""
         L, p = self.lib, (lambda t: None if t is None else t.data_ptr())
         W, xp, yp, v = self.W.data_ptr(), x.data_ptr(), y.data_ptr(), self.variant
-        if self.kind == "bf16":
+        if self.rope is not None:
+            rows, hd, pos, theta = self.rope
+            L.rope(self.kind, W, p(self.s), p(self.z), xp, p(self.bias), yp, self.N, self.K, rows, hd, pos, theta)
+        elif self.kind == "bf16":
             L.bf16_bias(W, xp, p(self.bias), yp, self.N, self.K, v) if self.bias is not None else \
                 L.bf16(W, xp, yp, self.N, self.K, v)
         elif self.kind == "fp8":
@@ -73,10 +90,22 @@ class Projection:
         return quant.dequant_int4_asym(self.W, self.s, self.z)
 
     def reference(self, x, y):
-        """The same projection as torch fp32 dequantise-then-matmul, rounded to bf16 (for checks)."""
+        """The same projection as torch fp32 dequantise-then-matmul (rotated in fp32 when rope is set), rounded to
+        bf16 once (for checks)."""
         r = self.dequantised() @ x.float()
         if self.bias is not None:
             r = r + self.bias.float()
+        if self.rope is not None:
+            rows, hd, pos, theta = self.rope
+            r = r[self.natural]
+            half = hd // 2
+            inv = theta ** (-torch.arange(0, hd, 2, device=r.device, dtype=torch.float64) / hd)
+            ang = pos * inv
+            cos = torch.cat([ang.cos(), ang.cos()]).float()
+            sin = torch.cat([ang.sin(), ang.sin()]).float()
+            t = r[:rows].view(-1, hd)
+            rot = torch.cat([-t[:, half:], t[:, :half]], dim=1)
+            r = torch.cat([(t * cos + rot * sin).reshape(-1), r[rows:]])
         y.copy_(r.to(torch.bfloat16))
         return y
 
@@ -98,25 +127,22 @@ class DecodeModel:
         g = torch.Generator(device="cuda").manual_seed(seed)
         self.embed = (torch.randn(V, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
         self.layers = []
+        # RoPE (rotate-half form) of q and k at the decoded position ctx - 1, in the qkv projection's epilogue
+        rope = ((nh + nkv) * hd, hd, float(ctx - 1), float(cfg["rope_theta"]))
+        norm = lambda: (1.0 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16).float()   # noqa: E731
         for _ in range(cfg["layers"]):
             self.layers.append({
-                "norm1": (1.0 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16),
-                "norm2": (1.0 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16),
-                "qkv": Projection(lib, kind, (nh + 2 * nkv) * hd, H, g, bias=cfg["qkv_bias"]),
+                "norm1": norm(),
+                "norm2": norm(),
+                "qkv": Projection(lib, kind, (nh + 2 * nkv) * hd, H, g, bias=cfg["qkv_bias"], rope=rope),
                 "o": Projection(lib, kind, H, nh * hd, g),
                 "gate_up": Projection(lib, kind, 2 * I, H, g),
                 "down": Projection(lib, kind, H, I, g),
                 "k": (torch.randn(nkv, ctx, hd, device="cuda", generator=g)).to(torch.bfloat16),
                 "v": (torch.randn(nkv, ctx, hd, device="cuda", generator=g)).to(torch.bfloat16),
             })
-        self.norm_f = (1.0 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
+        self.norm_f = norm()
         self.lm_head = Projection(lib, kind, V, H, g)
-        # RoPE (rotate-half form) at the decoded position ctx - 1
-        pos = ctx - 1
-        inv = cfg["rope_theta"] ** (-torch.arange(0, hd, 2, device="cuda", dtype=torch.float64) / hd)
-        ang = pos * inv
-        self.cos = torch.cat([ang.cos(), ang.cos()]).float()
-        self.sin = torch.cat([ang.sin(), ang.sin()]).float()
         # activations, reused every token (fixed addresses, so the token captures as a CUDA graph)
         dev = dict(device="cuda", dtype=torch.bfloat16)
         self.token = torch.zeros(1, device="cuda", dtype=torch.long)
@@ -138,20 +164,14 @@ class DecodeModel:
 
     @staticmethod
     def _rmsnorm(x, w, out, eps=1e-5):
-        xf = x.float()
-        out.copy_((xf * torch.rsqrt(xf.pow(2).mean() + eps) * w.float()).to(torch.bfloat16))
+        """out = bf16(x * rsqrt(mean(x^2) + eps) * w), computed in fp32 (w is kept in fp32)."""
+        out.copy_(F.rms_norm(x.float(), (x.numel(),), w, eps))
         return out
-
-    def _rope(self, t, n):
-        hd = self.cfg["head_dim"]
-        x = t.view(n, hd).float()
-        half = hd // 2
-        rot = torch.cat([-x[:, half:], x[:, :half]], dim=1)
-        return (x * self.cos + rot * self.sin).to(torch.bfloat16)
 
     def step(self, reference=False):
         """Decode one token: reads self.token, writes self.logits and the argmax into self.token. reference=True
-        runs every projection as torch fp32 dequantise-then-matmul instead of the library's GEMVs."""
+        runs every projection as torch fp32 dequantise-then-matmul (RoPE in fp32) instead of the library's GEMVs;
+        everything else is the same code in both."""
         c = self.cfg
         nh, nkv, hd, I = c["heads"], c["kv_heads"], c["head_dim"], c["inter"]
         proj = (lambda P, x, y: P.reference(x, y)) if reference else (lambda P, x, y: P(x, y))
@@ -159,26 +179,22 @@ class DecodeModel:
         pos = self.ctx - 1
         for lay in self.layers:
             self._rmsnorm(self.h, lay["norm1"], self.a)
-            proj(lay["qkv"], self.a, self.qkv)
-            q = self._rope(self.qkv[:nh * hd], nh)
-            k = self._rope(self.qkv[nh * hd:(nh + nkv) * hd], nkv)
-            lay["k"][:, pos].copy_(k)
+            proj(lay["qkv"], self.a, self.qkv)                  # q and k come out rotated
+            lay["k"][:, pos].copy_(self.qkv[nh * hd:(nh + nkv) * hd].view(nkv, hd))
             lay["v"][:, pos].copy_(self.qkv[(nh + nkv) * hd:].view(nkv, hd))
-            qg = q.view(nkv, nh // nkv, hd).float()
-            s = torch.bmm(qg, lay["k"].float().transpose(1, 2)) * (1.0 / math.sqrt(hd))
-            p = torch.softmax(s, dim=-1)
-            self.attn.copy_(torch.bmm(p, lay["v"].float()).reshape(-1).to(torch.bfloat16))
+            att = F.scaled_dot_product_attention(self.qkv[:nh * hd].view(1, nh, 1, hd), lay["k"].unsqueeze(0),
+                                                 lay["v"].unsqueeze(0), enable_gqa=True)
+            self.attn.copy_(att.reshape(-1))
             proj(lay["o"], self.attn, self.o)
-            self.h.copy_((self.h.float() + self.o.float()).to(torch.bfloat16))
+            self.h.add_(self.o)                                  # bf16 add: fp32 sum rounded once
             self._rmsnorm(self.h, lay["norm2"], self.a)
             proj(lay["gate_up"], self.a, self.gu)
-            gf = self.gu[:I].float()
-            self.m.copy_((gf * torch.sigmoid(gf) * self.gu[I:].float()).to(torch.bfloat16))
+            torch.mul(F.silu(self.gu[:I]), self.gu[I:], out=self.m)
             proj(lay["down"], self.m, self.d)
-            self.h.copy_((self.h.float() + self.d.float()).to(torch.bfloat16))
+            self.h.add_(self.d)
         self._rmsnorm(self.h, self.norm_f, self.a)
         proj(self.lm_head, self.a, self.logits)
-        self.token.copy_(torch.argmax(self.logits.float()).view(1))
+        self.token.copy_(torch.argmax(self.logits).view(1))
         return self.logits
 
 
