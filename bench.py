@@ -787,6 +787,28 @@ def run_main(args, rank, world, local_rank):
         raise RuntimeError("e2e: non-finite output copied to the host")
     e2e_value = headline_bytes() * e2e_steps / (e2e_ms * 1e-3) / 1e9
 
+    # the same steps with every copy in stream order on the compute stream (no overlap), reported beside it
+    def serial_step(i):
+        c = i % n
+        x_dev[c].copy_(x_host, non_blocking=True)
+        ys = [op.api_call(c, x_dev[c]) for op in ops]
+        if exchange is not None:
+            exchange.run()
+        for y, yh in zip(ys, y_host[c]):
+            yh.copy_(y, non_blocking=True)
+
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(comp)
+    for i in range(e2e_steps):
+        serial_step(i)
+    s1.record(comp)
+    torch.cuda.synchronize()
+    serial_ms = max_over_ranks([s0.elapsed_time(s1)], world)[0]
+    e2e_serial = headline_bytes() * e2e_steps / (serial_ms * 1e-3) / 1e9
+
     # roofline of the dominant kernel: FP8 lm_head (this rank's shard), bytes per launch / per-launch device time
     peak, peak_src = measured_peaks()
     dom = ops[0]
@@ -841,6 +863,7 @@ def run_main(args, rank, world, local_rank):
                                    f"graph of rotated launches{', including the exchange' if world > 1 else ''})"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 2,
                     "d2h_bytes_per_step": sum(op.N * 2 for op in ops), "steps": e2e_steps,
+                    "value_copies_in_stream_order": round(e2e_serial, 2),
                     "how": "public API (paia_gemv.loader GemvLib methods; on > 1 GPU tp.ShardedGemv.deferred and "
                            "TpExchange.run), eager launches; per step a pinned H2D of x and a pinned D2H of every op's "
                            "full y on a copy stream (step i's outputs leave while step i + 1 computes into the other "
