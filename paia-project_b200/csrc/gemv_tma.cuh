@@ -451,11 +451,11 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
         // two words of one half against the matching even / odd x of those words. Per group:
         // sum_d 256^d (L_d + H_d / 16 - 8 S_d) = sum_d (16 L_d + H_d) 256^d / 16 - C, with C = 8 sum_d 256^d S_d of the
         // lane's digits staged per group (lanes c = 0 / 1 hold digits 0-1 / 2-3; c = 2, 3 hold unused columns).
-        // 16 L + H stays below 2^22, so every product with 256^d / 16 is an exact float.
+        // t_d = 16 L_d + H_d stays below 2^22, so a lane's two digits merge in int32 as t_a + 256 t_b (below 2^31)
+        // and convert once: (t_a + 256 t_b) 256^a / 16 - C.
         const int grp = (int)(threadIdx.x & 31) >> 2;
         const uint8_t* xp = reinterpret_cast<const uint8_t*>(xs) + (size_t)(grp & 3) * xps + (size_t)gs * 128 + 32 * c;
-        const float flo = c == 0 ? 0.0625f : (c == 1 ? 4096.f : 0.f);          // 256^d / 16
-        const float fhi = c == 0 ? 16.f : (c == 1 ? 1048576.f : 0.f);
+        const float flo = c == 0 ? 0.0625f : (c == 1 ? 4096.f : 0.f);          // 256^a / 16, a = 0 or 2
 #pragma unroll
         for (int u = 0; u < NU; ++u) {
             const uint4 xa = *reinterpret_cast<const uint4*>(xp + 128 * u);
@@ -473,8 +473,10 @@ __device__ __forceinline__ void tma_steps(TmaAcc<U>& A, float& acc0, float& acc1
             }
             const int gidx = 8 * (gs + u);
             const float cg = gsum[gidx + 5 + (c & 1)];
-            const float r0 = fmaf((float)(16 * dl[0] + dh[0]), flo, fmaf((float)(16 * dl[1] + dh[1]), fhi, -cg));
-            const float r1 = fmaf((float)(16 * dl[2] + dh[2]), flo, fmaf((float)(16 * dl[3] + dh[3]), fhi, -cg));
+            const int t0 = 16 * dl[0] + dh[0] + 256 * (16 * dl[1] + dh[1]);   // row g
+            const int t1 = 16 * dl[2] + dh[2] + 256 * (16 * dl[3] + dh[3]);   // row g + 8
+            const float r0 = fmaf((float)t0, flo, -cg);
+            const float r1 = fmaf((float)t1, flo, -cg);
             if constexpr (F == kINT4) {
                 acc0 = fmaf(__half2float(__ushort_as_half(sc0[sl + u])), r0, acc0);
                 acc1 = fmaf(__half2float(__ushort_as_half(sc1[sl + u])), r1, acc1);

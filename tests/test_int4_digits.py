@@ -87,9 +87,10 @@ def _fma(a, b, c):
 
 def test_split_nibble_fold_matches_the_exact_group_sum():
     """Mirror of the TMA kernel's integer INT4 step: per 128-group and row, chain L = low nibbles (even k) against
-    the even-k digits, chain H = high nibbles kept as 16 n (odd k) against the odd-k digits; lane c = 0 folds digits
-    0, 1 and lane c = 1 digits 2, 3 as (16 L + H) 256^d / 16 - C with C = 8 sum 256^d S_d staged per group. Every
-    product is an exact float and the two lanes add up to sum_d 256^d (D_d - 8 S_d) to float rounding."""
+    the even-k digits, chain H = high nibbles kept as 16 n (odd k) against the odd-k digits; with t_d = 16 L_d + H_d,
+    lane c = 0 folds digits 0, 1 as (t_0 + 256 t_1) / 16 - C_0 and lane c = 1 digits 2, 3 as (t_2 + 256 t_3) 4096 - C_1
+    (the two digits merged in int32, one conversion each), C = 8 sum 256^d S_d staged per group. The two lanes add up
+    to sum_d 256^d (D_d - 8 S_d) to float rounding."""
     rng = np.random.default_rng(3)
     for trial in range(300):
         if trial == 0:
@@ -114,19 +115,18 @@ def test_split_nibble_fold_matches_the_exact_group_sum():
         H = [int((16 * q[odd] * dg[d][odd]).sum()) for d in range(4)]
         S = [int(dg[d].sum()) for d in range(4)]
         exact = sum(256 ** d * (int((q * dg[d]).sum()) - 8 * S[d]) for d in range(4))
+        t = [16 * L[d] + H[d] for d in range(4)]
         for d in range(4):
-            assert abs(16 * L[d] + H[d]) < 2 ** 22                     # exact as a float
+            assert abs(t[d]) < 2 ** 22
+        m0, m1 = t[0] + 256 * t[1], t[2] + 256 * t[3]
+        assert abs(m0) < 2 ** 31 and abs(m1) < 2 ** 31                  # the int32 merges do not overflow
         lo, hi = _f32(S[0] + 256 * S[1]), _f32(S[2] + 256 * S[3])
         c0, c1 = _f32(8.0 * lo), _f32(524288.0 * hi)                   # staged offsets, exact
         assert float(c0) == 8 * (S[0] + 256 * S[1]) and float(c1) == 524288 * (S[2] + 256 * S[3])
-        lane0 = _fma(_f32(16 * L[0] + H[0]), 0.0625, _fma(_f32(16 * L[1] + H[1]), 16.0, -c0))
-        lane1 = _fma(_f32(16 * L[2] + H[2]), 4096.0, _fma(_f32(16 * L[3] + H[3]), 1048576.0, -c1))
+        lane0 = _fma(_f32(m0), 0.0625, -c0)
+        lane1 = _fma(_f32(m1), 4096.0, -c1)
         got = float(np.float32(lane0 + lane1))
-        # each fmaf rounds once relative to its own exact result, the add relative to the sum: the error is float
-        # rounding of the lanes' exact partial values, not of the (larger) products that cancel inside an fmaf
-        in0 = (16 * L[1] + H[1]) * 16 - 8 * (S[0] + 256 * S[1])
-        in1 = (16 * L[3] + H[3]) * 1048576 - 524288 * (S[2] + 256 * S[3])
-        l0 = (16 * L[0] + H[0]) / 16 + in0
-        l1 = (16 * L[2] + H[2]) * 4096 + in1
-        bound = 2.0 ** -23 * (abs(in0) + abs(in1) + abs(l0) + abs(l1) + abs(exact))
+        # the conversions round relative to the merged integers, each fmaf and the add relative to their results
+        l0, l1 = m0 / 16 - 8 * (S[0] + 256 * S[1]), m1 * 4096 - 524288 * (S[2] + 256 * S[3])
+        bound = 2.0 ** -23 * (abs(m0) / 16 + abs(m1) * 4096 + abs(l0) + abs(l1) + abs(exact))
         assert abs(got - exact) <= bound, (trial, got, exact, bound)
