@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}] [--sweep]
 
-Workload (BASELINE config 5 at every N; its shapes are configs 2 and 3's): one step = the Llama-3.1-8B lm_head
+Workload (the same at every N: the row-sharded tensor-parallel configuration): one step = the Llama-3.1-8B lm_head
 128256x4096 and fused gate_up 28672x4096 in FP8 W8A16 (e4m3 + fp32 row scale) and in INT4 g128 (asymmetric: bf16
 scale + bf16 zero), batch 1 -- four GEMVs. On N GPUs (torchrun, one process per GPU) each rank holds N-th of every
 matrix's rows and one fused kernel per op stores its outputs into every rank's y over NVLink; on 1 GPU the four
@@ -38,7 +38,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "paia-project_b200"))
 
 METRIC = ("GEMV achieved HBM GB/s (weights + scales / device time), Llama-3.1-8B lm_head 128256x4096 + gate_up "
-          "28672x4096 in FP8 W8A16 and INT4 g128, batch 1, rows sharded over the GPUs (BASELINE config 5)")
+          "28672x4096 in FP8 W8A16 and INT4 g128, batch 1, rows sharded over the GPUs (row-sharded tensor parallel)")
 WORKLOAD = ("llama31_8b lm_head 128256x4096 + gate_up_fused 28672x4096, fp8 w8a16 and int4 g128 (asym), batch 1, "
             "row-sharded tensor parallel over n_gpus (1 GPU: whole matrices)")
 FALLBACK_HBM_GBS = 6650.0
@@ -342,8 +342,8 @@ def check_layer(layer):
 
 # ----------------------------------------------------------------------------------------------- headline workload
 
-# Llama-3.1-8B lm_head and fused gate_up in FP8 W8A16 and INT4 g128 (the asymmetric bf16
-# scale + zero format of config 3), batch 1; rows sharded over the ranks of the launch (one GPU: the whole matrices).
+# The headline step: Llama-3.1-8B lm_head and fused gate_up in FP8 W8A16 and INT4 g128 (the asymmetric bf16
+# scale + zero format), batch 1; rows sharded over the ranks of the launch (one GPU: the whole matrices).
 HEADLINE = (("fp8", "lm_head"), ("fp8", "gate_up_fused"), ("int4_asym", "lm_head"), ("int4_asym", "gate_up_fused"))
 HEADLINE_MODEL = "llama31_8b"
 
@@ -947,7 +947,7 @@ def run_extras(lib, g, l2, peak, args):
 
 
 def run_sweep(args):
-    """All BASELINE configs 1-4 per shape and format (graph mode, L2 rotation), one JSON line each, plus the decode
+    """Every Llama and Qwen decode shape in every format (graph mode, L2 rotation), one JSON line each, plus the decode
     us/token of both models in every format (layers back to back with PDL, distinct weights per layer)."""
     import torch
     from paia_gemv import load_lib, synthetic, timing
@@ -1252,7 +1252,7 @@ def run_families(args):
 
 
 def run_tp(args, rank, world, local_rank):
-    """row-sharded TP GEMV over the ranks of this launch (torchrun, one process per GPU). For
+    """Row-sharded TP GEMV over the ranks of this launch (torchrun, one process per GPU). For
     Llama-3.1-8B lm_head 128256x4096 and gate_up 28672x4096 in FP8 W8A16 and INT4 (asymmetric) g128: per-call device
     time of the fused path (peer-store epilogue + bounded arrival wait) and of the NCCL all-gather baseline, CUDA
     events around a CUDA graph (fused) or an eager loop (NCCL) over L2-rotated weight shards, max over ranks. One
@@ -1476,7 +1476,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the 1-GPU extra keys (decode layer, shapes, tokens)")
     ap.add_argument("--one", default=None, help="profiling aid: KIND:NxK, e.g. fp8:28672x4096 (default variant)")
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
-    ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks (config 5)")
+    ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks")
     ap.add_argument("--launches", type=int, default=4)
     ap.add_argument("--tune", action="store_true", help="per-shape variant sweep -> paia-project_b200/tuned/b200.json")
     ap.add_argument("--decode-loop", action="store_true",

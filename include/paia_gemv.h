@@ -71,7 +71,7 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
 int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
                                   void* stream);
 
-/* ---- Row-sharded tensor parallelism (no reference kernel; BASELINE config 5, survey row 8e) ----
+/* ---- Row-sharded tensor parallelism (no reference kernel; the outputs of a row-partitioned GEMV gathered) ----
  * Rank `rank` of `world` (<= 8) holds rows [rank N_local, (rank+1) N_local) of W (and their scales/zeros/bias) and
  * computes them with the TMA-fed kernel, storing every output to every rank's full-size y (world * N_local bf16;
  * y_all[r] = rank r's buffer as mapped in this process, e.g. through CUDA IPC) at rank * N_local + row.
@@ -111,7 +111,7 @@ int paia_gemv_ipc_handle(const void* ptr, void* handle64);
 int paia_gemv_ipc_open(const void* handle64, void** ptr);
 int paia_gemv_ipc_close(void* ptr);
 
-/* ---- B200 additions (no reference kernel; the reference's survey of this path proposes them) ---- */
+/* ---- B200 additions (no reference kernel) ---- */
 
 /* Library identification string. */
 const char* paia_gemv_version(void);
@@ -153,7 +153,7 @@ int paia_gemv_launch_ex(int kind, int R, int U, int W, int math, int pdl, int ks
                         const void* s, const void* z, const void* x, const void* bias, void* y, int N, int K,
                         void* stream);
 
-/* No reference kernel (survey row f3, the QKV neighbour of the decode GEMV): y = RoPE(W x + bias) for a fused QKV
+/* No reference kernel (the QKV neighbour of the decode GEMV): y = RoPE(W x + bias) for a fused QKV
  * projection, the rotary embedding applied in the epilogue. Rows [0, rope_rows) are the q and k heads (head_dim rows
  * each) in pair-interleaved order - row 2i + h of a head holds dimension i + h head_dim / 2 (rope_pair_rows in
  * paia_gemv.quant permutes W, its scales / zeros and the bias once) - and rows past rope_rows (v) are as usual. The

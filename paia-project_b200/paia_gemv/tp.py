@@ -1,4 +1,4 @@
-"""Row-sharded tensor-parallel batch-1 GEMV (Llama-3.1-8B lm_head and gate_up over 2/4/8 GPUs).
+"""Row-sharded tensor-parallel batch-1 GEMV (e.g. Llama-3.1-8B lm_head and gate_up over 2/4/8 GPUs).
 
 W [N, K] is split into `world` contiguous row blocks of N / world rows; rank r holds rows [r N/world, (r+1) N/world)
 with their scales / zeros / bias, and x is replicated. Two ways to assemble y [N] on every rank:
