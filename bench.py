@@ -933,16 +933,23 @@ def run_extras(lib, g, l2, peak, args):
                 del copies, xs, ys, calls, first
                 torch.cuda.empty_cache()
     out["per_shape_us"] = shapes
-    tokens = {}
+    tokens, plans = {}, {}
     for kind in ("bf16", "fp8", "int4", "int4_asym"):
         for model in ("llama31_8b", "qwen25_7b"):
             d = decode_token(lib, kind, model, g, tuned, peak, "per_op", reps=5)
             tokens[f"{kind}:{model}"] = {"us_per_token": d["decode_us_per_token"], "GBps": d["GBps"],
                                          "frac": d["frac_of_peak"]}
+            if kind.startswith("int4"):                  # the whole token as one plan launch: INT4's faster form
+                d = decode_token(lib, kind, model, g, tuned, peak, "plan", reps=5)
+                plans[f"{kind}:{model}"] = {"us_per_token": d["decode_us_per_token"], "GBps": d["GBps"],
+                                            "frac": d["frac_of_peak"]}
     out["decode_us_per_token"] = tokens
     out["decode_how"] = ("per token: every layer's qkv, o, gate_up, down chained (distinct weights per layer, Qwen qkv "
                          "with bias), then the lm_head; one CUDA graph with PDL (the reference's per-token sum of "
                          "per-op launches, paia-bench analyze_e4.py:177-196, measured as one sequence)")
+    out["decode_us_per_token_plan"] = plans
+    out["decode_plan_how"] = ("the same token as one paia_gemv_plan launch (every GEMV of the token in one persistent "
+                              "kernel, the next op's weights streaming while the previous op finishes), INT4 formats")
     return out
 
 
