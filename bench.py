@@ -1457,7 +1457,7 @@ def run_one(args):
     kind, shape = args.one.split(":")
     N, K = (int(v) for v in shape.split("x"))
     g = torch.Generator(device="cuda").manual_seed(7)
-    vid, _ = variant_for(lib, kind, N, K, None)
+    vid, _ = variant_for(lib, kind, N, K, load_tuned() if args.one_tuned else None)
     gms = [Gemv(lib, kind, N, K, g, "one", variant=vid, random_codes=True) for _ in range(2)]
     x = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16)
     y = torch.empty(N, device="cuda", dtype=torch.bfloat16)
@@ -1482,6 +1482,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the 1-GPU extra keys (decode layer, shapes, tokens)")
     ap.add_argument("--one", default=None, help="profiling aid: KIND:NxK, e.g. fp8:28672x4096 (default variant)")
+    ap.add_argument("--one-tuned", action="store_true", help="--one with the tuned table's variant (as the bench)")
     ap.add_argument("--families", action="store_true", help="per-shape comparison of the kernel families")
     ap.add_argument("--tp", action="store_true", help="row-sharded TP GEMV over the launched ranks")
     ap.add_argument("--launches", type=int, default=4)
