@@ -1372,6 +1372,58 @@ def run_decode_loop(args):
     return 0
 
 
+# The layer GEMVs of a decode step run back to back, and a chain whose launches switch kernel instances starts each
+# launch on code that is not in the instruction cache: measured on B200, the Llama INT4 asym per-op token took 1685 us
+# with the per-shape best instances (U = 4 for qkv / gate_up, U = 2 for o / down) and 1386 us with one instance for
+# every op (Qwen 1521 -> 1404, INT4 1351 -> 1270 and 1313 -> 1294), while that instance is within 0.2-3.3 % of the
+# per-shape best in isolation. So for the integer INT4 formats the GEMVs of a model's decode chain all take the one
+# TMA-fed variant that is fastest summed over them. FP8 and BF16 need no rule: their per-shape picks already map to
+# one kernel instance.
+CHAIN_KINDS = ("int4", "int4_asym")
+
+
+def chain_rule(tuned, keys, models, chain=None):
+    """Apply the decode-chain rule in place: per integer INT4 format and model, the shapes of the decode chain (the
+    layer sequence qkv, o, gate_up, down and the lm_head) all take the TMA variant (R = 0) with the lowest summed
+    estimated time over them (a shape whose top 5 lacks it counted at its fifth entry's time, a lower bound), ties
+    broken by how many top-5 lists hold it. The per-shape pick stays as "isolated_best". Returns
+    {(kind, model): variant}."""
+    from paia_gemv import synthetic
+    chain = chain or synthetic.LAYER_SEQUENCE + ("lm_head",)
+    tup = lambda v: tuple(v[k] for k in "RUWSH")                # noqa: E731
+    chosen = {}
+    for kind in CHAIN_KINDS:
+        table = tuned.get(keys[kind], {})
+        for model, shapes in models.items():
+            entries = [table.get("{}x{}".format(*shapes[name])) for name in chain if name in shapes]
+            entries = [e for e in entries if e and e.get("top5")]
+            if not entries:
+                continue
+            cands = {tup(t["variant"]) for e in entries for t in e["top5"] if t["variant"]["R"] == 0}
+            scored = []
+            for c in sorted(cands):
+                hits, total = 0, 0.0
+                for e in entries:
+                    best_us = e.get("isolated_best", {}).get("us", e["us"])
+                    top = e["top5"]
+                    pct = next((t["pct_of_best"] for t in top if tup(t["variant"]) == c), None)
+                    hits += pct is not None
+                    total += best_us * 100.0 / (pct if pct else top[-1]["pct_of_best"])
+                scored.append((total, -hits, c))
+            if not scored:
+                continue
+            _, _, c = min(scored)
+            var = dict(zip("RUWSH", c))
+            for e in entries:
+                if "isolated_best" not in e:
+                    e["isolated_best"] = {"variant": e["variant"], "us": e["us"]}
+                e["variant"] = dict(var)
+                e["chain"] = ("one kernel instance for every GEMV of the model's decode chain (decode-chain rule); us, "
+                              "gbps and top5 are the isolated per-shape measurements")
+            chosen[(kind, model)] = var
+    return chosen
+
+
 def run_tune(args):
     """Per-shape variant choice for B200 written to paia-project_b200/tuned/b200.json in the reference's tuned-table
     schema (src/tools/dev_sweep_bf16.py:90-99: per N x K the best (R, U, W, S, H) with its us and GB/s and the top 5 with
@@ -1443,6 +1495,8 @@ def run_tune(args):
                               "default_us": round(next(u for u, v in rows if v["id"] == dflt), 3)}), flush=True)
             del copies, xs, ys, first
             torch.cuda.empty_cache()
+    for (kind, model), var in chain_rule(tuned, keys, synthetic.SHAPES).items():
+        print(json.dumps({"chain_rule": kind, "model": model, "variant": var}))
     out_f.parent.mkdir(parents=True, exist_ok=True)
     out_f.write_text(json.dumps(tuned, indent=1) + "\n")
     print(json.dumps({"wrote": str(out_f.relative_to(ROOT))}))
