@@ -132,3 +132,54 @@ def test_reference_loader_loads_this_library(lib_path, monkeypatch):
     assert any(all(v[k] == want[k] for k in "RUWSH") for v in lib.variants)
     with pytest.raises(RuntimeError):
         lib.bf16(0x10000, 0x10000, 0x10000, 4, 12, 0, stream=0)    # K % 8 -> -2 -> RuntimeError, as the reference
+
+
+def test_argument_contract_of_the_b200_entry_points(lib_path):
+    """The entry points without a reference counterpart reject bad arguments with -2 on the host, before any device
+    call: rotary QKV (odd rows or head size, rope rows not whole heads or past N, theta <= 0, pos < 0), tensor
+    parallelism (kind, world, rank, missing or misaligned buffers), the exchange, the no-alloc unfused control beyond
+    its 16 Mi-element scratch, batched x (M < 1) and layer launches (op count, counters)."""
+    L = ctypes.CDLL(lib_path)
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    a16 = P(0x10000)
+    f = L.paia_gemv_rope
+    f.argtypes = [I, P, P, P, P, P, P, I, I, I, I, F, F, P]
+    assert f(7, a16, None, None, a16, None, a16, 256, 16, 128, 64, 5.0, 1e4, None) == -2   # kind
+    assert f(0, a16, None, None, a16, None, a16, 255, 16, 128, 64, 5.0, 1e4, None) == -2   # odd N
+    assert f(0, a16, None, None, a16, None, a16, 256, 16, 128, 63, 5.0, 1e4, None) == -2   # odd head size
+    assert f(0, a16, None, None, a16, None, a16, 256, 16, 96, 64, 5.0, 1e4, None) == -2    # rope rows not whole heads
+    assert f(0, a16, None, None, a16, None, a16, 256, 16, 320, 64, 5.0, 1e4, None) == -2   # rope rows past N
+    assert f(0, a16, None, None, a16, None, a16, 256, 16, 128, 64, 5.0, 0.0, None) == -2   # theta
+    assert f(0, a16, None, None, a16, None, a16, 256, 16, 128, 64, -1.0, 1e4, None) == -2  # position
+    ptrs = lambda *v: (P * len(v))(*v)                                                      # noqa: E731
+    for name in ("paia_gemv_tp", "paia_gemv_tp_deferred"):
+        f = getattr(L, name)
+        f.argtypes = [I, P, P, P, P, P, ctypes.POINTER(P), ctypes.POINTER(P), I, I, I, I, P]
+        y2, fl2 = ptrs(a16, a16), ptrs(a16, a16)
+        assert f(5, a16, None, None, a16, None, y2, fl2, 2, 0, 64, 16, None) == -2           # kind
+        assert f(0, a16, None, None, a16, None, y2, fl2, 0, 0, 64, 16, None) == -2           # world
+        assert f(0, a16, None, None, a16, None, y2, fl2, 9, 0, 64, 16, None) == -2
+        assert f(0, a16, None, None, a16, None, y2, fl2, 2, 2, 64, 16, None) == -2           # rank
+        assert f(0, a16, None, None, a16, None, None, fl2, 2, 0, 64, 16, None) == -2         # no y pointers
+        assert f(0, a16, None, None, a16, None, y2, ptrs(a16, P(0x10004)), 2, 0, 64, 16, None) == -2  # counters
+        assert f(0, a16, None, None, a16, None, y2, fl2, 2, 0, 64, 12, None) == -2           # K % 8
+    f = L.paia_gemv_tp_exchange
+    f.argtypes = [ctypes.POINTER(P), I, I, P]
+    assert f(ptrs(a16, a16), 0, 0, None) == -2
+    assert f(ptrs(a16, a16), 2, 2, None) == -2
+    assert f(None, 2, 0, None) == -2
+    assert f(ptrs(a16, P(0x10008)), 2, 0, None) == -2
+    f = L.paia_gemv_int4_unfused_static
+    f.argtypes = [P, P, P, P, I, I, P]
+    assert f(a16, a16, a16, a16, 8192, 4096, None) == -2                                     # past 16 Mi elements
+    assert f(a16, a16, a16, a16, 0, 4096, None) == -2
+    f = L.paia_gemv_batched
+    f.argtypes = [I, P, P, P, P, P, P, I, I, I, P]
+    assert f(0, a16, None, None, a16, None, a16, 0, 64, 16, None) == -2                      # M < 1
+    assert f(4, a16, None, None, a16, None, a16, 2, 64, 16, None) == -2                      # kind
+    f = L.paia_gemv_layer
+    f.argtypes = [I, I, I, P, P, P]
+    assert f(1, 0, 0, a16, a16, None) == -2                                                  # no ops
+    assert f(1, 0, 7, a16, a16, None) == -2                                                  # more than 6
+    assert f(1, 0, 2, None, a16, None) == -2                                                 # no op table
+    assert f(1, 0, 2, a16, P(0x10002), None) == -2                                           # counters alignment
