@@ -65,3 +65,17 @@ def test_chain_rule_prefers_the_lowest_summed_time():
     chosen = bench.chain_rule(t, KEYS, shapes)
     assert chosen[("int4", "m")] == a
     assert t["int4_shapes"]["103x128"]["isolated_best"]["variant"] == c
+
+
+def test_every_tuned_variant_exists_in_the_library():
+    """Every (R, U, W, S, H) the table names is in its format's variant table (the adapters and bench.py look tuples
+    up by value and raise on a missing one); the library loads and answers variant_info without a GPU."""
+    from paia_gemv import load_lib
+    lib = load_lib()
+    tables = {"bf16": lib.variants, "fp8": lib.variants_fp8, "int4": lib.variants_int4,
+              "int4_asym": lib.variants_int4_asym}
+    t = table()
+    for kind, key in KEYS.items():
+        have = {tuple(v[k] for k in "RUWSH") for v in tables[kind]}
+        for shape, e in t[key].items():
+            assert tuple(e["variant"][k] for k in "RUWSH") in have, (kind, shape, e["variant"])
