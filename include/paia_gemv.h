@@ -66,8 +66,8 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
  * and codes as paia_gemv_int4_unfused (a >0 cudaError_t also when the array's address cannot be looked up). The
  * array keeps the last call's contents; each call overwrites the N * K elements it reads, so nothing needs clearing.
  * Calls that overlap on the GPU (two streams, or two host threads) share the array and race. The first call on each
- * device looks the array's address up with a runtime call and caches it; the cached address does not survive a
- * cudaDeviceReset. */
+ * device does a set-up step: it looks the array's address up with a runtime call and caches it, so make that first
+ * call before any stream capture; the cached address does not survive a cudaDeviceReset. */
 int paia_gemv_int4_unfused_static(const void* Wq, const void* scales, const void* x, void* y, int N, int K,
                                   void* stream);
 

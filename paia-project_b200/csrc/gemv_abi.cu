@@ -455,7 +455,8 @@ int paia_gemv_int4_unfused(const void* Wq, const void* scales, const void* x, vo
 // The scratch is a file-scope device array (module-load storage, not an allocation in this call); its device
 // address is looked up once per device with cudaGetSymbolAddress, with that device current, and cached (the cache
 // does not survive cudaDeviceReset). Calls that overlap on the GPU (two streams, or two host threads) share the array
-// and race; it keeps the last call's contents, and every call overwrites the N x K elements it reads.
+// and race; it keeps the last call's contents, and every call overwrites the N x K elements it reads. The first call
+// on a device does the address lookup (a host-side runtime call), so it should come before any stream capture.
 namespace {
 constexpr size_t kStaticScratchElems = (size_t)16 << 20;       // 16 Mi bf16 = 32 MiB (e.g. N x K = 4096 x 4096)
 static __device__ __align__(256) __nv_bfloat16 g_static_scratch[kStaticScratchElems];

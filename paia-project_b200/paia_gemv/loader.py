@@ -183,7 +183,7 @@ class GemvLib:
         """int4_unfused with the library's own 32 MiB scratch, for callers that cannot allocate device memory on the
         call path (a memory pool that owns all of HBM, a host without a device allocator, a loop that must not
         synchronise the device). N * K must not exceed 16 Mi; calls that overlap on the GPU race on the shared
-        scratch."""
+        scratch; the first call on a device looks the scratch's address up, so make it before any stream capture."""
         if N * K > self.STATIC_SCRATCH_ELEMS:
             raise RuntimeError(f"paia_gemv_int4_unfused_static: N*K = {N * K} exceeds the static scratch of "
                                f"{self.STATIC_SCRATCH_ELEMS} elements; use int4_unfused with a caller scratch")
