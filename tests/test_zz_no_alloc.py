@@ -1,6 +1,12 @@
-"""paia_gemv_int4_unfused_static (library-owned static scratch, no allocation per call) against
-paia_gemv_int4_unfused with a caller scratch: same bytes out, on two calls in a row, plus the size limit.
-The file name sorts last so the test also runs after every other GPU test in one session."""
+"""paia_gemv_int4_unfused_static is the unfused INT4 control for callers that cannot hand the library a scratch
+buffer: a serving engine whose memory pool already owns the whole HBM budget, a plain C host with no device
+allocator of its own, or a latency-critical loop where cudaMalloc / cudaFree would synchronise the device. It
+dequantises into the library's own file-scope device array instead, so a call allocates nothing.
+
+Checked through the C ABI against paia_gemv_int4_unfused with a caller-owned scratch: the same output bytes on two
+calls in a row (the second call reuses the array the first one filled), and a clear -2 (a RuntimeError from the
+Python binding) for N x K beyond the array's 16 Mi elements. The file name sorts last, so a run that stops at the
+first failure has run every other test first; the test passes alone in a fresh process as well as after the rest."""
 import numpy as np
 import pytest
 import torch
