@@ -5,7 +5,8 @@ only for the byte-counted `full` barriers, whose phase waits there for its bytes
 The kernel's rules, modelled here: the producer's lane 0 arms a slot's `full` barrier (arrival + expected bytes) only
 after its wait on the slot's `empty` barrier succeeded, and arrives on nothing after its first failed wait; the other
 producer lanes issue the slot's copies (bytes that land later) and learn lane 0's failure one stage late (a shared
-flag read at the end of each stage, BF16 / FP8); a consumer warp waits on `full`, and releases the slot on `empty`
+flag read at the end of each stage, BF16 / FP8; INT4 lanes, whose metadata copies arrive on `full` too, take lane 0's
+status by a shuffle of the same stage before they arrive); a consumer warp waits on `full`, and releases the slot on `empty`
 only while every `full` wait of its own has seen the phase complete. Any wait may give up while its phase is
 incomplete. Checked: no arrival ever lands on a phase at zero pending arrivals, and no byte count leaves the
 barrier's range. The model also shows that the earlier, unguarded rules (consumers release after a failed wait) break
@@ -46,11 +47,13 @@ class Barrier:
         return self.phase > lap
 
 
-def run(seed, guarded=True, st=4, nc=4, stages=40, nbytes=65536, p_timeout=0.02, out=None):
+def run(seed, guarded=True, st=4, nc=4, stages=40, nbytes=65536, p_timeout=0.02, out=None, int4=False):
     """Returns the first broken-barrier finding (or None); out, if given, receives whether every stage was produced
     and consumed and every copy landed."""
     rng = random.Random(seed)
-    full = [Barrier(1) for _ in range(st)]
+    # INT4: lane 0's expect-bytes arrival, the lanes' metadata cp.async arrivals (one, after their copies land) and
+    # lane 0's closing arrival; BF16 / FP8: lane 0's expect-bytes arrival alone
+    full = [Barrier(3 if int4 else 1) for _ in range(st)]
     empty = [Barrier(nc) for _ in range(st)]
     inflight = []                                   # (slot, bytes) copies issued, not landed
     prod_g = 0                                      # next stage the producer handles
@@ -79,19 +82,31 @@ def run(seed, guarded=True, st=4, nc=4, stages=40, nbytes=65536, p_timeout=0.02,
                         live0, stop_flag = False, True
                 if live0:
                     full[s].arrive(tx=nbytes)                        # lane 0: arrival + expected bytes
-                if lanes_live:                                       # the lanes' copies, with last stage's flag
+                if lanes_live:                                       # the lanes' copies, with last stage's status
                     inflight.append((s, nbytes))
-                lanes_live = lanes_live and not stop_flag           # flag read at the end of the stage
+                if int4:
+                    lanes_live = live0                              # a shuffle of lane 0's status, this stage
+                    if lanes_live:
+                        inflight.append((s, "arrive"))               # the lanes' cp.async arrival, when it lands
+                        full[s].arrive()                             # lane 0's closing arrival
+                else:
+                    lanes_live = lanes_live and not stop_flag       # flag read at the end of the stage
             else:                                                    # carries on after a failed wait
                 if prod_g >= st and wait(empty[s], lap - 1) == "pending":
                     continue
                 full[s].arrive(tx=nbytes)
                 inflight.append((s, nbytes))
+                if int4:
+                    inflight.append((s, "arrive"))
+                    full[s].arrive()
             prod_g += 1
         elif actor == nc + 1 and inflight:                          # a copy lands
             k = rng.randrange(len(inflight))
             s, b = inflight.pop(k)
-            full[s].complete_tx(b)
+            if b == "arrive":
+                full[s].arrive()
+            else:
+                full[s].complete_tx(b)
         elif actor < nc and cons_g[actor] < stages:                 # consumer warp: one stage
             g = cons_g[actor]
             s, lap = g % st, g // st
@@ -121,17 +136,20 @@ def test_guarded_protocol_never_breaks_a_barrier():
     for seed in range(1000):
         for p in (0.0, 0.01, 0.05, 0.3):
             assert run(seed, guarded=True, p_timeout=p) is None, (seed, p)
+            assert run(seed, guarded=True, p_timeout=p, int4=True) is None, (seed, p, "int4")
 
 
 def test_unguarded_protocol_is_caught():
-    broken = sum(run(seed, guarded=False, p_timeout=0.05) is not None for seed in range(1000))
-    assert broken > 0
+    for int4 in (False, True):
+        broken = sum(run(seed, guarded=False, p_timeout=0.05, int4=int4) is not None for seed in range(1000))
+        assert broken > 0, int4
 
 
 def test_no_timeouts_run_to_completion():
     """Without timeouts every stage is produced and consumed and every copy lands, both forms alike."""
     for seed in range(200):
         for guarded in (True, False):
-            out = {}
-            assert run(seed, guarded=guarded, p_timeout=0.0, out=out) is None
-            assert out["complete"], (seed, guarded)
+            for int4 in (False, True):
+                out = {}
+                assert run(seed, guarded=guarded, p_timeout=0.0, out=out, int4=int4) is None
+                assert out["complete"], (seed, guarded, int4)
